@@ -1,0 +1,148 @@
+/* wasr.h -- additive C ABI of the B200 batch-transcription engine (libwasr_gpu.so).
+ *
+ * These entry points have no one-to-one counterpart in the reference ABI: they are the
+ * "new-build additions" layered on top of the reference's wp_* / wk_* calls (which are
+ * declared, unchanged, in wtlgpu.h).  They cover:
+ *   - the weight-blob plan (which byte offset holds which tensor), mirroring the
+ *     reference's Plan / PlanLayer / PlanQ structs (src/model.rs:58-94) and the blob
+ *     packer build_plan (src/model.rs:148-237);
+ *   - a whole-model batched, ragged forward: many windows stacked into one set of
+ *     GEMMs (the reference runs one window at a time: Model::run_gpu, src/model.rs:546-619);
+ *   - batch transcription with the reference's window schedule (Stream::push/commit/
+ *     finish, src/stream.rs:58-168) driven round by round across utterances;
+ *   - the HTK fbank of src/fbank.rs on the host (feature extraction for the schedule);
+ *   - per-output-channel weight scales and device selection.
+ *
+ * Model constants follow src/model.rs:21-32.
+ */
+#ifndef WASR_H
+#define WASR_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WASR_D 512          /* model width */
+#define WASR_HEADS 8
+#define WASR_HD 64          /* head dim */
+#define WASR_FF 2048
+#define WASR_DIM 40         /* fbank feature dim (39 log-mel + log-energy) */
+#define WASR_C1 32          /* conv channels */
+#define WASR_C2 64
+#define WASR_C3 192
+#define WASR_W2 41          /* conv2 output width (40 + one zero column) */
+#define WASR_FLAT 3840      /* 192 * 20 */
+#define WASR_MAX_LAYERS 40
+#define WASR_NONE ((uint64_t)-1)
+
+/* Stream schedule defaults (src/stream.rs:11-18). */
+#define WASR_PREV 200
+#define WASR_POST 100
+#define WASR_PAD 50
+#define WASR_WHOLE_MAX 2000
+
+/* One int8 weight matrix [n][k] (row-major = K-major) inside the blob.
+ * `s` is the per-tensor scale the reference keeps (src/xnet.rs:70, PlanQ src/model.rs:60-63).
+ * `scale_off` != WASR_NONE points at an fp32 [n] per-output-channel scale vector, which then
+ * replaces `s` in the epilogue:  out = (acc * xs[i]) * ws[j] + bias[j]. */
+typedef struct WasrMat {
+  uint64_t off;
+  uint64_t scale_off;
+  float s;
+  int32_t n;
+  int32_t k;
+  int32_t reserved;
+} WasrMat;
+
+/* One encoder layer (PlanLayer, src/model.rs:66-79).  qb/kb/vb/ob are optional projection
+ * biases (WASR_NONE in the reference model, which has none: src/model.rs:526-531). */
+typedef struct WasrLayer {
+  uint64_t pn_g, pn_b, mn_g, mn_b;
+  WasrMat q, k, v, o, f1, f2;
+  uint64_t qb, kb, vb, ob, f1b, f2b;
+} WasrLayer;
+
+/* Whole model (Plan, src/model.rs:81-94).  out.n = out_n = vocab rounded up to a multiple
+ * of 4, with zero weight rows and -1e30 bias in the padding (src/model.rs:229-231). */
+typedef struct WasrPlan {
+  int32_t n_layers;
+  int32_t vocab;
+  int32_t out_n;
+  int32_t reserved;
+  WasrMat lin, out;
+  uint64_t lin_b, out_b, c1, c2, c3;
+  WasrLayer layers[WASR_MAX_LAYERS];
+} WasrPlan;
+
+typedef struct WasrModel WasrModel;
+
+/* Upload the blob to `device` and size activation buffers for up to `max_rows` stacked
+ * output frames (t1 rows) per batched forward.  Returns NULL on failure. */
+WasrModel* wasr_model_create(const void* blob, size_t bytes, const WasrPlan* plan, int device,
+                             int max_rows);
+void wasr_model_destroy(WasrModel* m);
+/* Stream every later call of this model runs on (NULL = the model's own stream). */
+int wasr_model_set_stream(WasrModel* m, void* stream);
+void* wasr_model_stream(WasrModel* m);
+/* Enable (1) / disable (0) CUDA-graph capture and replay of whole batched forwards. */
+int wasr_model_set_graphs(WasrModel* m, int on);
+/* Most recent device-side error word (0 = none); a nonzero value means a bounded wait in a
+ * kernel gave up.  Cleared by reading. */
+int wasr_model_error(WasrModel* m);
+
+#define WASR_F_DEVICE 1   /* feats / ids / logits pointers are device pointers */
+#define WASR_F_NOSYNC 2   /* do not synchronise the stream before returning (device mode) */
+
+/* Per-kernel timing.  With profiling on, every kernel the engine enqueues is bracketed by a
+ * pair of CUDA events on the model's stream (captured into the CUDA graphs as event nodes), so
+ * the timing is taken inside the real, graph-replayed run.  wasr_model_profile() sums, per
+ * kernel class, the durations of the most recent execution of every cached graph (plus the
+ * last eager chunk).  Turning profiling on or off drops the cached graphs. */
+enum {
+  WASR_K_CONV1 = 0, WASR_K_CONV2, WASR_K_CONV3, WASR_K_QUANT, WASR_K_GEMM_LIN, WASR_K_LN,
+  WASR_K_GEMM_QKV, WASR_K_ATTN, WASR_K_GEMM_O, WASR_K_GEMM_F1, WASR_K_GEMM_F2, WASR_K_GEMM_OUT,
+  WASR_K_IDS, WASR_K_COUNT
+};
+int wasr_model_set_profile(WasrModel* m, int on);
+int wasr_model_profile(WasrModel* m, double* ms, int64_t* launches, int ncat);
+/* Kernels launched by this model so far (a graph replay counts every kernel it holds). */
+int64_t wasr_model_kernel_launches(WasrModel* m);
+
+/* Batched ragged forward (Model::forward on n_win windows at once, src/model.rs:368-386):
+ *   feats  : [sum t][40] fp32, windows concatenated
+ *   t      : [n_win] frames per window (host array); t < 5 gives zero output frames
+ *   ids    : [sum t1] uint32 argmax token ids, t1 = (t-5)/5+1
+ *   logits : optional [sum t1][out_n] fp32 (debug/parity); NULL = fused GEMM+argmax only
+ * Returns 0 or a negative error code. */
+int wasr_forward(WasrModel* m, const float* feats, const int32_t* t, int n_win, uint32_t* ids,
+                 float* logits, int flags);
+
+/* Batch transcription with the reference stream schedule (src/stream.rs:58-168): every
+ * utterance runs its own commit/finish sequence; the k-th windows of all utterances are
+ * stacked into one wasr_forward.
+ *   feats    : [sum n_frames][40] host fp32 (CMS-normalised fbank frames)
+ *   sil      : [n_utt][40] host fp32 silence frame of each utterance (Fbank::silence)
+ *   ids      : output per-frame token ids (before CTC collapse), utterances concatenated
+ *   ids_off  : [n_utt+1] offsets into ids
+ * Returns 0, or a negative code (-20: ids_cap too small). */
+int wasr_transcribe(WasrModel* m, const float* feats, const int64_t* n_frames, const float* sil,
+                    int n_utt, int prev, int blk, int post, uint32_t* ids, int64_t* ids_off,
+                    int64_t ids_cap);
+
+/* Host fbank (src/fbank.rs:79-161): int16 PCM -> CMS-normalised [frames][40] fp32 and the
+ * utterance's silence frame.  Returns the frame count (or, if feats is NULL, the count only). */
+int64_t wasr_fbank(const int16_t* pcm, int64_t n, float* feats, int64_t cap, float* sil);
+
+/* CTC collapse (Model::text without the vocabulary, src/model.rs:622-642): drop repeats
+ * and blank id 0.  Returns the collapsed length. */
+int64_t wasr_ctc_collapse(const uint32_t* ids, int64_t n, uint32_t* out);
+
+const char* wasr_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* WASR_H */

@@ -1,0 +1,138 @@
+"""GPU parity of the wk_* kernels (reference ABI, csrc/wtl_kern.cu / csrc/wk_attention_*.cu)
+against the oracle.  Bit-exact: quant, LayerNorm+quant, add+LayerNorm+quant, add, argmax and
+the conv frontend (same operation order as src/model.rs / src/kernels.rs).  Attention: fp32
+within rtol 1e-5 / atol 1e-6 (only expf's last place may differ from glibc).  GELU+quant:
+within one int8 step where tanhf differs in the last place."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("t,k", [(1, 512), (390, 512), (77, 2048), (129, 3840), (5, 10), (3, 1000)])
+def test_wk_quant(gpu_lib, dev, orc, t, k):
+    L = gpu_lib
+    rng = np.random.default_rng(t * k)
+    x = (rng.standard_normal((t, k)) * rng.uniform(0.01, 100)).astype(np.float32)
+    x[0, : min(k, 8)] = [0.5, -0.5, 1.5, 127, -127, 0.25, 3.0, -2.5][: min(k, 8)]
+    if t > 2:
+        x[2] = 0.0
+    px, pq, ps = dev.put(x), dev.empty(t * k), dev.empty(t * 4)
+    L.wk_quant(None, px, t, k, pq, ps)
+    assert L.wk_last_error() == 0
+    q, s = orc.quant(x)
+    np.testing.assert_array_equal(dev.get(ps, (t,), np.float32), s)
+    np.testing.assert_array_equal(dev.get(pq, (t, k), np.int8), q)
+    # wp_quant_rows: same rounding
+    assert L.wp_quant_rows(px, t, k, None, pq, ps) == 0
+    np.testing.assert_array_equal(dev.get(pq, (t, k), np.int8), q)
+
+
+@pytest.mark.parametrize("t", [1, 31, 33, 390, 777])
+def test_wk_norm_quant_and_add(gpu_lib, dev, orc, t):
+    L = gpu_lib
+    rng = np.random.default_rng(t)
+    h = (4 * rng.standard_normal((t, 512)) + 0.3).astype(np.float32)
+    o = rng.standard_normal((t, 512)).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(512)).astype(np.float32)
+    b = (0.05 * rng.standard_normal(512)).astype(np.float32)
+    ph, po, pg, pb = dev.put(h), dev.put(o), dev.put(g), dev.put(b)
+    pq, ps = dev.empty(t * 512), dev.empty(t * 4)
+    L.wk_norm_quant(None, ph, pg, pb, t, 512, pq, ps)
+    q, s = orc.quant(orc.norm(h, g, b))
+    np.testing.assert_array_equal(dev.get(ps, (t,), np.float32), s)
+    np.testing.assert_array_equal(dev.get(pq, (t, 512), np.int8), q)
+    L.wk_add_norm_quant(None, ph, po, pg, pb, t, 512, pq, ps)
+    h2 = (h + o).astype(np.float32)
+    np.testing.assert_array_equal(dev.get(ph, (t, 512), np.float32), h2)
+    q, s = orc.quant(orc.norm(h2, g, b))
+    np.testing.assert_array_equal(dev.get(ps, (t,), np.float32), s)
+    np.testing.assert_array_equal(dev.get(pq, (t, 512), np.int8), q)
+    L.wk_add(None, ph, po, t, 512)
+    np.testing.assert_array_equal(dev.get(ph, (t, 512), np.float32), (h2 + o).astype(np.float32))
+    assert L.wk_last_error() == 0
+
+
+def test_wk_norm_quant_other_width(gpu_lib, dev, orc):
+    L = gpu_lib
+    t, d = 9, 200
+    rng = np.random.default_rng(2)
+    h = rng.standard_normal((t, d)).astype(np.float32)
+    g, b = np.ones(d, np.float32), np.zeros(d, np.float32)
+    ph, pg, pb, pq, ps = dev.put(h), dev.put(g), dev.put(b), dev.empty(t * d), dev.empty(t * 4)
+    L.wk_norm_quant(None, ph, pg, pb, t, d, pq, ps)
+    q, s = orc.quant(orc.norm(h, g, b))
+    np.testing.assert_array_equal(dev.get(pq, (t, d), np.int8), q)
+    np.testing.assert_array_equal(dev.get(ps, (t,), np.float32), s)
+
+
+def test_wk_gelu_quant(gpu_lib, dev, orc):
+    L = gpu_lib
+    t, k = 300, 2048
+    rng = np.random.default_rng(4)
+    x = (2 * rng.standard_normal((t, k))).astype(np.float32)
+    px, pq, ps = dev.put(x), dev.empty(t * k), dev.empty(t * 4)
+    L.wk_gelu_quant(None, px, t, k, pq, ps)
+    gx = orc.gelu(x)
+    got = dev.get(px, (t, k), np.float32)
+    # tolerance: CUDA tanhf vs glibc tanhf may differ in the last place
+    np.testing.assert_allclose(got, gx, rtol=2e-6, atol=1e-7)
+    assert np.mean(got == gx) > 0.99
+    q, s = orc.quant(gx)
+    gq = dev.get(pq, (t, k), np.int8).astype(np.int32)
+    assert np.abs(gq - q).max() <= 1 and np.mean(gq == q) >= 0.9999
+    np.testing.assert_allclose(dev.get(ps, (t,), np.float32), s, rtol=1e-6)
+
+
+@pytest.mark.parametrize("t,n", [(390, 10504), (7, 10502), (1, 3), (64, 257)])
+def test_wk_argmax_first_max_wins(gpu_lib, dev, orc, t, n):
+    L = gpu_lib
+    rng = np.random.default_rng(n)
+    x = rng.standard_normal((t, n)).astype(np.float32)
+    x[0, :] = 1.0                      # all equal -> index 0
+    if t > 1:
+        x[1, 5] = 9.0
+        x[1, n - 1] = 9.0              # tie -> lower index
+    if n > 10502:
+        x[:, 10502:] = -1e30           # padded vocabulary columns never win
+    px, po = dev.put(x), dev.empty(t * 4)
+    L.wk_argmax(None, px, t, n, po)
+    ref = np.array([orc.lib().wo_argmax(x[i].ctypes.data, n) for i in range(t)], np.uint32)
+    np.testing.assert_array_equal(dev.get(po, (t,), np.uint32), ref)
+
+
+@pytest.mark.parametrize("t", [5, 9, 64, 1950, 2003])
+def test_wk_front_bit_exact(gpu_lib, dev, orc, pkg, t):
+    L = gpu_lib
+    rng = np.random.default_rng(t)
+    x = (3 * rng.standard_normal((t, 40))).astype(np.float32)
+    c1 = (rng.standard_normal((32, 1, 5, 5)) * np.sqrt(2 / 25)).astype(np.float32)
+    c2 = (rng.standard_normal((64, 32, 7, 7)) * np.sqrt(2 / 1568)).astype(np.float32)
+    c3 = (rng.standard_normal((192, 64, 3, 3)) * np.sqrt(2 / 576)).astype(np.float32)
+    t1 = (t - 5) // 5 + 1
+    px, p1, p2, p3 = dev.put(x), dev.put(c1), dev.put(c2), dev.put(c3)
+    y1, y2, y3 = dev.empty(t * 1280 * 4), dev.empty(t1 * 2624 * 4), dev.empty(t1 * 3840 * 4)
+    L.wk_front(None, px, p1, p2, p3, t, t1, y1, y2, y3)
+    assert L.wk_last_error() == 0
+    got = dev.get(y3, (t1, 3840), np.float32)
+    np.testing.assert_array_equal(got, orc.frontend(x, c1, c2, c3))
+
+
+@pytest.mark.parametrize("t", [1, 5, 31, 32, 33, 150, 390, 512])
+def test_wk_attention(gpu_lib, dev, orc, t):
+    L = gpu_lib
+    rng = np.random.default_rng(t + 100)
+    q, k, v = [(rng.standard_normal((t, 512)) * 1.5).astype(np.float32) for _ in range(3)]
+    pq, pk, pv, po, sc = dev.put(q), dev.put(k), dev.put(v), dev.empty(t * 512 * 4), dev.empty(8 * t * t * 4)
+    assert L.wk_attention_fast(None, pq, pk, pv, t, 512, 8, sc, po) == 0
+    got = dev.get(po, (t, 512), np.float32)
+    ref = orc.attention(q, k, v)
+    np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-6)
+    assert L.wk_attention_tiled(None, pq, pk, pv, t, 512, 8, None, po) == 0
+    assert L.wk_attention_cublas(None, pq, pk, pv, t, 512, 8, sc, po) == 0
+    np.testing.assert_allclose(dev.get(po, (t, 512), np.float32), ref, rtol=1e-5, atol=1e-6)
+    # return codes of csrc/wk_attention_*.cu
+    assert L.wk_attention_fast(None, None, pk, pv, t, 512, 8, sc, po) == -1
+    assert L.wk_attention_fast(None, pq, pk, pv, t, 512, 7, sc, po) == -2
+    assert L.wk_attention_fast(None, pq, pk, pv, t, 256, 8, sc, po) == -3
+    assert L.wk_attention_tiled_tuned(None, pq, pk, pv, t, 512, 8, po, 12, 64) == -4

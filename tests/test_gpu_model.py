@@ -1,0 +1,205 @@
+"""Model-level GPU parity: the batched engine (include/wasr.h) and the reference-ABI window
+path (host.WindowModel, a mirror of src/model.rs:504-619) against the oracle.
+
+Bars: fp32 logits within 1e-3 relative error; per-frame argmax ids
+agree on >= 99.9% of frames; CTC output identical where no logit tie falls within 1e-3.
+"""
+import ctypes as C
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def rel_err(a, b):
+    return float(np.max(np.abs(a - b)) / max(np.max(np.abs(b)), 1e-30))
+
+
+def near_tie_rows(lo, tol=1e-3):
+    top = -np.sort(-lo, axis=1)[:, :2]
+    return np.abs(top[:, 0] - top[:, 1]) <= tol * np.maximum(np.abs(top[:, 0]), 1.0)
+
+
+def check_ids(got, ref, lo_ref):
+    got, ref = np.asarray(got), np.asarray(ref)
+    assert got.shape == ref.shape
+    agree = np.mean(got == ref) if ref.size else 1.0
+    assert agree >= 0.999 or np.all((got == ref) | near_tie_rows(lo_ref)), agree
+
+
+@pytest.fixture(scope="module")
+def model40(pkg):
+    return pkg.synth.make_model(seed=11, n_layers=40)
+
+
+def test_golden_small_model(pkg, gpu_lib):
+    g = np.load(os.path.join(GOLD, "fwd_small.npz"))
+    blob, plan = pkg.synth.make_model(seed=3, n_layers=2)
+    eng = pkg.Engine(blob, plan, max_rows=512)
+    try:
+        (ids,), (lo,) = eng.forward([g["feats"]], want_logits=True)
+        top = -np.sort(-lo, axis=1)[:, :5]
+        assert rel_err(top, g["top5"]) <= 1e-3
+        assert rel_err(lo[0], g["logits0"]) <= 1e-3 and rel_err(lo[7], g["logits7"]) <= 1e-3
+        full = np.stack([g["logits0"], g["logits7"]])
+        check_ids(ids, g["ids"], np.concatenate([full, np.repeat(full[:1], len(ids) - 2, 0)])
+                  if len(ids) > 2 else full)
+        (ids2,) = eng.forward([g["feats"]])
+        np.testing.assert_array_equal(ids2, ids)
+    finally:
+        eng.close()
+
+
+def test_full_model_window_vs_oracle(pkg, orc, gpu_lib, model40):
+    """40 layers, one blk-1600 window (t = 200 + 1600 + 100 + 50 = 1950 frames, t1 = 390)."""
+    blob, plan = model40
+    pcm = pkg.synth.make_audio(5, 19.6)
+    feats, sil = pkg.fbank(pcm)
+    x = feats[:1950]
+    ids_ref, lo_ref = orc.forward(blob, plan, x, want_logits=True)
+    eng = pkg.Engine(blob, plan, max_rows=2048)
+    try:
+        (ids,), (lo,) = eng.forward([x], want_logits=True)
+        assert rel_err(lo, lo_ref) <= 1e-3, rel_err(lo, lo_ref)
+        check_ids(ids, ids_ref, lo_ref)
+        (ids_fused,) = eng.forward([x])             # fused GEMM+argmax path
+        np.testing.assert_array_equal(ids_fused, ids)
+        assert eng.error() == 0
+    finally:
+        eng.close()
+
+
+def test_reference_abi_window_path_matches_engine(pkg, orc, gpu_lib, model40):
+    """The per-window op sequence through wp_*/wk_* (as the Rust shell drives it) gives the same
+    ids as the batched engine, with and without CUDA-graph capture/replay."""
+    blob, plan = model40
+    feats, _ = pkg.fbank(pkg.synth.make_audio(6, 8.0))
+    x = feats[:700]
+    eng = pkg.Engine(blob, plan, max_rows=1024)
+    wm = pkg.WindowModel(blob, plan, graphs=True)
+    try:
+        (ids_e,) = eng.forward([x])
+        ids_w = wm.forward(x)               # first call captures the t1 graph and replays it
+        ids_w2 = wm.forward(x)              # replay
+        np.testing.assert_array_equal(ids_w, ids_e)
+        np.testing.assert_array_equal(ids_w2, ids_e)
+        wm.graph_on = False
+        wm.g.graphs.clear()
+        np.testing.assert_array_equal(wm.forward(x[:333]), eng.forward([x[:333]])[0])
+    finally:
+        wm.close()
+        eng.close()
+
+
+def test_batched_ragged_equals_one_by_one(pkg, gpu_lib):
+    """Stacking windows of different lengths changes nothing per window (row-independent ops,
+    per-segment conv and attention); also t < 5 windows give no frames."""
+    blob, plan = pkg.synth.make_model(seed=4, n_layers=3)
+    feats, _ = pkg.fbank(pkg.synth.make_audio(8, 30.0))
+    lens = [1950, 5, 4, 6, 33, 1234, 9, 400, 2000, 1]
+    wins, p = [], 0
+    for n in lens:
+        wins.append(feats[p:p + n])
+        p += n
+    eng = pkg.Engine(blob, plan, max_rows=1500)     # forces several chunks
+    try:
+        ids_b, lo_b = eng.forward(wins, want_logits=True)
+        for w, ib, lb in zip(wins, ids_b, lo_b):
+            (i1,), (l1,) = eng.forward([w], want_logits=True)
+            np.testing.assert_array_equal(ib, i1)
+            np.testing.assert_array_equal(lb, l1)
+        ids_g = eng.forward(wins)                   # graph path (captured, then replayed)
+        ids_g2 = eng.forward(wins)
+        for a, b, c in zip(ids_b, ids_g, ids_g2):
+            np.testing.assert_array_equal(a, b)
+            np.testing.assert_array_equal(a, c)
+        assert [len(i) for i in ids_b] == [(n - 5) // 5 + 1 if n >= 5 else 0 for n in lens]
+    finally:
+        eng.close()
+
+
+def test_transcribe_schedule_vs_oracle(pkg, orc, gpu_lib):
+    """src/stream.rs schedule (commit windows, blank-pair cut, tail decode, whole utterance
+    <= 2000 frames) over a batch of utterances, 4-layer model."""
+    blob, plan = pkg.synth.make_model(seed=12, n_layers=4)
+    utts = [pkg.synth.make_audio(30 + i, s) for i, s in enumerate([58.65, 3.0, 21.0, 0.02, 19.99, 45.5])]
+    fs = [pkg.fbank(u) for u in utts]
+    eng = pkg.Engine(blob, plan, max_rows=4096)
+    try:
+        got = eng.transcribe([f for f, _ in fs], [s for _, s in fs], blk=1600)
+        for (f, s), g in zip(fs, got):
+            ref, nf = orc.transcribe(blob, plan, f, s, blk=1600)
+            assert abs(len(g) - len(ref)) <= 2
+            m = min(len(g), len(ref))
+            assert m == 0 or np.mean(g[:m] == ref[:m]) >= 0.999
+            np.testing.assert_array_equal(pkg.ctc_collapse(g), orc.ctc(ref))
+        got400 = eng.transcribe([fs[0][0]], [fs[0][1]], blk=400)
+        ref400, _ = orc.transcribe(blob, plan, fs[0][0], fs[0][1], blk=400)
+        np.testing.assert_array_equal(pkg.ctc_collapse(got400[0]), orc.ctc(ref400))
+    finally:
+        eng.close()
+
+
+def test_config1_layer_with_biases_per_channel(pkg, orc, gpu_lib, dev):
+    """one encoder layer, T=400, h ~ N(0,1), gamma=1, beta=0, per-channel
+    scales and a bias on every projection, composed from the reference ABI calls."""
+    L = gpu_lib
+    blob, plan = pkg.synth.make_model(seed=21, n_layers=1, per_channel=True, proj_bias=True, ln_identity=True)
+    T = 400
+    rng = np.random.default_rng(77)
+    h = rng.standard_normal((T, 512)).astype(np.float32)
+    lay = plan.layers[0]
+    bf = lambda off, n: np.frombuffer(blob[off:off + 4 * n].tobytes(), np.float32)  # noqa: E731
+    wm = lambda m: np.frombuffer(blob[m.off:m.off + m.n * m.k].tobytes(), np.int8).reshape(m.n, m.k)  # noqa: E731
+    # oracle (src/model.rs:490-497 with the bias extension)
+    y = orc.norm(h, bf(lay.pn_g, 512), bf(lay.pn_b, 512))
+    xq, xs = orc.quant(y)
+    mm = lambda xq, xs, m, b: orc.qgemm(xq, xs, wm(m), m.s, ws_vec=bf(m.scale_off, m.n), bias=bf(b, m.n))  # noqa
+    q, k, v = mm(xq, xs, lay.q, lay.qb), mm(xq, xs, lay.k, lay.kb), mm(xq, xs, lay.v, lay.vb)
+    aq, asc = orc.quant(orc.attention(q, k, v))
+    h_ref = (h + mm(aq, asc, lay.o, lay.ob)).astype(np.float32)
+    fq, fs = orc.quant(orc.norm(h_ref, bf(lay.mn_g, 512), bf(lay.mn_b, 512)))
+    f = orc.gelu(mm(fq, fs, lay.f1, lay.f1b))
+    gq, gs = orc.quant(f)
+    h_ref = (h_ref + mm(gq, gs, lay.f2, lay.f2b)).astype(np.float32)
+    # GPU through the ABI
+    ctx = L.wp_create(blob.ctypes.data, blob.size)
+    assert ctx
+    try:
+        dv = lambda off: L.wp_devptr(ctx, off)  # noqa: E731
+        ph = dev.put(h)
+        pxq, pxs = dev.empty(T * 2048), dev.empty(T * 4)
+        pq, pk, pv, pa, po = [dev.empty(T * 512 * 4) for _ in range(5)]
+        pf = dev.empty(T * 2048 * 4)
+        L.wk_norm_quant(None, ph, dv(lay.pn_g), dv(lay.pn_b), T, 512, pxq, pxs)
+        for m, b, out in ((lay.q, lay.qb, pq), (lay.k, lay.kb, pk), (lay.v, lay.vb, pv)):
+            assert L.wp_gemm2_pc(ctx, pxq, pxs, T, 512, m.off, m.n, dv(m.scale_off), dv(b), None, out) == 0
+        assert L.wk_attention_fast(None, pq, pk, pv, T, 512, 8, None, pa) == 0
+        L.wk_quant(None, pa, T, 512, pxq, pxs)
+        assert L.wp_gemm2_pc(ctx, pxq, pxs, T, 512, lay.o.off, 512, dv(lay.o.scale_off), dv(lay.ob), None, po) == 0
+        L.wk_add_norm_quant(None, ph, po, dv(lay.mn_g), dv(lay.mn_b), T, 512, pxq, pxs)
+        assert L.wp_gemm2_pc(ctx, pxq, pxs, T, 512, lay.f1.off, 2048, dv(lay.f1.scale_off), dv(lay.f1b), None,
+                             pf) == 0
+        L.wk_gelu_quant(None, pf, T, 2048, pxq, pxs)
+        assert L.wp_gemm2_pc(ctx, pxq, pxs, T, 2048, lay.f2.off, 512, dv(lay.f2.scale_off), dv(lay.f2b), None,
+                             po) == 0
+        L.wk_add(None, ph, po, T, 512)
+        assert L.wp_sync(ctx) == 0
+        got = dev.get(ph, (T, 512), np.float32)
+        assert rel_err(got, h_ref) <= 1e-3, rel_err(got, h_ref)
+    finally:
+        L.wp_destroy(ctx)
+    # the batched engine runs the same layer (with q/k/v biases, non-fused q/k/v because the
+    # per-channel scale vectors sit between the matrices) -- checked end to end on ids
+    eng = pkg.Engine(blob, plan, max_rows=512)
+    try:
+        feats, _ = pkg.fbank(pkg.synth.make_audio(3, 4.0))
+        ids_ref, lo_ref = orc.forward(blob, plan, feats, want_logits=True)
+        (ids,), (lo,) = eng.forward([feats], want_logits=True)
+        assert rel_err(lo, lo_ref) <= 1e-3
+        check_ids(ids, ids_ref, lo_ref)
+    finally:
+        eng.close()

@@ -1,0 +1,874 @@
+// engine.cu -- the batched transcription engine behind include/wasr.h.
+//
+// The reference runs one window per forward (Model::run_gpu, src/model.rs:546-619: upload
+// feats, conv frontend, quant, linear, 40 x window_ops, output GEMM, argmax, download ids)
+// and one utterance at a time (src/bin/wasr.rs:147-169).  Here many windows -- the k-th
+// window of every utterance in flight -- are stacked along the row axis of every GEMM, so
+// the int8 GEMMs see M = sum of t1 instead of t1 <= 400, while the conv frontend and
+// attention stay inside each window (segment tables).  The op sequence per layer follows
+// window_ops (src/model.rs:522-541) / run_post (src/model.rs:488-502), with these fusions:
+//   q/k/v         : one GEMM over the contiguous [1536][512] weight block (per-column scale)
+//   o, f2         : residual add fused into the GEMM epilogue (h += ...)
+//   f1            : bias + GELU + row |max| fused into the GEMM epilogue; the quant pass reads it
+//   output layer  : GEMM fused with the argmax (logits never written unless asked for)
+// A whole chunk of windows is captured once in a CUDA graph and replayed when the same
+// window layout comes back (the reference graphs one window per t1, src/model.rs:576-604).
+#include <omp.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/wasr.h"
+#include "gemm.cuh"
+#include "kern.cuh"
+
+using namespace wasr;
+
+namespace {
+
+constexpr size_t kMaxGraphs = 64;
+
+struct Chunk {
+  int w0, w1;        // windows [w0, w1) of the call
+  int frames, rows;  // totals over the chunk
+  int max_t1;
+  int tiles;         // attention query tiles
+};
+
+struct Rec {
+  int cat;
+  cudaEvent_t a, b;
+};
+
+struct GraphEntry {
+  cudaGraphExec_t exec = nullptr;
+  int* seg = nullptr;  // device copy of this layout's segment tables
+  uint64_t use = 0;
+  int64_t kernels = 0;  // kernel nodes in the graph
+  std::vector<Rec> recs;
+};
+
+}  // namespace
+
+struct WasrModel {
+  int dev = 0;
+  cudaStream_t own = nullptr, stream = nullptr;
+  uint8_t* w = nullptr;
+  size_t w_bytes = 0;
+  WasrPlan plan{};
+  int max_rows = 0, max_frames = 0;
+  // q/k/v fused: per-column scale (and bias) vectors over the [1536] output
+  float* qkv_scale[WASR_MAX_LAYERS] = {};
+  float* qkv_bias[WASR_MAX_LAYERS] = {};
+  bool qkv_fused[WASR_MAX_LAYERS] = {};
+  // activations
+  float *feats = nullptr, *y1 = nullptr, *y2 = nullptr, *y3 = nullptr;
+  int8_t* xq = nullptr;
+  float* xs = nullptr;
+  float *h = nullptr, *qkv = nullptr, *att = nullptr, *f = nullptr;
+  unsigned* rowmax = nullptr;
+  unsigned long long* keys = nullptr;
+  uint32_t* ids = nullptr;
+  int* seg = nullptr;  // segment tables of eager runs: foff | roff | toff
+  int seg_cap = 0;
+  int* err_host = nullptr;
+  int* err_dev = nullptr;
+  bool graphs = true;
+  bool prof = false;
+  int64_t launches = 0;
+  std::vector<Rec> eager_recs;
+  uint64_t tick = 0;
+  std::unordered_map<std::string, GraphEntry> graph_cache;
+  // pinned host staging
+  float* h_feats = nullptr;
+  size_t h_feats_cap = 0;
+  uint32_t* h_ids = nullptr;
+  size_t h_ids_cap = 0;
+  int* h_seg = nullptr;
+  size_t h_seg_cap = 0;
+  std::mutex mu;
+};
+
+namespace {
+
+template <typename T>
+bool dmalloc(T** p, size_t n) {
+  return cudaMalloc(reinterpret_cast<void**>(p), std::max<size_t>(n, 1) * sizeof(T)) == cudaSuccess;
+}
+
+template <typename T>
+bool hgrow(T** p, size_t* cap, size_t n) {
+  if (n <= *cap) return true;
+  if (*p) cudaFreeHost(*p);
+  *p = nullptr;
+  *cap = 0;
+  if (cudaHostAlloc(reinterpret_cast<void**>(p), n * sizeof(T), cudaHostAllocDefault) != cudaSuccess) return false;
+  *cap = n;
+  return true;
+}
+
+struct DevGuard {
+  int prev = -1;
+  explicit DevGuard(int d) {
+    cudaGetDevice(&prev);
+    if (prev != d) cudaSetDevice(d);
+  }
+  ~DevGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+inline int t1_of(int t) { return t >= 5 ? (t - 5) / 5 + 1 : 0; }
+
+const float* fptr(const WasrModel* m, uint64_t off) {
+  return off == WASR_NONE ? nullptr : reinterpret_cast<const float*>(m->w + off);
+}
+
+GemmArgs gemm_args(WasrModel* m, const int8_t* a, const float* xs, int M, int K, const WasrMat& q, int N,
+                   uint64_t bias, int epi, float* out, int ldo) {
+  GemmArgs g{};
+  g.a = a;
+  g.b = reinterpret_cast<const int8_t*>(m->w + q.off);
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.n_store = N;
+  g.xs = xs;
+  g.ws = q.s;
+  g.ws_vec = fptr(m, q.scale_off);
+  g.bias = fptr(m, bias);
+  g.out = out;
+  g.ldo = ldo;
+  g.err = m->err_dev;
+  g.epi = epi;
+  return g;
+}
+
+#define TRY(x)           \
+  do {                   \
+    int rc_ = (x);       \
+    if (rc_) return rc_; \
+  } while (0)
+
+void free_recs(std::vector<Rec>* r) {
+  for (Rec& x : *r) {
+    cudaEventDestroy(x.a);
+    cudaEventDestroy(x.b);
+  }
+  r->clear();
+}
+
+// Counts every kernel enqueued and, when recs != nullptr, brackets it with an event pair.
+struct Launcher {
+  WasrModel* m;
+  std::vector<Rec>* recs;
+  int64_t kernels = 0;
+  template <typename F>
+  int operator()(int cat, F&& f) {
+    Rec r{cat, nullptr, nullptr};
+    if (recs) {
+      if (cudaEventCreate(&r.a) != cudaSuccess || cudaEventCreate(&r.b) != cudaSuccess) return -4;
+      cudaEventRecord(r.a, m->stream);
+    }
+    const int rc = f();
+    if (recs) {
+      cudaEventRecord(r.b, m->stream);
+      recs->push_back(r);
+    }
+    kernels++;
+    return rc;
+  }
+};
+
+// Enqueue the whole forward of one chunk on m->stream.  The chunk's frames are at m->feats;
+// seg points at its device segment tables [foff n+1 | roff n+1 | toff n+1].
+int enqueue_chunk(WasrModel* m, const Chunk& c, const int* seg, float* logits, Launcher& K) {
+  cudaStream_t st = m->stream;
+  const int n = c.w1 - c.w0;
+  Segs s{};
+  s.foff = seg;
+  s.roff = seg + (n + 1);
+  s.n = n;
+  const int* toff = seg + 2 * (n + 1);
+  const int M = c.rows;
+  const WasrPlan& P = m->plan;
+  // conv frontend -> y3 -> int8 -> linear (src/model.rs:389-478,489)
+  TRY(K(WASR_K_CONV1, [&] { return launch_conv1(m->feats, fptr(m, P.c1), s, c.frames, m->y1, st); }));
+  TRY(K(WASR_K_CONV2, [&] { return launch_conv2(m->y1, fptr(m, P.c2), s, M, m->y2, st); }));
+  TRY(K(WASR_K_CONV3, [&] { return launch_conv3(m->y2, fptr(m, P.c3), s, M, m->y3, st); }));
+  TRY(K(WASR_K_QUANT, [&] { return launch_quant_rows(m->y3, M, FLAT, FLAT, m->xq, m->xs, st); }));
+  TRY(K(WASR_K_GEMM_LIN, [&] { return gemm_run(gemm_args(m, m->xq, m->xs, M, FLAT, P.lin, D, P.lin_b, EPI_F32, m->h, D), st); }));
+  for (int l = 0; l < P.n_layers; l++) {
+    const WasrLayer& L = P.layers[l];
+    // prior norm -> q, k, v
+    TRY(K(WASR_K_LN, [&] { return launch_ln_quant(m->h, nullptr, fptr(m, L.pn_g), fptr(m, L.pn_b), M, m->xq, m->xs, st); }));
+    if (m->qkv_fused[l]) {
+      GemmArgs g = gemm_args(m, m->xq, m->xs, M, D, L.q, 3 * D, WASR_NONE, EPI_F32, m->qkv, 3 * D);
+      g.ws_vec = m->qkv_scale[l];
+      g.bias = m->qkv_bias[l];
+      TRY(K(WASR_K_GEMM_QKV, [&] { return gemm_run(g, st); }));
+    } else {
+      const WasrMat* pm[3] = {&L.q, &L.k, &L.v};
+      const uint64_t pb[3] = {L.qb, L.kb, L.vb};
+      for (int p = 0; p < 3; p++)
+        TRY(K(WASR_K_GEMM_QKV, [&] {
+          return gemm_run(gemm_args(m, m->xq, m->xs, M, D, *pm[p], D, pb[p], EPI_F32, m->qkv + p * D, 3 * D), st);
+        }));
+    }
+    // attention -> quant -> o projection, residual fused (src/model.rs:493)
+    TRY(K(WASR_K_ATTN, [&] { return launch_attention(m->qkv, m->qkv + D, m->qkv + 2 * D, 3 * D, s, toff, c.tiles, c.max_t1, m->att, D, st); }));
+    TRY(K(WASR_K_QUANT, [&] { return launch_quant_rows(m->att, M, D, D, m->xq, m->xs, st); }));
+    TRY(K(WASR_K_GEMM_O, [&] { return gemm_run(gemm_args(m, m->xq, m->xs, M, D, L.o, D, L.ob, EPI_F32_ADD, m->h, D), st); }));
+    // middle norm -> f1 + bias + GELU (+ row max) -> quant -> f2 + bias, residual fused
+    TRY(K(WASR_K_LN, [&] { return launch_ln_quant(m->h, nullptr, fptr(m, L.mn_g), fptr(m, L.mn_b), M, m->xq, m->xs, st); }));
+    if (cudaMemsetAsync(m->rowmax, 0, static_cast<size_t>(M) * sizeof(unsigned), st) != cudaSuccess) return -4;
+    {
+      GemmArgs g = gemm_args(m, m->xq, m->xs, M, D, L.f1, FF, L.f1b, EPI_GELU_ROWMAX, m->f, FF);
+      g.rowmax = m->rowmax;
+      TRY(K(WASR_K_GEMM_F1, [&] { return gemm_run(g, st); }));
+    }
+    TRY(K(WASR_K_QUANT, [&] { return launch_quant_rows_max(m->f, M, FF, m->rowmax, m->xq, m->xs, st); }));
+    TRY(K(WASR_K_GEMM_F2, [&] { return gemm_run(gemm_args(m, m->xq, m->xs, M, FF, L.f2, D, L.f2b, EPI_F32_ADD, m->h, D), st); }));
+  }
+  // output layer + argmax (src/model.rs:498-501)
+  TRY(K(WASR_K_QUANT, [&] { return launch_quant_rows(m->h, M, D, D, m->xq, m->xs, st); }));
+  if (logits) {
+    TRY(K(WASR_K_GEMM_OUT, [&] { return gemm_run(gemm_args(m, m->xq, m->xs, M, D, P.out, P.out_n, P.out_b, EPI_F32, logits, P.out_n), st); }));
+    TRY(K(WASR_K_IDS, [&] { return launch_argmax_rows(logits, M, P.out_n, m->ids, st); }));
+  } else {
+    if (cudaMemsetAsync(m->keys, 0, static_cast<size_t>(M) * sizeof(unsigned long long), st) != cudaSuccess)
+      return -4;
+    GemmArgs g = gemm_args(m, m->xq, m->xs, M, D, P.out, P.out_n, P.out_b, EPI_ARGMAX, nullptr, P.out_n);
+    g.keys = m->keys;
+    TRY(K(WASR_K_GEMM_OUT, [&] { return gemm_run(g, st); }));
+    TRY(K(WASR_K_IDS, [&] { return launch_keys_to_ids(m->keys, M, m->ids, st); }));
+  }
+  return 0;
+}
+
+// segment tables of windows [w0, w1): foff | roff | toff, each n+1 ints
+void build_seg(const int32_t* t, int w0, int w1, int* out) {
+  const int n = w1 - w0;
+  int* fo = out;
+  int* ro = out + n + 1;
+  int* to = out + 2 * (n + 1);
+  fo[0] = ro[0] = to[0] = 0;
+  for (int i = 0; i < n; i++) {
+    const int tt = std::max(0, t[w0 + i]);
+    const int t1 = t1_of(tt);
+    fo[i + 1] = fo[i] + tt;
+    ro[i + 1] = ro[i] + t1;
+    to[i + 1] = to[i] + (t1 + ATT_QT - 1) / ATT_QT;
+  }
+}
+
+// split windows into chunks that fit the activation buffers
+bool plan_chunks(const WasrModel* m, const int32_t* t, int n, std::vector<Chunk>* out) {
+  out->clear();
+  int i = 0;
+  while (i < n) {
+    Chunk c{i, i, 0, 0, 0, 0};
+    while (c.w1 < n) {
+      const int tt = std::max(0, t[c.w1]);
+      const int t1 = t1_of(tt);
+      if (tt > m->max_frames || t1 > m->max_rows) return false;  // one window alone too big
+      if (c.frames + tt > m->max_frames || c.rows + t1 > m->max_rows) break;
+      c.frames += tt;
+      c.rows += t1;
+      c.max_t1 = std::max(c.max_t1, t1);
+      c.tiles += (t1 + ATT_QT - 1) / ATT_QT;
+      c.w1++;
+    }
+    out->push_back(c);
+    i = c.w1;
+  }
+  return true;
+}
+
+std::string layout_key(const int32_t* t, const Chunk& c, bool logits) {
+  std::string k;
+  k.reserve((c.w1 - c.w0) * 4 + 2);
+  k.push_back(logits ? 'L' : 'I');
+  k.append(reinterpret_cast<const char*>(t + c.w0), (c.w1 - c.w0) * sizeof(int32_t));
+  return k;
+}
+
+void free_graphs(WasrModel* m) {
+  for (auto& kv : m->graph_cache) {
+    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    if (kv.second.seg) cudaFree(kv.second.seg);
+    free_recs(&kv.second.recs);
+  }
+  m->graph_cache.clear();
+}
+
+// Run one chunk (frames already in m->feats): replay its graph if this layout was seen,
+// else capture it (graphs on) or run it eagerly.
+int run_chunk(WasrModel* m, const int32_t* t, const Chunk& c, float* logits) {
+  const int n = c.w1 - c.w0;
+  const size_t seg_ints = 3 * static_cast<size_t>(n + 1);
+  if (!hgrow(&m->h_seg, &m->h_seg_cap, seg_ints)) return -5;
+  cudaStream_t st = m->stream;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(st, &cs);
+  const bool use_graph = m->graphs && logits == nullptr && cs == cudaStreamCaptureStatusNone;
+  if (use_graph) {
+    const std::string key = layout_key(t, c, false);
+    auto it = m->graph_cache.find(key);
+    if (it == m->graph_cache.end()) {
+      if (m->graph_cache.size() >= kMaxGraphs) {
+        auto lru = m->graph_cache.begin();
+        for (auto i2 = m->graph_cache.begin(); i2 != m->graph_cache.end(); ++i2)
+          if (i2->second.use < lru->second.use) lru = i2;
+        cudaStreamSynchronize(st);
+        if (lru->second.exec) cudaGraphExecDestroy(lru->second.exec);
+        if (lru->second.seg) cudaFree(lru->second.seg);
+        free_recs(&lru->second.recs);
+        m->graph_cache.erase(lru);
+      }
+      GraphEntry e;
+      if (!dmalloc(&e.seg, seg_ints)) return -5;
+      build_seg(t, c.w0, c.w1, m->h_seg);
+      if (cudaMemcpy(e.seg, m->h_seg, seg_ints * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaFree(e.seg);
+        return -4;
+      }
+      if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaFree(e.seg);
+        cudaGetLastError();
+        return -10;
+      }
+      Launcher K{m, m->prof ? &e.recs : nullptr};
+      const int rc = enqueue_chunk(m, c, e.seg, nullptr, K);
+      e.kernels = K.kernels;
+      cudaGraph_t g = nullptr;
+      const cudaError_t ee = cudaStreamEndCapture(st, &g);
+      if (rc || ee != cudaSuccess || !g) {
+        if (g) cudaGraphDestroy(g);
+        cudaFree(e.seg);
+        free_recs(&e.recs);
+        cudaGetLastError();
+        return rc ? rc : -13;
+      }
+      const cudaError_t ie = cudaGraphInstantiate(&e.exec, g, 0);
+      cudaGraphDestroy(g);
+      if (ie != cudaSuccess) {
+        cudaFree(e.seg);
+        free_recs(&e.recs);
+        cudaGetLastError();
+        return -15;
+      }
+      it = m->graph_cache.emplace(key, e).first;
+    }
+    it->second.use = ++m->tick;
+    m->launches += it->second.kernels;
+    return cudaGraphLaunch(it->second.exec, st) == cudaSuccess ? 0 : -17;
+  }
+  // eager: per-call segment tables
+  if (static_cast<size_t>(m->seg_cap) < seg_ints) {
+    cudaStreamSynchronize(st);
+    if (m->seg) cudaFree(m->seg);
+    m->seg = nullptr;
+    m->seg_cap = 0;
+    if (!dmalloc(&m->seg, seg_ints * 2)) return -5;
+    m->seg_cap = static_cast<int>(seg_ints * 2);
+  }
+  build_seg(t, c.w0, c.w1, m->h_seg);
+  if (cudaMemcpyAsync(m->seg, m->h_seg, seg_ints * sizeof(int), cudaMemcpyHostToDevice, st) != cudaSuccess)
+    return -4;
+  cudaStreamSynchronize(st);  // the previous eager chunk's events may still be pending
+  free_recs(&m->eager_recs);
+  Launcher K{m, m->prof ? &m->eager_recs : nullptr};
+  const int rc = enqueue_chunk(m, c, m->seg, logits, K);
+  m->launches += K.kernels;
+  // the pinned table is reused by the next chunk: make sure this copy has consumed it
+  cudaStreamSynchronize(st);
+  return rc;
+}
+
+int device_error(WasrModel* m) {
+  const int e = *reinterpret_cast<volatile int*>(m->err_host);
+  if (e) {
+    *m->err_host = 0;
+    return -21;
+  }
+  return 0;
+}
+
+// forward over windows whose frames are at feats (host or device per flags)
+int forward_impl(WasrModel* m, const float* feats, const int32_t* t, int n, uint32_t* ids, float* logits, int flags) {
+  if (!m || !t || n < 0 || (!feats && n > 0) || !ids) return -1;
+  if (n == 0) return 0;
+  std::vector<Chunk> chunks;
+  if (!plan_chunks(m, t, n, &chunks)) return -2;
+  const bool on_dev = flags & WASR_F_DEVICE;
+  cudaStream_t st = m->stream;
+  int64_t f_off = 0, r_off = 0;
+  for (const Chunk& c : chunks) {
+    const size_t fbytes = static_cast<size_t>(c.frames) * DIM * sizeof(float);
+    if (fbytes) {
+      const float* src = feats + f_off * DIM;
+      if (on_dev) {
+        if (cudaMemcpyAsync(m->feats, src, fbytes, cudaMemcpyDeviceToDevice, st) != cudaSuccess) return -4;
+      } else {
+        if (cudaMemcpyAsync(m->feats, src, fbytes, cudaMemcpyHostToDevice, st) != cudaSuccess) return -4;
+      }
+    }
+    float* lo = nullptr;
+    if (logits) lo = logits + r_off * m->plan.out_n;
+    float* lo_dev = lo;
+    if (logits && !on_dev) lo_dev = nullptr;  // host logits: computed into m->f-sized scratch below
+    if (logits && !on_dev) {
+      if (!dmalloc(&lo_dev, static_cast<size_t>(c.rows) * m->plan.out_n)) return -5;
+    }
+    TRY(run_chunk(m, t, c, lo_dev));
+    const size_t ibytes = static_cast<size_t>(c.rows) * sizeof(uint32_t);
+    if (ibytes) {
+      const cudaMemcpyKind kind = on_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
+      if (cudaMemcpyAsync(ids + r_off, m->ids, ibytes, kind, st) != cudaSuccess) return -4;
+    }
+    if (logits && !on_dev) {
+      const size_t lb = static_cast<size_t>(c.rows) * m->plan.out_n * sizeof(float);
+      cudaMemcpyAsync(lo, lo_dev, lb, cudaMemcpyDeviceToHost, st);
+      cudaStreamSynchronize(st);
+      cudaFree(lo_dev);
+    }
+    // the next chunk overwrites m->feats / m->ids: host copies must have landed
+    if (!on_dev || chunks.size() > 1) cudaStreamSynchronize(st);
+    f_off += c.frames;
+    r_off += c.rows;
+  }
+  if (!(flags & WASR_F_NOSYNC) || !on_dev) {
+    if (cudaStreamSynchronize(st) != cudaSuccess) return -4;
+    return device_error(m);
+  }
+  return 0;
+}
+
+}  // namespace
+
+// ============================================================================ host fbank
+// src/fbank.rs restated for the product (feature extraction feeding the window schedule):
+// 25 ms Hamming window, pre-emphasis 0.97, f64 radix-2 FFT512, 39 HTK mel bands + log
+// energy, CMS over the last 50 frames.  Same operation order as the reference, so the
+// features are bit-identical (host code is compiled with -ffp-contract=off).
+namespace fb {
+
+constexpr int WIN = 400, HOP = 160, NFFT = 512, NCH = 39, CMS_WIN = 50;
+
+struct Tables {
+  double ham[WIN];
+  double twr[NFFT / 2], twi[NFFT / 2];
+  int lo[NFFT / 2], hi[NFFT / 2];
+  double wl[NFFT / 2], wh[NFFT / 2];
+  Tables() {
+    const double pi = 3.14159265358979323846;
+    for (int i = 0; i < WIN; i++) ham[i] = 0.54 - 0.46 * std::cos(2.0 * pi * static_cast<double>(i) / (WIN - 1));
+    for (int i = 0; i < NFFT / 2; i++) {
+      const double a = -2.0 * pi * static_cast<double>(i) / NFFT;
+      twr[i] = std::cos(a);
+      twi[i] = std::sin(a);
+    }
+    auto mel = [](double f) { return 1127.0 * std::log(1.0 + f / 700.0); };
+    const double top = mel(8000.0);
+    double cf[NCH + 1];
+    for (int i = 1; i <= NCH + 1; i++) cf[i - 1] = top * static_cast<double>(i) / (NCH + 1);
+    for (int k = 1; k <= NFFT / 2; k++) {
+      const double mv = mel(static_cast<double>(k) * 16000.0 / NFFT);
+      int c = 0;
+      while (c < NCH + 1 && cf[c] < mv) c++;
+      const int x = k - 1;
+      lo[x] = hi[x] = 0;
+      wl[x] = wh[x] = 0.0;
+      if (c == 0) {
+        wl[x] = mv / cf[0];
+      } else if (c < NCH) {
+        const double w = (cf[c] - mv) / (cf[c] - cf[c - 1]);
+        lo[x] = c - 1;
+        wl[x] = w;
+        hi[x] = c;
+        wh[x] = 1.0 - w;
+      } else if (c == NCH) {
+        lo[x] = NCH - 1;
+        wl[x] = (cf[NCH] - mv) / (cf[NCH] - cf[NCH - 1]);
+      }
+    }
+  }
+};
+
+const Tables& tables() {
+  static const Tables T;
+  return T;
+}
+
+void frame(const int16_t* x, double* out) {
+  const Tables& T = tables();
+  double re[NFFT] = {0}, im[NFFT] = {0};
+  double e = 0.0;
+  for (int i = 0; i < WIN; i++) {
+    const double v = x[i];
+    e += v * v;
+    const double pe = i == 0 ? v * (1.0 - 0.97) : v - 0.97 * static_cast<double>(x[i - 1]);
+    re[i] = pe * T.ham[i];
+  }
+  for (int i = 1, j = 0; i < NFFT; i++) {
+    int b = NFFT >> 1;
+    while (j & b) {
+      j ^= b;
+      b >>= 1;
+    }
+    j |= b;
+    if (i < j) {
+      std::swap(re[i], re[j]);
+      std::swap(im[i], im[j]);
+    }
+  }
+  for (int len = 2; len <= NFFT; len <<= 1) {
+    const int step = NFFT / len;
+    for (int s = 0; s < NFFT; s += len)
+      for (int k = 0; k < len / 2; k++) {
+        const double wr = T.twr[k * step], wi = T.twi[k * step];
+        const int a = s + k, b = s + k + len / 2;
+        const double tr = re[b] * wr - im[b] * wi;
+        const double ti = re[b] * wi + im[b] * wr;
+        re[b] = re[a] - tr;
+        im[b] = im[a] - ti;
+        re[a] += tr;
+        im[a] += ti;
+      }
+  }
+  for (int i = 0; i < DIM; i++) out[i] = 0.0;
+  for (int k = 0; k < NFFT / 2; k++) {
+    const double p = re[k + 1] * re[k + 1] + im[k + 1] * im[k + 1];
+    out[T.lo[k]] += p * T.wl[k];
+    out[T.hi[k]] += p * T.wh[k];
+  }
+  for (int i = 0; i < NCH; i++) out[i] = std::log(out[i] > 1.0 ? out[i] : 1.0);
+  out[NCH] = std::log(e > 1e-10 ? e : 1e-10);
+}
+
+}  // namespace fb
+
+// ============================================================================ C ABI
+extern "C" {
+
+const char* wasr_version(void) { return "wasr-b200 engine 1.0 (batched ragged windows; sm_100a)"; }
+
+WasrModel* wasr_model_create(const void* blob, size_t bytes, const WasrPlan* plan, int device, int max_rows) {
+  if (!blob || !bytes || !plan || max_rows <= 0) return nullptr;
+  if (plan->n_layers < 0 || plan->n_layers > WASR_MAX_LAYERS || plan->out_n <= 0) return nullptr;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) return nullptr;
+  DevGuard dg(device);
+  gemm_prepare();
+  kern_prepare();
+  WasrModel* m = new WasrModel();
+  m->dev = device;
+  m->plan = *plan;
+  m->max_rows = max_rows;
+  m->max_frames = 5 * max_rows + 4 * std::max(1, max_rows / 20);  // t = 5*t1 + 0..4 per window
+  bool ok = cudaStreamCreateWithFlags(&m->own, cudaStreamNonBlocking) == cudaSuccess;
+  m->stream = m->own;
+  ok = ok && cudaHostAlloc(reinterpret_cast<void**>(&m->err_host), sizeof(int), cudaHostAllocMapped) == cudaSuccess;
+  ok = ok && cudaHostGetDevicePointer(reinterpret_cast<void**>(&m->err_dev), m->err_host, 0) == cudaSuccess;
+  if (ok) *m->err_host = 0;
+  m->w_bytes = bytes;
+  ok = ok && dmalloc(&m->w, bytes) && cudaMemcpy(m->w, blob, bytes, cudaMemcpyHostToDevice) == cudaSuccess;
+  const size_t R = static_cast<size_t>(max_rows), Fr = static_cast<size_t>(m->max_frames);
+  ok = ok && dmalloc(&m->feats, Fr * DIM) && dmalloc(&m->y1, Fr * C1 * DIM) && dmalloc(&m->y2, R * C2 * W2) &&
+       dmalloc(&m->y3, R * FLAT) && dmalloc(&m->xq, R * FLAT) && dmalloc(&m->xs, R) && dmalloc(&m->h, R * D) &&
+       dmalloc(&m->qkv, R * 3 * D) && dmalloc(&m->att, R * D) && dmalloc(&m->f, R * FF) &&
+       dmalloc(&m->rowmax, R) && dmalloc(&m->keys, R) && dmalloc(&m->ids, R);
+  // q/k/v fusion: the three [512][512] matrices must sit back to back in the blob
+  for (int l = 0; ok && l < plan->n_layers; l++) {
+    const WasrLayer& L = plan->layers[l];
+    const uint64_t mat = static_cast<uint64_t>(D) * D;
+    if (L.k.off != L.q.off + mat || L.v.off != L.k.off + mat) continue;
+    std::vector<float> sc(3 * D), bs(3 * D, 0.0f);
+    const WasrMat* qs[3] = {&L.q, &L.k, &L.v};
+    const uint64_t bo[3] = {L.qb, L.kb, L.vb};
+    bool any_bias = false;
+    for (int p = 0; p < 3; p++) {
+      if (qs[p]->scale_off != WASR_NONE)
+        std::memcpy(&sc[p * D], static_cast<const uint8_t*>(blob) + qs[p]->scale_off, D * sizeof(float));
+      else
+        std::fill(sc.begin() + p * D, sc.begin() + (p + 1) * D, qs[p]->s);
+      if (bo[p] != WASR_NONE) {
+        std::memcpy(&bs[p * D], static_cast<const uint8_t*>(blob) + bo[p], D * sizeof(float));
+        any_bias = true;
+      }
+    }
+    ok = ok && dmalloc(&m->qkv_scale[l], 3 * D) &&
+         cudaMemcpy(m->qkv_scale[l], sc.data(), 3 * D * sizeof(float), cudaMemcpyHostToDevice) == cudaSuccess;
+    if (ok && any_bias)
+      ok = dmalloc(&m->qkv_bias[l], 3 * D) &&
+           cudaMemcpy(m->qkv_bias[l], bs.data(), 3 * D * sizeof(float), cudaMemcpyHostToDevice) == cudaSuccess;
+    m->qkv_fused[l] = ok;
+  }
+  if (!ok) {
+    wasr_model_destroy(m);
+    return nullptr;
+  }
+  return m;
+}
+
+void wasr_model_destroy(WasrModel* m) {
+  if (!m) return;
+  DevGuard dg(m->dev);
+  cudaDeviceSynchronize();
+  free_graphs(m);
+  free_recs(&m->eager_recs);
+  void* dptrs[] = {m->w, m->feats, m->y1, m->y2, m->y3, m->xq, m->xs, m->h, m->qkv, m->att, m->f, m->rowmax,
+                   m->keys, m->ids, m->seg};
+  for (void* p : dptrs)
+    if (p) cudaFree(p);
+  for (int l = 0; l < WASR_MAX_LAYERS; l++) {
+    if (m->qkv_scale[l]) cudaFree(m->qkv_scale[l]);
+    if (m->qkv_bias[l]) cudaFree(m->qkv_bias[l]);
+  }
+  if (m->h_feats) cudaFreeHost(m->h_feats);
+  if (m->h_ids) cudaFreeHost(m->h_ids);
+  if (m->h_seg) cudaFreeHost(m->h_seg);
+  if (m->err_host) cudaFreeHost(m->err_host);
+  if (m->own) cudaStreamDestroy(m->own);
+  delete m;
+}
+
+int wasr_model_set_stream(WasrModel* m, void* stream) {
+  if (!m) return -1;
+  std::lock_guard<std::mutex> lk(m->mu);
+  DevGuard dg(m->dev);
+  cudaStreamSynchronize(m->stream);
+  m->stream = stream ? static_cast<cudaStream_t>(stream) : m->own;
+  return 0;
+}
+
+void* wasr_model_stream(WasrModel* m) { return m ? static_cast<void*>(m->stream) : nullptr; }
+
+int wasr_model_set_graphs(WasrModel* m, int on) {
+  if (!m) return -1;
+  std::lock_guard<std::mutex> lk(m->mu);
+  DevGuard dg(m->dev);
+  m->graphs = on != 0;
+  if (!m->graphs) {
+    cudaStreamSynchronize(m->stream);
+    free_graphs(m);
+  }
+  return 0;
+}
+
+int wasr_model_set_profile(WasrModel* m, int on) {
+  if (!m) return -1;
+  std::lock_guard<std::mutex> lk(m->mu);
+  DevGuard dg(m->dev);
+  cudaStreamSynchronize(m->stream);
+  if (m->prof != (on != 0)) free_graphs(m);
+  m->prof = on != 0;
+  return 0;
+}
+
+int wasr_model_profile(WasrModel* m, double* ms, int64_t* launches, int ncat) {
+  if (!m || !ms || !launches || ncat <= 0) return -1;
+  std::lock_guard<std::mutex> lk(m->mu);
+  DevGuard dg(m->dev);
+  if (cudaStreamSynchronize(m->stream) != cudaSuccess) return -4;
+  for (int i = 0; i < ncat; i++) {
+    ms[i] = 0.0;
+    launches[i] = 0;
+  }
+  auto add = [&](const std::vector<Rec>& recs) {
+    for (const Rec& r : recs) {
+      float t = 0.0f;
+      if (r.cat < ncat && cudaEventElapsedTime(&t, r.a, r.b) == cudaSuccess) {
+        ms[r.cat] += t;
+        launches[r.cat]++;
+      }
+    }
+  };
+  for (auto& kv : m->graph_cache) add(kv.second.recs);
+  add(m->eager_recs);
+  cudaGetLastError();  // events of graphs not yet replayed report "not ready"
+  return 0;
+}
+
+int64_t wasr_model_kernel_launches(WasrModel* m) { return m ? m->launches : -1; }
+
+int wasr_model_error(WasrModel* m) {
+  if (!m) return -1;
+  const int e = *reinterpret_cast<volatile int*>(m->err_host);
+  *m->err_host = 0;
+  return e;
+}
+
+int wasr_forward(WasrModel* m, const float* feats, const int32_t* t, int n_win, uint32_t* ids, float* logits,
+                 int flags) {
+  if (!m) return -1;
+  std::lock_guard<std::mutex> lk(m->mu);
+  DevGuard dg(m->dev);
+  return forward_impl(m, feats, t, n_win, ids, logits, flags);
+}
+
+int64_t wasr_fbank(const int16_t* pcm, int64_t n, float* feats, int64_t cap, float* sil) {
+  using namespace fb;
+  if (!pcm && n > 0) return -1;
+  const int64_t nfr = n >= WIN ? (n - WIN) / HOP + 1 : 0;
+  if (!feats) return nfr;
+  if (nfr > cap) return -1;
+  std::vector<double> raw(static_cast<size_t>(std::max<int64_t>(nfr, 1)) * DIM);
+  (void)tables();
+#pragma omp parallel for schedule(static)
+  for (int64_t k = 0; k < nfr; k++) frame(pcm + k * HOP, raw.data() + k * DIM);
+  double sum[DIM] = {0};
+  int64_t hn = 0;
+  for (int64_t k = 0; k < nfr; k++) {
+    const double* f = raw.data() + k * DIM;
+    if (hn == CMS_WIN) {
+      const double* o = raw.data() + (k - CMS_WIN) * DIM;
+      for (int i = 0; i < DIM; i++) sum[i] -= o[i];
+      hn--;
+    }
+    hn++;
+    for (int i = 0; i < DIM; i++) sum[i] += f[i];
+    const double nn = static_cast<double>(hn > 0 ? hn : 1);
+    for (int i = 0; i < DIM; i++) feats[k * DIM + i] = static_cast<float>(f[i] - sum[i] / nn);
+  }
+  if (sil) {
+    double s[DIM] = {0};
+    s[NCH] = std::log(1e-10);
+    const double nn = static_cast<double>(hn > 0 ? hn : 1);
+    for (int i = 0; i < DIM; i++) sil[i] = static_cast<float>(s[i] - sum[i] / nn);
+  }
+  return nfr;
+}
+
+int64_t wasr_ctc_collapse(const uint32_t* ids, int64_t n, uint32_t* out) {
+  if ((!ids || !out) && n > 0) return -1;
+  int64_t k = 0;
+  uint32_t prev = 0xFFFFFFFFu;
+  for (int64_t i = 0; i < n; i++) {
+    if (ids[i] != prev && ids[i] != 0) out[k++] = ids[i];
+    prev = ids[i];
+  }
+  return k;
+}
+
+// Batch transcription (src/stream.rs:58-70 push, 128-134 decode, 136-147 commit, 159-168
+// finish).  Every utterance keeps its own commit position; each round stacks one window per
+// unfinished utterance into a single wasr_forward.
+int wasr_transcribe(WasrModel* m, const float* feats, const int64_t* n_frames, const float* sil, int n_utt, int prev,
+                    int blk, int post, uint32_t* ids, int64_t* ids_off, int64_t ids_cap) {
+  if (!m || !n_frames || !sil || !ids || !ids_off || n_utt < 0 || (!feats && n_utt > 0)) return -1;
+  if (prev < 0 || blk <= 0 || post < 0) return -1;
+  std::lock_guard<std::mutex> lk(m->mu);
+  DevGuard dg(m->dev);
+  std::vector<int64_t> start(n_utt + 1, 0);
+  for (int u = 0; u < n_utt; u++) start[u + 1] = start[u] + std::max<int64_t>(0, n_frames[u]);
+  struct U {
+    int64_t s = 0;
+    bool done = false;
+    std::vector<uint32_t> out;
+  };
+  std::vector<U> st(n_utt);
+  // windows of the current round
+  struct Win {
+    int u;
+    int64_t a, end;  // frames [a, end) of utterance u, then `pad` silence frames
+    int pad;
+    int kind;        // 0 whole, 1 commit, 2 finish tail
+  };
+  for (;;) {
+    std::vector<Win> wins;
+    for (int u = 0; u < n_utt; u++) {
+      U& x = st[u];
+      if (x.done) continue;
+      const int64_t n = std::max<int64_t>(0, n_frames[u]);
+      if (n <= WASR_WHOLE_MAX) {  // finish(): whole utterance, no pad (commits are discarded)
+        wins.push_back({u, 0, n, 0, 0});
+      } else if (n >= x.s + blk + post) {
+        wins.push_back({u, x.s > prev ? x.s - prev : 0, x.s + blk + post, WASR_PAD, 1});
+      } else if (n > x.s) {
+        wins.push_back({u, x.s > prev ? x.s - prev : 0, n, WASR_PAD, 2});
+      } else {
+        x.done = true;
+      }
+    }
+    if (wins.empty()) break;
+    // assemble frames into pinned staging; a round made only of whole utterances laid out
+    // back to back in the caller's array is copied straight from it
+    std::vector<int32_t> tv(wins.size());
+    int64_t total = 0;
+    for (size_t i = 0; i < wins.size(); i++) {
+      tv[i] = static_cast<int32_t>(wins[i].end - wins[i].a + wins[i].pad);
+      total += tv[i];
+    }
+    bool contiguous = true;
+    for (size_t i = 0; i < wins.size() && contiguous; i++)
+      contiguous = wins[i].kind == 0 && (i == 0 ? start[wins[i].u] == 0 : start[wins[i].u] == start[wins[i - 1].u] +
+                                                                              (wins[i - 1].end - wins[i - 1].a));
+    const float* src = feats;
+    if (!contiguous) {
+      if (!hgrow(&m->h_feats, &m->h_feats_cap, static_cast<size_t>(total) * DIM)) return -5;
+      float* d = m->h_feats;
+      for (const Win& w : wins) {
+        const float* uf = feats + start[w.u] * DIM;
+        std::memcpy(d, uf + w.a * DIM, static_cast<size_t>(w.end - w.a) * DIM * sizeof(float));
+        d += (w.end - w.a) * DIM;
+        for (int p = 0; p < w.pad; p++, d += DIM) std::memcpy(d, sil + static_cast<int64_t>(w.u) * DIM, DIM * 4);
+      }
+      src = m->h_feats;
+    }
+    int64_t rows = 0;
+    for (int32_t tt : tv) rows += t1_of(tt);
+    if (!hgrow(&m->h_ids, &m->h_ids_cap, static_cast<size_t>(std::max<int64_t>(rows, 1)))) return -5;
+    TRY(forward_impl(m, src, tv.data(), static_cast<int>(wins.size()), m->h_ids, nullptr, 0));
+    int64_t r = 0;
+    for (size_t i = 0; i < wins.size(); i++) {
+      const Win& w = wins[i];
+      U& x = st[w.u];
+      const int64_t t1 = t1_of(tv[i]);
+      const uint32_t* o = m->h_ids + r;
+      r += t1;
+      if (w.kind == 0) {
+        x.out.assign(o, o + t1);
+        x.done = true;
+        continue;
+      }
+      const int64_t from = (x.s - w.a) / 5;
+      int64_t len = t1 > from ? t1 - from : 0;
+      if (w.kind == 2) {
+        x.out.insert(x.out.end(), o + from, o + from + len);
+        x.done = true;
+        continue;
+      }
+      // commit: keep blk/5 frames, cut at the last blank pair of the second half
+      len = std::min<int64_t>(len, blk / 5);
+      for (int64_t cpos = len - 1; cpos >= len / 2 && cpos >= 1; cpos--)
+        if (o[from + cpos] == 0 && o[from + cpos - 1] == 0) {
+          len = cpos;
+          break;
+        }
+      x.out.insert(x.out.end(), o + from, o + from + len);
+      x.s += len * 5;
+      if (len == 0) x.done = true;  // cannot advance (only reachable for blk < 10)
+    }
+  }
+  int64_t k = 0;
+  ids_off[0] = 0;
+  for (int u = 0; u < n_utt; u++) {
+    if (k + static_cast<int64_t>(st[u].out.size()) > ids_cap) return -20;
+    std::memcpy(ids + k, st[u].out.data(), st[u].out.size() * sizeof(uint32_t));
+    k += static_cast<int64_t>(st[u].out.size());
+    ids_off[u + 1] = k;
+  }
+  return 0;
+}
+
+}  // extern "C"
