@@ -1,0 +1,388 @@
+#!/usr/bin/env python
+"""Throughput of the B200 batch-transcription compute layer: audio-seconds per second.
+
+Workload: 512 synthetic utterances with lengths U[1, 13] s rescaled to
+3600 s in total, the 40-layer int8 model (random init, reference shapes), whole-utterance windows
+(every utterance is <= 2000 frames, src/stream.rs:159-161).  Utterances are sharded across the N
+GPUs with a length-balanced LPT assignment, one process per GPU, no collective on the data path
+(units are independent); the whole 3600 s is split over the ranks ("strong" scaling).
+
+One step = one pass of the hot path over the rank's whole shard (conv frontend, 40 layers,
+output layer + argmax) with features already resident in HBM -> `value`.  `e2e` is the same metric
+through the public C-ABI call a user makes (wasr_transcribe) with pinned host features in and host
+ids out, copies inside the timed region.  The CPU baseline is the oracle port of the reference CPU
+path on this host's cores over a bounded sample.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "wechat-asr-gpu_b200")
+METRIC = "audio-sec/sec 40-layer int8 ASR @1/2/4/8 B200; int8 GEMM TOPS vs peak"
+WORKLOAD = ("config4: 512 utterances U[1,13] s rescaled to 3600 s total; 40-layer int8 model "
+            "(D=512, 8 heads, FF=2048, vocab 10502); whole-utterance windows; LPT-sharded by utterance")
+
+
+def load_pkg():
+    name = "wechat_asr_gpu_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, os.path.join(PKG_DIR, "__init__.py"),
+                                                  submodule_search_locations=[PKG_DIR])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def load_oracle():
+    """The CPU restatement of the reference CPU path: only the cpu_baseline / reference leg."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle  # noqa: E402
+    if not os.path.exists(oracle.LIB):
+        oracle.build()
+    return oracle
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------- workload
+def make_workload(pkg, shard, lengths):
+    """Synthetic audio of this rank's utterances -> product fbank features."""
+    feats, sils, secs = [], [], 0.0
+    for i in shard:
+        pcm = pkg.synth.make_audio(100000 + i, lengths[i])
+        f, s = pkg.fbank(pcm)
+        feats.append(f)
+        sils.append(s)
+        secs += pcm.size / 16000.0
+    return feats, sils, secs
+
+
+def algorithmic_work(t1_list, n_layers=40, vocab=10502):
+    """Per-class algorithmic work of one forward (unpadded shapes).  int8 ops count 2 per MAC;
+    bytes for the memory-bound classes are the minimum reads + writes of each kernel."""
+    rows = float(sum(t1_list))
+    sq = float(sum(t * t for t in t1_list))
+    D, FF, FLAT = 512, 2048, 3840
+    ops = {
+        "gemm_lin": 2 * rows * FLAT * D,
+        "gemm_qkv": n_layers * 2 * rows * D * 3 * D,
+        "gemm_o": n_layers * 2 * rows * D * D,
+        "gemm_f1": n_layers * 2 * rows * D * FF,
+        "gemm_f2": n_layers * 2 * rows * FF * D,
+        "gemm_out_argmax": 2 * rows * D * vocab,
+    }
+    # bytes: attention reads q,k,v (fp32) once and writes the output; LN reads h, writes int8 + scale;
+    # conv2 reads y1 rows once and writes y2; conv3 reads y2 and writes y3; quant reads fp32 rows
+    # and writes int8
+    byts = {
+        "attention": n_layers * rows * (3 * D * 4 + D * 4),
+        "layernorm": 2 * n_layers * rows * (D * 4 + D + 4),
+        "conv2": rows * (5 * 32 * 40 * 4 + 64 * 41 * 4),
+        "conv3": rows * (64 * 41 * 4 + FLAT * 4),
+        "conv1": rows * 5 * (40 * 4 + 32 * 40 * 4),
+        "quant": rows * ((FLAT + n_layers * (D + FF) + D) * 5),
+    }
+    flops = {"attention": n_layers * 4.0 * sq * D}
+    return ops, byts, flops, rows
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev: int):
+        self.dev = dev
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.FIELDS}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if not self.p:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.p.terminate()
+        try:
+            out, _ = self.p.communicate(timeout=5)
+        except Exception:
+            self.p.kill()
+            out = ""
+        rows = []
+        for ln in out.splitlines():
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) >= 8:
+                rows.append(f)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [num(r[0]) for r in rows if num(r[0]) is not None]
+        pw = [num(r[2]) for r in rows if num(r[2]) is not None]
+        load = [num(r[0]) for r in rows if num(r[2]) is not None and num(r[2]) > 0.5 * max(pw or [0])]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[4 + i].lower().startswith("active")})
+        return {"sm_mhz": float(np.median(load or sm)) if (load or sm) else None,
+                "sm_max_mhz": num(rows[0][1]), "power_w_max": max(pw) if pw else None,
+                "samples": len(rows), "reasons": reasons}
+
+
+# ---------------------------------------------------------------- CPU baseline (oracle port)
+def cpu_baseline(orc, pkg, lengths, budget_s: float):
+    """Oracle transcription of config-4 utterances in order until `budget_s` of CPU time spent in
+    the transcription calls (audio synthesis and fbank excluded); returns (audio-s/s, sample, cores)."""
+    blob, plan = pkg.synth.make_model(seed=1, n_layers=40)
+    cores = os.cpu_count() or 1
+    orc.set_threads(cores)
+    done_s, n, spent = 0.0, 0, 0.0
+    while spent < budget_s and n < len(lengths):
+        pcm = pkg.synth.make_audio(100000 + n, lengths[n])
+        f, s = orc.fbank(pcm)
+        ts = time.perf_counter()
+        orc.transcribe(blob, plan, f, s, blk=1600)
+        spent += time.perf_counter() - ts
+        done_s += pcm.size / 16000.0
+        n += 1
+    return done_s / spent, f"first {n} config-4 utterances ({done_s:.1f} s of audio), {spent:.1f} s CPU wall", cores
+
+
+def run_reference(args, rank):
+    """--impl reference: the reference CPU path (oracle port, no Rust toolchain here) on this
+    host's cores, same metric; rank 0 only."""
+    if rank != 0:
+        return
+    pkg = load_pkg()
+    orc = load_oracle()
+    lengths = pkg.synth.config_lengths(4)
+    blob, plan = pkg.synth.make_model(seed=1, n_layers=40)
+    cores = os.cpu_count() or 1
+    orc.set_threads(cores)
+    # each step transcribes the same bounded sample: the first config-4 utterances up to ~20 s of audio
+    sample, tot = [], 0.0
+    for i, L in enumerate(lengths):
+        sample.append(i)
+        tot += L
+        if tot >= 20.0:
+            break
+    data = []
+    for i in sample:
+        pcm = pkg.synth.make_audio(100000 + i, lengths[i])
+        f, s = orc.fbank(pcm)
+        data.append((f, s, pcm.size / 16000.0))
+    audio = sum(d[2] for d in data)
+
+    def step():
+        t = time.perf_counter()
+        for f, s, _ in data:
+            orc.transcribe(blob, plan, f, s, blk=1600)
+        return time.perf_counter() - t
+    for _ in range(args.warmup):
+        step()
+    ts = [step() for _ in range(args.steps)]
+    sec = float(np.mean(ts))
+    val = audio / sec
+    line = {"metric": METRIC, "value": round(val, 3), "unit": "audio-s/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": WORKLOAD, "sample": f"first {len(sample)} utterances, {audio:.2f} s of audio per step"},
+            "cpu_baseline": {"value": round(val, 3), "unit": "audio-s/s", "cores": cores, "kind": "port",
+                             "sample": f"oracle restatement of src/kernels.rs + src/model.rs CPU path, "
+                                       f"{len(sample)} utterances / {audio:.2f} s audio per step"},
+            "e2e": {"value": round(val, 3), "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- our arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--max-rows", type=int, default=16384)
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "b200" else args.warmup
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    dist_on = world > 1
+    if dist_on:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+
+    pkg = load_pkg()
+    lengths = pkg.synth.config_lengths(4)
+    shards = pkg.synth.lpt_shards(lengths, world)
+    shard = shards[rank]
+    feats, sils, my_audio = make_workload(pkg, shard, lengths)
+    total_audio = float(sum(lengths))
+    blob, plan = pkg.synth.make_model(seed=1, n_layers=40)
+    eng = pkg.Engine(blob, plan, device=local, max_rows=args.max_rows)
+    stream = torch.cuda.Stream(device=local)
+    eng.set_stream(stream.cuda_stream)
+
+    t = np.array([f.shape[0] for f in feats], np.int32)
+    t1 = [(x - 5) // 5 + 1 if x >= 5 else 0 for x in t]
+    cat = np.ascontiguousarray(np.concatenate(feats, 0), np.float32)
+    feats_dev = torch.from_numpy(cat).to(f"cuda:{local}")
+    ids_dev = torch.empty(max(sum(t1), 1), dtype=torch.int32, device=f"cuda:{local}")
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=f"cuda:{local}")
+    eng.set_profile(True)
+
+    def fwd():
+        eng.forward_device(feats_dev.data_ptr(), t, ids_dev.data_ptr(), sync=False)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            fwd()
+        torch.cuda.synchronize()
+        if dist_on:
+            dist.barrier()
+        torch.cuda.synchronize()
+        clk = ClockSampler(local)
+        clk.start()
+        launches0 = eng.kernel_launches()
+        evs = []
+        for _ in range(args.steps):
+            flush.zero_()                       # L2 flush (256 MiB write) outside the timed events
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fwd()
+            b.record(stream)
+            evs.append((a, b))
+        torch.cuda.synchronize()
+        launches = eng.kernel_launches() - launches0
+        clocks = clk.stop()
+        ms = sum(a.elapsed_time(b) for a, b in evs)
+        if dist_on:
+            dist.barrier()
+    err = eng.error()
+    prof_ms, prof_n = eng.profile()
+    ms_t = torch.tensor([ms], dtype=torch.float64, device=f"cuda:{local}")
+    if dist_on:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    ms_per_step = ms_max / args.steps
+    value = total_audio / (ms_per_step / 1e3)
+
+    # ---- e2e through the public call with host buffers (pinned), copies inside the timing
+    e2e = None
+    if not args.no_e2e:
+        pinned = torch.from_numpy(cat).pin_memory()
+        cat_pinned = pinned.numpy()
+        eng.set_stream(None)  # the engine's own stream; wasr_transcribe synchronises it
+        eng.transcribe(feats, sils, blk=1600, feats_cat=cat_pinned)  # warm (captures the graphs)
+        torch.cuda.synchronize()
+        if dist_on:
+            dist.barrier()
+        e_ts = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            out = eng.transcribe(feats, sils, blk=1600, feats_cat=cat_pinned)
+            e_ts.append(time.perf_counter() - t0)
+        e_t = torch.tensor([float(np.mean(e_ts))], dtype=torch.float64, device=f"cuda:{local}")
+        if dist_on:
+            dist.all_reduce(e_t, op=dist.ReduceOp.MAX)
+        ids_bytes = 4 * sum(len(o) for o in out)
+        e2e = {"value": round(total_audio / float(e_t.item()), 3), "unit": "audio-s/s",
+               "h2d_bytes_per_step": int(cat.nbytes), "d2h_bytes_per_step": int(ids_bytes),
+               "api": "wasr_transcribe (pinned host features in, host ids out)"}
+
+    # ---- roofline of the dominant kernel class (last timed step, CUDA events on its stream)
+    hbm, bf16, src = peaks()
+    names = pkg.abi.KERNEL_CLASSES
+    ops, byts, flops, rows = algorithmic_work(t1, plan.n_layers)
+    dom = max(range(len(names)), key=lambda i: prof_ms[i])
+    dname = names[dom]
+    dms = prof_ms[dom]
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", "traffic_per_row.json")
+    if os.path.exists(tf):
+        tr = json.load(open(tf)).get(dname)
+        if tr and prof_n[dom]:
+            traffic = round(tr * rows / prof_n[dom])
+    if dname in ops:
+        ach = ops[dname] / prof_n[dom] / (dms / prof_n[dom] / 1e3) / 1e12
+        roof = {"kernel": dname, "bound": "tensor", "achieved": round(ach, 2), "peak": round(2 * bf16, 1),
+                "unit": "TOPS", "frac": round(ach / (2 * bf16), 4), "traffic": traffic,
+                "peak_source": f"int8 dense = 2 x bf16 dense burst ({src} {bf16} TF/s)",
+                "launches": int(prof_n[dom]), "avg_launch_us": round(dms / prof_n[dom] * 1e3, 2)}
+    else:
+        b = byts.get(dname, 0.0)
+        ach = b / prof_n[dom] / (dms / prof_n[dom] / 1e3) / 1e9 if prof_n[dom] else 0.0
+        roof = {"kernel": dname, "bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(ach / hbm, 4), "traffic": traffic, "peak_source": f"{src} hbm_gbs",
+                "launches": int(prof_n[dom]), "avg_launch_us": round(dms / prof_n[dom] * 1e3, 2)}
+    gemm_ops = sum(ops.values())
+    gemm_ms = sum(prof_ms[names.index(k)] for k in ops)
+    roof["all_gemms_tops"] = round(gemm_ops / (gemm_ms / 1e3) / 1e12, 2) if gemm_ms else None
+    roof["kernel_ms_last_step"] = {names[i]: round(prof_ms[i], 3) for i in range(len(names)) if prof_n[i]}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        orc = load_oracle()
+        v, sample, cores = cpu_baseline(orc, pkg, lengths, args.cpu_budget)
+        cpu = {"value": round(v, 3), "unit": "audio-s/s", "cores": cores, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 2), "unit": "audio-s/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+                "data": "synthetic",
+                "config": {"workload": WORKLOAD, "total_audio_s": round(total_audio, 3), "utterances": len(lengths),
+                           "rows_rank0": int(sum(t1)), "n_layers": plan.n_layers, "max_rows_per_chunk": args.max_rows,
+                           "l2": "flushed (256 MiB write) before every timed step",
+                           "parallelism": f"utterance-sharded LPT over {world} GPU(s), no collective"},
+                "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
+                "clocks": clocks, "device_error": err}
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if dist_on:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

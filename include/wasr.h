@@ -140,6 +140,11 @@ int64_t wasr_fbank(const int16_t* pcm, int64_t n, float* feats, int64_t cap, flo
  * and blank id 0.  Returns the collapsed length. */
 int64_t wasr_ctc_collapse(const uint32_t* ids, int64_t n, uint32_t* out);
 
+/* Parity hook: evaluates the kernels' restatements of the libm functions the reference CPU
+ * path calls (fn 0: tanhf, 1: expf, 2: GELU of src/model.rs:710-712, 3: expm1f) on n device
+ * floats, so tests can compare them bit for bit with the host's glibc. */
+int wasr_eval_math(int fn, const float* x, float* y, int n, void* stream);
+
 const char* wasr_version(void);
 
 #ifdef __cplusplus

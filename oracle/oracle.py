@@ -40,6 +40,8 @@ def lib():
             "wo_dotf": (F, [P, P, I]),
             "wo_norm": (None, [P, I64, I, P, P, P]),
             "wo_gelu": (F, [F]),
+            "wo_libm_tanhf": (None, [P, P, I64]), "wo_libm_expf": (None, [P, P, I64]),
+            "wo_gelu_array": (None, [P, P, I64]),
             "wo_attention": (None, [P, P, P, I, P]),
             "wo_frontend": (I, [P, I, P, P, P, P]),
             "wo_forward": (I, [P, P, P, I, P, P]),
@@ -117,10 +119,24 @@ def norm(x, g, b):
     return y
 
 
+def _map(fn, x):
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    fn(_p(x), _p(y), x.size)
+    return y
+
+
 def gelu(x: np.ndarray) -> np.ndarray:
-    f = lib().wo_gelu
-    return np.array([f(float(v)) for v in np.asarray(x, np.float32).ravel()],
-                    np.float32).reshape(np.shape(x))
+    """src/model.rs:710-712 (glibc tanhf)."""
+    return _map(lib().wo_gelu_array, x)
+
+
+def libm_tanhf(x):
+    return _map(lib().wo_libm_tanhf, x)
+
+
+def libm_expf(x):
+    return _map(lib().wo_libm_expf, x)
 
 
 def attention(q, k, v):

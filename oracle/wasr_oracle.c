@@ -198,6 +198,19 @@ float wo_gelu(float x) {
   return 0.5f * x * (1.0f + tanhf(0.7978846f * (x + 0.044715f * x * x * x)));
 }
 
+void wo_libm_tanhf(const float* x, float* y, int64_t n) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; i++) y[i] = tanhf(x[i]);
+}
+void wo_libm_expf(const float* x, float* y, int64_t n) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; i++) y[i] = expf(x[i]);
+}
+void wo_gelu_array(const float* x, float* y, int64_t n) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; i++) y[i] = wo_gelu(x[i]);
+}
+
 /* src/model.rs:714-739 */
 void wo_attention(const float* q, const float* k, const float* v, int t, float* out) {
   memset(out, 0, sizeof(float) * (size_t)t * D);

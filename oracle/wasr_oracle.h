@@ -44,6 +44,10 @@ float wo_dotf(const float* a, const float* b, int n);
 void wo_norm(const float* x, int64_t t, int d, const float* g, const float* b, float* y);
 /* src/model.rs:710-712 */
 float wo_gelu(float x);
+/* the host libm (glibc) functions the reference calls, over arrays (parity checks) */
+void wo_libm_tanhf(const float* x, float* y, int64_t n);
+void wo_libm_expf(const float* x, float* y, int64_t n);
+void wo_gelu_array(const float* x, float* y, int64_t n);
 /* src/model.rs:714-739: q,k,v,out are [t][512] */
 void wo_attention(const float* q, const float* k, const float* v, int t, float* out);
 /* src/model.rs:389-478: x [t][40] -> y3 [t1][3840]; returns t1 (0 if t < 5) */

@@ -65,6 +65,10 @@ def test_full_model_window_vs_oracle(pkg, orc, gpu_lib, model40):
         (ids,), (lo,) = eng.forward([x], want_logits=True)
         assert rel_err(lo, lo_ref) <= 1e-3, rel_err(lo, lo_ref)
         check_ids(ids, ids_ref, lo_ref)
+        # every op follows the CPU operation order and glibc's tanhf/expf algorithms, so the
+        # whole 40-layer forward is expected to be bit-identical, not just within tolerance
+        np.testing.assert_array_equal(lo, lo_ref)
+        np.testing.assert_array_equal(ids, ids_ref)
         (ids_fused,) = eng.forward([x])             # fused GEMM+argmax path
         np.testing.assert_array_equal(ids_fused, ids)
         assert eng.error() == 0
@@ -98,7 +102,7 @@ def test_batched_ragged_equals_one_by_one(pkg, gpu_lib):
     """Stacking windows of different lengths changes nothing per window (row-independent ops,
     per-segment conv and attention); also t < 5 windows give no frames."""
     blob, plan = pkg.synth.make_model(seed=4, n_layers=3)
-    feats, _ = pkg.fbank(pkg.synth.make_audio(8, 30.0))
+    feats, _ = pkg.fbank(pkg.synth.make_audio(8, 60.0))
     lens = [1950, 5, 4, 6, 33, 1234, 9, 400, 2000, 1]
     wins, p = [], 0
     for n in lens:
@@ -132,9 +136,7 @@ def test_transcribe_schedule_vs_oracle(pkg, orc, gpu_lib):
         got = eng.transcribe([f for f, _ in fs], [s for _, s in fs], blk=1600)
         for (f, s), g in zip(fs, got):
             ref, nf = orc.transcribe(blob, plan, f, s, blk=1600)
-            assert abs(len(g) - len(ref)) <= 2
-            m = min(len(g), len(ref))
-            assert m == 0 or np.mean(g[:m] == ref[:m]) >= 0.999
+            np.testing.assert_array_equal(g, ref)           # per-frame ids, before CTC
             np.testing.assert_array_equal(pkg.ctc_collapse(g), orc.ctc(ref))
         got400 = eng.transcribe([fs[0][0]], [fs[0][1]], blk=400)
         ref400, _ = orc.transcribe(blob, plan, fs[0][0], fs[0][1], blk=400)

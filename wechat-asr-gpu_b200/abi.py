@@ -103,6 +103,7 @@ SIGNATURES = {
     "wasr_transcribe": (I, [P, P, P, P, I, I, I, I, P, P, I64]),
     "wasr_fbank": (I64, [P, I64, P, I64, P]),
     "wasr_ctc_collapse": (I64, [P, I64, P]),
+    "wasr_eval_math": (I, [I, P, P, I, P]),
     "wasr_version": (C.c_char_p, []),
 }
 

@@ -159,12 +159,153 @@ __device__ __forceinline__ int8_t quant_one(float v, float inv) {
   q = fminf(127.0f, fmaxf(-127.0f, q));
   return static_cast<int8_t>(q);
 }
+// ---------------------------------------------------------------- libm restatements
+// The reference CPU path calls the platform libm: Rust's f32::tanh / f32::exp are glibc's
+// tanhf / expf (glibc 2.39 on this image).  CUDA's tanhf / expf differ from those in the last
+// place for a few percent of inputs, and over 40 layers such one-ulp differences flip int8
+// roundings that the random network then amplifies.  So the kernels evaluate the same
+// published algorithms glibc uses, with every operation explicitly rounded:
+//   tanhf: the fdlibm algorithm (tanh via expm1: 1 - 2/(expm1(2|x|)+2) for |x| >= 1,
+//          -t/(t+2) with t = expm1(-2|x|) below, +-1 beyond 22);
+//   expm1f: fdlibm's argument reduction by ln2 (hi/lo split) and its rational correction
+//          with the five-term polynomial in x^2/2;
+//   expf: the table-driven double-precision method (x*32/ln2 = k + r, 2^(k/32) from a 32-entry
+//          table of 2^(i/32), cubic polynomial in r).
+// Exhaustive comparison against glibc on every float input: tanhf identical for all
+// 4,278,190,082 non-NaN inputs; expf identical for all inputs except two, which are special-
+// cased below with glibc's values.
+__device__ __forceinline__ float f_from_bits(uint32_t u) { return __uint_as_float(u); }
+
+__device__ __forceinline__ float expm1f_ref(float x) {
+  const float ln2_hi = 6.9313812256e-01f, ln2_lo = 9.0580006145e-06f, invln2 = 1.4426950216e+00f;
+  const float Q1 = -3.3333335072e-02f, Q2 = 1.5873016091e-03f, Q3 = -7.9365076090e-05f, Q4 = 4.0082177293e-06f,
+              Q5 = -2.0109921195e-07f;
+  uint32_t hx = __float_as_uint(x);
+  const uint32_t xsb = hx & 0x80000000u;
+  hx &= 0x7fffffffu;
+  if (hx >= 0x4195b844u && xsb) return -1.0f;  // x < -27 ln2 (callers never pass large positive x)
+  float hi, lo, c = 0.0f, t;
+  int k;
+  if (hx > 0x3eb17218u) {
+    if (hx < 0x3F851592u) {
+      if (xsb == 0) { hi = __fsub_rn(x, ln2_hi); lo = ln2_lo; k = 1; }
+      else { hi = __fadd_rn(x, ln2_hi); lo = -ln2_lo; k = -1; }
+    } else {
+      k = static_cast<int>(__fadd_rn(__fmul_rn(invln2, x), xsb == 0 ? 0.5f : -0.5f));
+      t = static_cast<float>(k);
+      hi = __fsub_rn(x, __fmul_rn(t, ln2_hi));
+      lo = __fmul_rn(t, ln2_lo);
+    }
+    x = __fsub_rn(hi, lo);
+    c = __fsub_rn(__fsub_rn(hi, x), lo);
+  } else if (hx < 0x33000000u) {
+    return x;
+  } else {
+    k = 0;
+  }
+  const float hfx = __fmul_rn(0.5f, x);
+  const float hxs = __fmul_rn(x, hfx);
+  float r1 = __fmul_rn(hxs, Q5);
+  r1 = __fmul_rn(hxs, __fadd_rn(Q4, r1));
+  r1 = __fmul_rn(hxs, __fadd_rn(Q3, r1));
+  r1 = __fmul_rn(hxs, __fadd_rn(Q2, r1));
+  r1 = __fadd_rn(1.0f, __fmul_rn(hxs, __fadd_rn(Q1, r1)));
+  t = __fsub_rn(3.0f, __fmul_rn(r1, hfx));
+  float e = __fmul_rn(hxs, __fdiv_rn(__fsub_rn(r1, t), __fsub_rn(6.0f, __fmul_rn(x, t))));
+  if (k == 0) return __fsub_rn(x, __fsub_rn(__fmul_rn(x, e), hxs));
+  e = __fsub_rn(__fmul_rn(x, __fsub_rn(e, c)), c);
+  e = __fsub_rn(e, hxs);
+  if (k == -1) return __fsub_rn(__fmul_rn(0.5f, __fsub_rn(x, e)), 0.5f);
+  if (k == 1) {
+    if (x < -0.25f) return __fmul_rn(-2.0f, __fsub_rn(e, __fadd_rn(x, 0.5f)));
+    return __fadd_rn(1.0f, __fmul_rn(2.0f, __fsub_rn(x, e)));
+  }
+  float y;
+  if (k <= -2 || k > 56) {
+    y = __fsub_rn(1.0f, __fsub_rn(e, x));
+    y = f_from_bits(__float_as_uint(y) + (static_cast<uint32_t>(k) << 23));
+    return __fsub_rn(y, 1.0f);
+  }
+  if (k < 23) {
+    t = f_from_bits(0x3f800000u - (0x1000000u >> k));
+    y = __fsub_rn(t, __fsub_rn(e, x));
+  } else {
+    t = f_from_bits(static_cast<uint32_t>(0x7f - k) << 23);
+    y = __fsub_rn(x, __fadd_rn(e, t));
+    y = __fadd_rn(y, 1.0f);
+  }
+  return f_from_bits(__float_as_uint(y) + (static_cast<uint32_t>(k) << 23));
+}
+
+__device__ __forceinline__ float tanhf_ref(float x) {
+  const uint32_t jx = __float_as_uint(x), ix = jx & 0x7fffffffu;
+  if (ix >= 0x7f800000u) return (jx >> 31) ? __fsub_rn(__fdiv_rn(1.0f, x), 1.0f) : __fadd_rn(__fdiv_rn(1.0f, x), 1.0f);
+  float z;
+  if (ix < 0x41b00000u) {  // |x| < 22
+    if (ix == 0) return x;
+    if (ix < 0x24000000u) return __fmul_rn(x, __fadd_rn(1.0f, x));
+    const float ax = fabsf(x);
+    if (ix >= 0x3f800000u) {
+      const float t = expm1f_ref(__fmul_rn(2.0f, ax));
+      z = __fsub_rn(1.0f, __fdiv_rn(2.0f, __fadd_rn(t, 2.0f)));
+    } else {
+      const float t = expm1f_ref(__fmul_rn(-2.0f, ax));
+      z = __fdiv_rn(-t, __fadd_rn(t, 2.0f));
+    }
+  } else {
+    z = __fsub_rn(1.0f, 1.0e-30f);
+  }
+  return (jx >> 31) ? -z : z;
+}
+
+__constant__ static const unsigned long long kExp2Tab[32] = {
+    0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
+    0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
+    0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
+    0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
+    0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
+    0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
+    0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
+    0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull};
+
+// tab[i] above = bits(2^(i/32)) - (i << 47): adding k << 47 to tab[k % 32] yields 2^(k/32).
+__device__ __forceinline__ float expf_ref(float x) {
+  const uint32_t ux = __float_as_uint(x);
+  if (ux == 0x4202422fu) return f_from_bits(0x56fc9f1cu);  // the two inputs where glibc's result
+  if (ux == 0xc27c65d9u) return f_from_bits(0x11fa2993u);  // is the other float neighbour
+  const uint32_t abstop = (ux >> 20) & 0x7ffu;
+  if (abstop >= (0x42b00000u >> 20)) {  // |x| >= 88 or non-finite
+    if (ux == 0xff800000u) return 0.0f;
+    if (abstop >= (0x7f800000u >> 20)) return __fadd_rn(x, x);
+    if (x > 88.72283172607421875f) return __int_as_float(0x7f800000);
+    if (x < -103.97207641601562f) return 0.0f;
+  }
+  const double inv_ln2_n = 0x1.71547652b82fep+0 * 32.0;
+  const double shift = 0x1.8p+52;
+  const double c0 = 0x1.c6af84b912394p-5 / 32768.0;  // cubic coefficients of 2^(r/32), r in [-1/2, 1/2]
+  const double c1 = 0x1.ebfce50fac4f3p-3 / 1024.0;
+  const double c2 = 0x1.62e42ff0c52d6p-1 / 32.0;
+  const double z = __dmul_rn(inv_ln2_n, static_cast<double>(x));
+  double kd = __dadd_rn(z, shift);
+  const unsigned long long ki = static_cast<unsigned long long>(__double_as_longlong(kd));
+  kd = __dsub_rn(kd, shift);
+  const double r = __dsub_rn(z, kd);
+  const unsigned long long t = kExp2Tab[ki & 31] + (ki << 47);
+  const double s = __longlong_as_double(static_cast<long long>(t));
+  const double zz = __dadd_rn(__dmul_rn(c0, r), c1);
+  const double r2 = __dmul_rn(r, r);
+  double y = __dadd_rn(__dmul_rn(c2, r), 1.0);
+  y = __dadd_rn(__dmul_rn(zz, r2), y);
+  y = __dmul_rn(y, s);
+  return __double2float_rn(y);
+}
+
 // GELU of src/model.rs:710-712, evaluated left to right like rustc:
 //   ((0.5*x) * (1 + tanh(0.7978846 * (x + ((0.044715*x)*x)*x))))
 __device__ __forceinline__ float gelu_ref(float x) {
   float c = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x);
   float u = __fmul_rn(0.7978846f, __fadd_rn(x, c));
-  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(u)));
+  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf_ref(u)));
 }
 // Epilogue of src/kernels.rs:53: (acc as f32 * xs[i]) * ws + bias (bias 0.0 when absent).
 __device__ __forceinline__ float dequant(int32_t acc, float xs, float ws, float bias) {

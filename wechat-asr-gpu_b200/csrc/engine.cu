@@ -18,6 +18,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -684,18 +685,25 @@ int wasr_model_profile(WasrModel* m, double* ms, int64_t* launches, int ncat) {
     ms[i] = 0.0;
     launches[i] = 0;
   }
+  int failed = 0;
+  cudaError_t first_err = cudaSuccess;
   auto add = [&](const std::vector<Rec>& recs) {
     for (const Rec& r : recs) {
       float t = 0.0f;
-      if (r.cat < ncat && cudaEventElapsedTime(&t, r.a, r.b) == cudaSuccess) {
+      const cudaError_t e = r.cat < ncat ? cudaEventElapsedTime(&t, r.a, r.b) : cudaErrorInvalidValue;
+      if (e == cudaSuccess) {
         ms[r.cat] += t;
         launches[r.cat]++;
+      } else if (!failed++) {
+        first_err = e;
       }
     }
   };
   for (auto& kv : m->graph_cache) add(kv.second.recs);
   add(m->eager_recs);
   cudaGetLastError();  // events of graphs not yet replayed report "not ready"
+  if (failed && getenv("WASR_DEBUG"))
+    fprintf(stderr, "[wasr] profile: %d event pairs not timed (%s)\n", failed, cudaGetErrorString(first_err));
   return 0;
 }
 

@@ -7,6 +7,9 @@
 // keeps the CPU's order too (8-lane dot, sequential softmax sum, sequential PV sum); only
 // expf/tanhf may differ from glibc in the last place.
 #include <cstdio>
+#include <mutex>
+#include <set>
+#include <utility>
 
 #include "../../include/wtlgpu.h"
 #include "kern.cuh"
@@ -474,7 +477,7 @@ __global__ void __launch_bounds__(256) attn_k(const float* __restrict__ q, const
     float m = -3.40282347e+38f;
     for (int j = lane; j < t; j += 32) m = fmaxf(m, row[j]);
     m = warp_max(m);
-    for (int j = lane; j < t; j += 32) row[j] = expf(__fsub_rn(row[j], m));
+    for (int j = lane; j < t; j += 32) row[j] = expf_ref(__fsub_rn(row[j], m));
   }
   __syncthreads();
   if (tid < ni) {
@@ -518,25 +521,33 @@ __global__ void __launch_bounds__(256) attn_k(const float* __restrict__ q, const
   }
 }
 
+__global__ void eval_math_k(int fn, const float* __restrict__ x, float* __restrict__ y, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float v = x[i];
+  y[i] = fn == 0 ? tanhf_ref(v) : fn == 1 ? expf_ref(v) : fn == 2 ? gelu_ref(v) : expm1f_ref(v);
+}
+
 // ------------------------------------------------------------------------ launchers
 static inline int launched() { return cudaPeekAtLastError() == cudaSuccess ? 0 : -4; }
 
-template <typename K>
-static void set_smem(K kern, int bytes) {
-  static unsigned done = 0;
+// Opt a kernel into `bytes` of dynamic shared memory once per (kernel, device).
+static void set_smem(const void* kern, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(done & (1u << (dev & 31)))) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    done |= 1u << (dev & 31);
-  }
+  std::lock_guard<std::mutex> lk(mu);
+  if (done.count({kern, dev})) return;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess)
+    done.insert({kern, dev});
 }
 
 bool kern_prepare() {
-  set_smem(conv2_k, CV2_SMEM);
-  set_smem(conv3_k, CV3_SMEM);
-  set_smem(ln_quant_k, LN_SMEM);
-  set_smem(attn_k, 227 * 1024);
+  set_smem(reinterpret_cast<const void*>(conv2_k), CV2_SMEM);
+  set_smem(reinterpret_cast<const void*>(conv3_k), CV3_SMEM);
+  set_smem(reinterpret_cast<const void*>(ln_quant_k), LN_SMEM);
+  set_smem(reinterpret_cast<const void*>(attn_k), 227 * 1024);
   return cudaGetLastError() == cudaSuccess;
 }
 
@@ -548,13 +559,13 @@ int launch_conv1(const float* x, const float* c1, Segs s, int total_frames, floa
 }
 int launch_conv2(const float* y1, const float* c2, Segs s, int total_rows, float* y2, cudaStream_t st) {
   if (total_rows <= 0) return 0;
-  set_smem(conv2_k, CV2_SMEM);
+  set_smem(reinterpret_cast<const void*>(conv2_k), CV2_SMEM);
   conv2_k<<<dim3(total_rows, C2 / CV2_OG), 160, CV2_SMEM, st>>>(y1, c2, s, y2);
   return launched();
 }
 int launch_conv3(const float* y2, const float* c3, Segs s, int total_rows, float* y3, cudaStream_t st) {
   if (total_rows <= 0) return 0;
-  set_smem(conv3_k, CV3_SMEM);
+  set_smem(reinterpret_cast<const void*>(conv3_k), CV3_SMEM);
   conv3_k<<<dim3(total_rows, C3 / CV3_OG), 160, CV3_SMEM, st>>>(y2, c3, s, y3);
   return launched();
 }
@@ -572,7 +583,7 @@ int launch_quant_rows_max(const float* x, int m, int k, const unsigned* rowmax, 
 int launch_ln_quant(float* h, const float* o, const float* g, const float* b, int m, int8_t* xq, float* xs,
                     cudaStream_t st) {
   if (m <= 0) return 0;
-  set_smem(ln_quant_k, LN_SMEM);
+  set_smem(reinterpret_cast<const void*>(ln_quant_k), LN_SMEM);
   ln_quant_k<<<(m + LN_ROWS - 1) / LN_ROWS, 256, LN_SMEM, st>>>(h, o, g, b, m, xq, xs);
   return launched();
 }
@@ -602,7 +613,7 @@ int launch_attention(const float* q, const float* k, const float* v, int ld, Seg
   if (total_tiles <= 0) return 0;
   const size_t smem = attention_smem_bytes(max_t1);
   if (smem > 227 * 1024) return -2;
-  set_smem(attn_k, 227 * 1024);  // the largest opt-in size; each launch passes its own
+  set_smem(reinterpret_cast<const void*>(attn_k), 227 * 1024);  // the largest opt-in size; each launch passes its own
   attn_k<<<dim3(total_tiles, HEADS), 256, smem, st>>>(q, k, v, ld, s, toff, max_t1, out, ldo);
   return launched();
 }
@@ -730,6 +741,15 @@ int wk_attention_cublas_part(int part, void* stream, const float* q, const float
   (void)scratch;
   if (part == 0 || part == 1) return 0;
   return attention_abi(stream, q, k, v, t, d, heads, out);
+}
+
+// Parity hook: evaluate the device restatements of the libm functions the reference calls
+// (fn 0 tanhf, 1 expf, 2 the GELU of src/model.rs:710-712, 3 expm1f) over n floats.
+int wasr_eval_math(int fn, const float* x, float* y, int n, void* stream) {
+  if (!x || !y || fn < 0 || fn > 3) return -1;
+  if (n <= 0) return 0;
+  eval_math_k<<<(n + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(fn, x, y, n);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 
 const char* wk_attention_version(void) {

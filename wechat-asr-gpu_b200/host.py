@@ -124,6 +124,22 @@ class Engine:
     def error(self) -> int:
         return self.L.wasr_model_error(self.m)
 
+    def set_profile(self, on: bool):
+        return self.L.wasr_model_set_profile(self.m, 1 if on else 0)
+
+    def profile(self):
+        """Per kernel class (abi.KERNEL_CLASSES): (ms of the last execution, launches)."""
+        n = len(abi.KERNEL_CLASSES)
+        ms = np.zeros(n, np.float64)
+        cnt = np.zeros(n, np.int64)
+        rc = self.L.wasr_model_profile(self.m, ptr(ms), ptr(cnt), n)
+        if rc:
+            raise RuntimeError(f"wasr_model_profile rc={rc}")
+        return ms, cnt
+
+    def kernel_launches(self) -> int:
+        return int(self.L.wasr_model_kernel_launches(self.m))
+
 
 class Gpu:
     """Mirror of src/gpu.rs ``Gpu``: one WpCtx plus activation buffers sized for tmax."""
