@@ -233,6 +233,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--utts", type=int, default=0,
+                    help="profiling aid: only the first N config-4 utterances (0 = all 512)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "b200" else args.warmup
 
@@ -255,6 +257,8 @@ def main():
 
     pkg = load_pkg()
     lengths = pkg.synth.config_lengths(4)
+    if args.utts:
+        lengths = lengths[:args.utts]
     shards = pkg.synth.lpt_shards(lengths, world)
     shard = shards[rank]
     feats, sils, my_audio = make_workload(pkg, shard, lengths)

@@ -104,7 +104,7 @@ int wasr_model_error(WasrModel* m);
 enum {
   WASR_K_CONV1 = 0, WASR_K_CONV2, WASR_K_CONV3, WASR_K_QUANT, WASR_K_GEMM_LIN, WASR_K_LN,
   WASR_K_GEMM_QKV, WASR_K_ATTN, WASR_K_GEMM_O, WASR_K_GEMM_F1, WASR_K_GEMM_F2, WASR_K_GEMM_OUT,
-  WASR_K_IDS, WASR_K_COUNT
+  WASR_K_IDS, WASR_K_GELU, WASR_K_COUNT
 };
 int wasr_model_set_profile(WasrModel* m, int on);
 int wasr_model_profile(WasrModel* m, double* ms, int64_t* launches, int ncat);

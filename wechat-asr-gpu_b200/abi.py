@@ -111,7 +111,7 @@ WASR_F_DEVICE = 1
 WASR_F_NOSYNC = 2
 # kernel classes of wasr_model_profile (include/wasr.h)
 KERNEL_CLASSES = ["conv1", "conv2", "conv3", "quant", "gemm_lin", "layernorm", "gemm_qkv", "attention",
-                  "gemm_o", "gemm_f1", "gemm_f2", "gemm_out_argmax", "ids"]
+                  "gemm_o", "gemm_f1", "gemm_f2", "gemm_out_argmax", "ids", "gelu_quant"]
 
 _lib = None
 

@@ -312,6 +312,26 @@ __device__ __forceinline__ float dequant(int32_t acc, float xs, float ws, float 
   return __fadd_rn(__fmul_rn(__fmul_rn(static_cast<float>(acc), xs), ws), bias);
 }
 
+// Packed FP32x2 multiply / add with round-to-nearest per component (Blackwell), written as
+// PTX so that no compiler stage can contract a multiply feeding an add into a fused
+// multiply-add: each component is rounded exactly like __fmul_rn / __fadd_rn.
+__device__ __forceinline__ unsigned long long f2_bits(float2 a) {
+  return (static_cast<unsigned long long>(__float_as_uint(a.y)) << 32) | __float_as_uint(a.x);
+}
+__device__ __forceinline__ float2 bits_f2(unsigned long long u) {
+  return make_float2(__uint_as_float(static_cast<uint32_t>(u)), __uint_as_float(static_cast<uint32_t>(u >> 32)));
+}
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return bits_f2(r);
+}
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return bits_f2(r);
+}
+
 // Order-preserving map of a float to uint32 (for packed argmax keys).
 __device__ __forceinline__ uint32_t float_order(float v) {
   uint32_t u = __float_as_uint(v);

@@ -9,7 +9,8 @@
 // window_ops (src/model.rs:522-541) / run_post (src/model.rs:488-502), with these fusions:
 //   q/k/v         : one GEMM over the contiguous [1536][512] weight block (per-column scale)
 //   o, f2         : residual add fused into the GEMM epilogue (h += ...)
-//   f1            : bias + GELU + row |max| fused into the GEMM epilogue; the quant pass reads it
+//   f1            : bias in the GEMM epilogue; GELU + row |max| + quant in one row kernel that
+//                   never writes the GELU values back
 //   output layer  : GEMM fused with the argmax (logits never written unless asked for)
 // A whole chunk of windows is captured once in a CUDA graph and replayed when the same
 // window layout comes back (the reference graphs one window per t1, src/model.rs:576-604).
@@ -175,13 +176,15 @@ struct Launcher {
   template <typename F>
   int operator()(int cat, F&& f) {
     Rec r{cat, nullptr, nullptr};
+    // during stream capture a plain record only becomes a dependency edge; the External flag
+    // makes it a real event-record node that is timed at every replay
     if (recs) {
       if (cudaEventCreate(&r.a) != cudaSuccess || cudaEventCreate(&r.b) != cudaSuccess) return -4;
-      cudaEventRecord(r.a, m->stream);
+      cudaEventRecordWithFlags(r.a, m->stream, cudaEventRecordExternal);
     }
     const int rc = f();
     if (recs) {
-      cudaEventRecord(r.b, m->stream);
+      cudaEventRecordWithFlags(r.b, m->stream, cudaEventRecordExternal);
       recs->push_back(r);
     }
     kernels++;
@@ -230,13 +233,10 @@ int enqueue_chunk(WasrModel* m, const Chunk& c, const int* seg, float* logits, L
     TRY(K(WASR_K_GEMM_O, [&] { return gemm_run(gemm_args(m, m->xq, m->xs, M, D, L.o, D, L.ob, EPI_F32_ADD, m->h, D), st); }));
     // middle norm -> f1 + bias + GELU (+ row max) -> quant -> f2 + bias, residual fused
     TRY(K(WASR_K_LN, [&] { return launch_ln_quant(m->h, nullptr, fptr(m, L.mn_g), fptr(m, L.mn_b), M, m->xq, m->xs, st); }));
-    if (cudaMemsetAsync(m->rowmax, 0, static_cast<size_t>(M) * sizeof(unsigned), st) != cudaSuccess) return -4;
-    {
-      GemmArgs g = gemm_args(m, m->xq, m->xs, M, D, L.f1, FF, L.f1b, EPI_GELU_ROWMAX, m->f, FF);
-      g.rowmax = m->rowmax;
-      TRY(K(WASR_K_GEMM_F1, [&] { return gemm_run(g, st); }));
-    }
-    TRY(K(WASR_K_QUANT, [&] { return launch_quant_rows_max(m->f, M, FF, m->rowmax, m->xq, m->xs, st); }));
+    TRY(K(WASR_K_GEMM_F1, [&] {
+      return gemm_run(gemm_args(m, m->xq, m->xs, M, D, L.f1, FF, L.f1b, EPI_F32, m->f, FF), st);
+    }));
+    TRY(K(WASR_K_GELU, [&] { return launch_gelu_quant_ro(m->f, M, FF, m->xq, m->xs, st); }));
     TRY(K(WASR_K_GEMM_F2, [&] { return gemm_run(gemm_args(m, m->xq, m->xs, M, FF, L.f2, D, L.f2b, EPI_F32_ADD, m->h, D), st); }));
   }
   // output layer + argmax (src/model.rs:498-501)

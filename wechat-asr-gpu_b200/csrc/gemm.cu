@@ -4,6 +4,7 @@
 // there is nothing to search and nothing to warm up.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <mutex>
 #include <unordered_map>
@@ -100,7 +101,7 @@ bool ensure_attr() {
 
 template <int EPI>
 bool prepare_epi() {
-  return ensure_attr<256, EPI>() && ensure_attr<128, EPI>() && ensure_attr<64, EPI>() && ensure_attr<32, EPI>();
+  return ensure_attr<256, EPI>() && ensure_attr<128, EPI>() && ensure_attr<64, EPI>();
 }
 
 template <int BN, int EPI>
@@ -109,8 +110,8 @@ int launch_tc(const GemmArgs& g, cudaStream_t s) {
   if (!tensor_map(g.a, g.M, g.K, 128, &ta) || !tensor_map(g.b, g.N, g.K, BN, &tb)) return -4;
   constexpr int smem = TcCfg<BN>::SMEM;
   if (!ensure_attr<BN, EPI>()) return -4;
-  dim3 grid((g.n_store + BN - 1) / BN, (g.M + 127) / 128);
-  gemm_i8_tc<BN, EPI><<<grid, 192, smem, s>>>(ta, tb, g);
+  const int tiles = ((g.n_store + BN - 1) / BN) * ((g.M + 127) / 128);
+  gemm_i8_tc<BN, EPI><<<std::min(tiles, num_sms()), TcCfg<BN>::THREADS, smem, s>>>(ta, tb, g);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 
@@ -128,8 +129,7 @@ int launch_epi(const GemmArgs& g, cudaStream_t s) {
   auto ctas = [&](int bn) { return tm * ((g.n_store + bn - 1) / bn); };
   if (ctas(256) >= sms) return launch_tc<256, EPI>(g, s);
   if (ctas(128) >= sms) return launch_tc<128, EPI>(g, s);
-  if (ctas(64) >= sms) return launch_tc<64, EPI>(g, s);
-  return launch_tc<32, EPI>(g, s);
+  return launch_tc<64, EPI>(g, s);
 }
 
 }  // namespace

@@ -6,10 +6,11 @@
 //
 // Both operands are K-major (row-major [rows][K]), exactly the layout of the reference's
 // xq buffers and blob weights, so TMA loads them directly with 128-byte swizzle into the
-// canonical UMMA K-major layout.  One CTA computes a 128 x BN tile:
+// canonical UMMA K-major layout.  CTAs are persistent over 128 x BN tiles:
 //   warp 0      : TMA producer (one elected lane), STAGES-deep smem ring
 //   warp 1      : TMEM allocator + MMA issuer (one lane issues tcgen05.mma, M=128, N=BN, K=32)
-//   warps 2..5  : epilogue; warp w reads TMEM lanes 32*(w%4).. with tcgen05.ld (thread = row)
+//   warps 2..9  : epilogue; warp w reads TMEM lanes 32*(w%4).. with tcgen05.ld (thread = row),
+//                 stages through shared memory and stores 128-byte row segments
 // Every spin-wait is bounded (common.cuh); a timeout sets the context's error word.
 #pragma once
 
@@ -113,41 +114,161 @@ __device__ __forceinline__ void epi_finish_row(const GemmArgs& g, int row, float
 
 template <int BN>
 struct TcCfg {
+  static_assert(BN == 64 || BN == 128 || BN == 256, "tile width");
   static constexpr int BM = 128;
   static constexpr int BK = 128;  // bytes of K per stage = one 128-byte swizzle row
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = BN * BK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = 4;
-  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
-  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + (2 * STAGES + 1) * 8 + 16;
+  static constexpr int STAGES = BN >= 256 ? 3 : 4;
+  static constexpr int EPI_WARPS = 8;                 // two per TMEM lane quarter, half the columns each
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int TMEM_COLS = 2 * BN;            // two accumulator buffers
+  static constexpr int STG_FLOATS = 32 * 32;          // per epilogue warp
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_WARPS * STG_FLOATS * 4 + (2 * STAGES + 4) * 8 + 16;
 };
 
+// Epilogue staging: a warp's 32 rows x 32 columns, stored so that row-per-thread float4
+// writes and row-contiguous float4 reads (8 lanes per 128-byte row segment) are both at the
+// minimum number of shared-memory wavefronts (16-byte groups XOR-swizzled by row).
+__device__ __forceinline__ int stg_off(int r, int c4) { return r * 32 + ((c4 ^ (r & 7)) << 2); }
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// One 32-column chunk of a warp's 32 rows.  r[] holds row (rowbase + lane), columns
+// col0..col0+31 of the accumulator; columns >= n_store and rows >= M are never written.
+template <int EPI>
+__device__ __forceinline__ void epi_chunk(const GemmArgs& g, float* stg, int lane, int rowbase, int col0,
+                                          const uint32_t (&r)[32], float& rmax, float& best, uint32_t& bidx) {
+  const int row = rowbase + lane;
+  const int ncols = min(32, g.n_store - col0);
+  if constexpr (EPI == EPI_ARGMAX) {
+    if (row < g.M) {
+      const float xs = g.xs[row];
+#pragma unroll
+      for (int j = 0; j < 32; j++) {
+        if (j < ncols) {
+          const int col = col0 + j;
+          const float ws = g.ws_vec ? __ldg(g.ws_vec + col) : g.ws;
+          const float bb = g.bias ? __ldg(g.bias + col) : 0.0f;
+          const float v = dequant(static_cast<int32_t>(r[j]), xs, ws, bb);
+          if (v > best) { best = v; bidx = static_cast<uint32_t>(col); }
+        }
+      }
+    }
+    return;
+  } else {
+    float v[32];
+    if constexpr (EPI == EPI_I32) {
+#pragma unroll
+      for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+    } else {
+      const float xs = row < g.M ? g.xs[row] : 0.0f;
+#pragma unroll
+      for (int j = 0; j < 32; j++) {
+        const int col = col0 + j;
+        const bool in = j < ncols;
+        const float ws = !in ? 0.0f : g.ws_vec ? __ldg(g.ws_vec + col) : g.ws;
+        const float bb = (in && g.bias) ? __ldg(g.bias + col) : 0.0f;
+        v[j] = dequant(static_cast<int32_t>(r[j]), xs, ws, bb);
+        if constexpr (EPI == EPI_F32_ROWMAX) {
+          if (in) rmax = fmaxf(rmax, fabsf(v[j]));
+        }
+      }
+    }
+#pragma unroll
+    for (int c4 = 0; c4 < 8; c4++)
+      *reinterpret_cast<float4*>(stg + stg_off(lane, c4)) = make_float4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
+    if constexpr (EPI == EPI_GELU_ROWMAX) {
+      // GELU in place, rolled (the exact tanh is long: one copy of its code, not 32)
+#pragma unroll 1
+      for (int j = 0; j < 32; j++) {
+        const int off = stg_off(lane, j >> 2) + (j & 3);
+        const float gv = gelu_ref(stg[off]);
+        stg[off] = gv;
+        if (j < ncols) rmax = fmaxf(rmax, fabsf(gv));
+      }
+    }
+    __syncwarp();
+    // coalesced write-out: lane -> (row group lane/8, 4-column group lane%8), 4 rows per pass
+    const int c4 = lane & 7;
+    const int col = col0 + 4 * c4;
+    const bool vec = (g.ldo & 3) == 0 && col + 3 < g.n_store;
+#pragma unroll 2
+    for (int i = 0; i < 8; i++) {
+      const int rr = 4 * i + (lane >> 3);
+      const int grow = rowbase + rr;
+      if (grow < g.M && col < g.n_store) {
+        const float4 x = *reinterpret_cast<const float4*>(stg + stg_off(rr, c4));
+        const int64_t o = static_cast<int64_t>(grow) * g.ldo + col;
+        if constexpr (EPI == EPI_I32) {
+          if (vec) {
+            *reinterpret_cast<int4*>(g.out_i32 + o) =
+                make_int4(__float_as_int(x.x), __float_as_int(x.y), __float_as_int(x.z), __float_as_int(x.w));
+          } else {
+            const float xv[4] = {x.x, x.y, x.z, x.w};
+            for (int k = 0; k < 4 && col + k < g.n_store; k++) g.out_i32[o + k] = __float_as_int(xv[k]);
+          }
+        } else if constexpr (EPI == EPI_F32_ADD) {
+          if (vec) {
+            const float4 h = *reinterpret_cast<const float4*>(g.out + o);
+            *reinterpret_cast<float4*>(g.out + o) =
+                make_float4(__fadd_rn(h.x, x.x), __fadd_rn(h.y, x.y), __fadd_rn(h.z, x.z), __fadd_rn(h.w, x.w));
+          } else {
+            const float xv[4] = {x.x, x.y, x.z, x.w};
+            for (int k = 0; k < 4 && col + k < g.n_store; k++) g.out[o + k] = __fadd_rn(g.out[o + k], xv[k]);
+          }
+        } else {
+          if (vec) {
+            *reinterpret_cast<float4*>(g.out + o) = x;
+          } else {
+            const float xv[4] = {x.x, x.y, x.z, x.w};
+            for (int k = 0; k < 4 && col + k < g.n_store; k++) g.out[o + k] = xv[k];
+          }
+        }
+      }
+    }
+    __syncwarp();  // the staging buffer is reused by the next chunk
+  }
+}
+
+// Persistent, warp-specialised tcgen05 GEMM.  CTAs walk the 128 x BN output tiles in a
+// static round robin.  Warp 0 (one lane) streams A/B k-blocks through a STAGES-deep TMA ring;
+// warp 1 (one lane) issues tcgen05.mma into one of two TMEM accumulators; warps 2..9 drain the
+// other accumulator, so a tile's epilogue overlaps the next tile's MMAs.
 template <int BN, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
     gemm_i8_tc(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, GemmArgs g) {
   using Cfg = TcCfg<BN>;
-  constexpr int STAGES = Cfg::STAGES;
+  constexpr int ST = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* accb = empty + STAGES;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(accb + 1);
+  uint8_t* sB = smem + ST * Cfg::A_BYTES;
+  float* stg_all = reinterpret_cast<float*>(sB + ST * Cfg::B_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(stg_all + Cfg::EPI_WARPS * Cfg::STG_FLOATS);
+  uint64_t* empty = full + ST;
+  uint64_t* tfull = empty + ST;   // [2] accumulator ready (MMA -> epilogue)
+  uint64_t* tempty = tfull + 2;   // [2] accumulator drained (epilogue -> MMA)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * Cfg::BM;
+  const int n_tiles = (g.n_store + BN - 1) / BN;
+  const int tiles = n_tiles * ((g.M + Cfg::BM - 1) / Cfg::BM);
   const int nk = (g.K + Cfg::BK - 1) / Cfg::BK;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; s++) {
+    for (int s = 0; s < ST; s++) {
       mbar_init(full + s, 1);
       mbar_init(empty + s, 1);
     }
-    mbar_init(accb, 1);
+    for (int b = 0; b < 2; b++) {
+      mbar_init(tfull + b, 1);
+      mbar_init(tempty + b, Cfg::EPI_WARPS);
+    }
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tma_a);
@@ -164,68 +285,85 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      int issued = 0;
-      for (int kb = 0; kb < nk; kb++) {
-        const int s = kb % STAGES, it = kb / STAGES;
-        if (kb >= STAGES && !mbar_wait(empty + s, (it - 1) & 1)) {
-          atomicExch(g.err, ERR_WAIT_EMPTY);
-          *abort_flag = 1;
-          break;
+      int kc = 0;
+      for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
+        const int m0 = (tile / n_tiles) * Cfg::BM, n0 = (tile % n_tiles) * BN;
+        for (int kb = 0; kb < nk; kb++, kc++) {
+          const int s = kc % ST;
+          if (kc >= ST && !mbar_wait(empty + s, ((kc / ST) - 1) & 1)) {
+            atomicExch(g.err, ERR_WAIT_EMPTY);
+            *abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(full + s, Cfg::STAGE_BYTES);
+          tma_load_2d(sA + s * Cfg::A_BYTES, &tma_a, full + s, kb * Cfg::BK, m0);
+          tma_load_2d(sB + s * Cfg::B_BYTES, &tma_b, full + s, kb * Cfg::BK, n0);
         }
-        if (*abort_flag) break;
-        mbar_arrive_expect_tx(full + s, Cfg::STAGE_BYTES);
-        tma_load_2d(sA + s * Cfg::A_BYTES, &tma_a, full + s, kb * Cfg::BK, m0);
-        tma_load_2d(sB + s * Cfg::B_BYTES, &tma_b, full + s, kb * Cfg::BK, n0);
-        issued++;
       }
       // drain: never leave the CTA while a bulk copy may still write its shared memory
-      for (int kb = issued > STAGES ? issued - STAGES : 0; kb < issued; kb++)
-        if (!mbar_wait(full + kb % STAGES, (kb / STAGES) & 1)) atomicExch(g.err, ERR_WAIT_FULL);
+      for (int k = kc > ST ? kc - ST : 0; k < kc; k++)
+        if (!mbar_wait(full + k % ST, (k / ST) & 1)) atomicExch(g.err, ERR_WAIT_FULL);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_i8(BN);
-      for (int kb = 0; kb < nk; kb++) {
-        const int s = kb % STAGES, it = kb / STAGES;
-        if (!mbar_wait(full + s, it & 1)) {
-          atomicExch(g.err, ERR_WAIT_FULL);
+      int kc = 0, it = 0;
+      for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x, it++) {
+        const int b = it & 1, u = it >> 1;
+        if (it >= 2 && !mbar_wait(tempty + b, (u - 1) & 1)) {
+          atomicExch(g.err, ERR_WAIT_ACC);
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
-        const uint32_t a0 = smem_u32(sA + s * Cfg::A_BYTES), b0 = smem_u32(sB + s * Cfg::B_BYTES);
+        const uint32_t d = tmem + static_cast<uint32_t>(b * BN);
+        for (int kb = 0; kb < nk; kb++, kc++) {
+          const int s = kc % ST;
+          if (!mbar_wait(full + s, (kc / ST) & 1)) {
+            atomicExch(g.err, ERR_WAIT_FULL);
+            *abort_flag = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * Cfg::A_BYTES), b0 = smem_u32(sB + s * Cfg::B_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < Cfg::BK / 32; kk++)
-          mma_i8(tmem, desc_sw128(a0 + kk * 32), desc_sw128(b0 + kk * 32), idesc, (kb | kk) != 0);
-        mma_commit(empty + s);
+          for (int kk = 0; kk < Cfg::BK / 32; kk++)
+            mma_i8(d, desc_sw128(a0 + kk * 32), desc_sw128(b0 + kk * 32), idesc, (kb | kk) != 0);
+          mma_commit(empty + s);
+        }
+        mma_commit(tfull + b);  // also on abort: the epilogue must not wait for nothing
       }
-      mma_commit(accb);
     }
   } else {
-    // epilogue warps 2..5 -> TMEM lane quarter (warp % 4)
-    const int q = warp & 3;
-    const int row = m0 + q * 32 + lane;
-    const bool ok = mbar_wait(accb, 0);
-    if (!ok) {
-      atomicExch(g.err, ERR_WAIT_ACC);
-      *abort_flag = 1;
-    }
-    __syncwarp();  // lanes may leave the wait loop apart: tcgen05.ld is .sync.aligned
-    tc_fence_after();
-    float rmax = 0.0f, best = -3.40282347e+38f;
-    uint32_t bidx = 0xFFFFFFFFu;
-    const bool live = ok && !*abort_flag;
-#pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      uint32_t r[32];
-      tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, r);  // warp-collective
-      const int col0 = n0 + c0;
-      if (live && row < g.M && col0 < g.n_store) {
-        const int nc = min(32, g.n_store - col0);
-        epi_store_row<EPI>(g, row, col0, reinterpret_cast<const int32_t*>(r), nc, rmax, best, bidx);
+    const int e = warp - 2, q = warp & 3, half = e >> 2;  // TMEM lane quarter = warp % 4
+    float* stg = stg_all + e * Cfg::STG_FLOATS;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, it++) {
+      const int b = it & 1, u = it >> 1;
+      const int m0 = (tile / n_tiles) * Cfg::BM, n0 = (tile % n_tiles) * BN;
+      const bool ok = mbar_wait(tfull + b, u & 1);
+      if (!ok) {
+        atomicExch(g.err, ERR_WAIT_ACC);
+        *abort_flag = 1;
       }
+      // lanes may leave the wait apart and tcgen05.ld is .sync.aligned: decide warp-uniformly
+      const bool stop = __any_sync(0xffffffffu, !ok || *abort_flag);
+      tc_fence_after();
+      if (stop) break;
+      const int rowbase = m0 + q * 32;
+      float rmax = 0.0f, best = -3.40282347e+38f;
+      uint32_t bidx = 0xFFFFFFFFu;
+#pragma unroll 1
+      for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * BN + c0), r);
+        if (n0 + c0 < g.n_store) epi_chunk<EPI>(g, stg, lane, rowbase, n0 + c0, r, rmax, best, bidx);
+      }
+      if (rowbase + lane < g.M) epi_finish_row<EPI>(g, rowbase + lane, rmax, best, bidx);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty + b);
     }
-    if (live && row < g.M) epi_finish_row<EPI>(g, row, rmax, best, bidx);
   }
   tc_fence_before();
   __syncthreads();

@@ -87,11 +87,9 @@ __global__ void __launch_bounds__(160) conv2_k(const float* __restrict__ y1, con
   }
   __syncthreads();
   const int f = threadIdx.x % DIM, sub = threadIdx.x / DIM;  // 40 x 4 threads
-  float a[4][8];
+  float2 a01[8], a23[8];
 #pragma unroll
-  for (int o = 0; o < 4; o++)
-#pragma unroll
-    for (int l = 0; l < 8; l++) a[o][l] = 0.0f;
+  for (int l = 0; l < 8; l++) a01[l] = a23[l] = make_float2(0.0f, 0.0f);
 #pragma unroll 1
   for (int c0 = 0; c0 < C1; c0 += 8) {
 #pragma unroll
@@ -104,20 +102,24 @@ __global__ void __launch_bounds__(160) conv2_k(const float* __restrict__ y1, con
           const int idx = (c0 + cc) * 49 + i * 7 + j;
           const float xv = xin[(i * C1 + c0 + cc) * CV2_PAD + f + j];
           const float4 w4 = *reinterpret_cast<const float4*>(wsm + idx * CV2_OG + sub * 4);
-          a[0][l] = __fadd_rn(a[0][l], __fmul_rn(w4.x, xv));
-          a[1][l] = __fadd_rn(a[1][l], __fmul_rn(w4.y, xv));
-          a[2][l] = __fadd_rn(a[2][l], __fmul_rn(w4.z, xv));
-          a[3][l] = __fadd_rn(a[3][l], __fmul_rn(w4.w, xv));
+          a01[l].x = __fadd_rn(a01[l].x, __fmul_rn(w4.x, xv));
+          a01[l].y = __fadd_rn(a01[l].y, __fmul_rn(w4.y, xv));
+          a23[l].x = __fadd_rn(a23[l].x, __fmul_rn(w4.z, xv));
+          a23[l].y = __fadd_rn(a23[l].y, __fmul_rn(w4.w, xv));
         }
   }
   float* out = y2 + static_cast<int64_t>(r) * (C2 * W2);
+  float2 s01 = a01[0], s23 = a23[0];
 #pragma unroll
-  for (int o = 0; o < 4; o++) {
-    float sum = a[o][0];
-#pragma unroll
-    for (int l = 1; l < 8; l++) sum = __fadd_rn(sum, a[o][l]);
-    out[(og * CV2_OG + sub * 4 + o) * W2 + f] = fmaxf(sum, 0.0f);
+  for (int l = 1; l < 8; l++) {
+    s01 = make_float2(__fadd_rn(s01.x, a01[l].x), __fadd_rn(s01.y, a01[l].y));
+    s23 = make_float2(__fadd_rn(s23.x, a23[l].x), __fadd_rn(s23.y, a23[l].y));
   }
+  const int ob = og * CV2_OG + sub * 4;
+  out[(ob + 0) * W2 + f] = fmaxf(s01.x, 0.0f);
+  out[(ob + 1) * W2 + f] = fmaxf(s01.y, 0.0f);
+  out[(ob + 2) * W2 + f] = fmaxf(s23.x, 0.0f);
+  out[(ob + 3) * W2 + f] = fmaxf(s23.y, 0.0f);
   if (threadIdx.x < CV2_OG) out[(og * CV2_OG + threadIdx.x) * W2 + DIM] = 0.0f;
 }
 
@@ -146,11 +148,9 @@ __global__ void __launch_bounds__(160) conv3_k(const float* __restrict__ y2, con
   }
   __syncthreads();
   const int f = threadIdx.x % 20, sub = threadIdx.x / 20;  // 20 x 8 threads
-  float a[4][8];
+  float2 a01[8], a23[8];
 #pragma unroll
-  for (int o = 0; o < 4; o++)
-#pragma unroll
-    for (int l = 0; l < 8; l++) a[o][l] = 0.0f;
+  for (int l = 0; l < 8; l++) a01[l] = a23[l] = make_float2(0.0f, 0.0f);
 #pragma unroll 1
   for (int c0 = 0; c0 < C2; c0 += 8) {
 #pragma unroll
@@ -163,20 +163,24 @@ __global__ void __launch_bounds__(160) conv3_k(const float* __restrict__ y2, con
           const int idx = (c0 + cc) * 9 + i * 3 + j;
           const float xv = xin[(i * C2 + c0 + cc) * W2 + 2 * f + j];
           const float4 w4 = *reinterpret_cast<const float4*>(wsm + idx * CV3_OG + sub * 4);
-          a[0][l] = __fadd_rn(a[0][l], __fmul_rn(w4.x, xv));
-          a[1][l] = __fadd_rn(a[1][l], __fmul_rn(w4.y, xv));
-          a[2][l] = __fadd_rn(a[2][l], __fmul_rn(w4.z, xv));
-          a[3][l] = __fadd_rn(a[3][l], __fmul_rn(w4.w, xv));
+          a01[l].x = __fadd_rn(a01[l].x, __fmul_rn(w4.x, xv));
+          a01[l].y = __fadd_rn(a01[l].y, __fmul_rn(w4.y, xv));
+          a23[l].x = __fadd_rn(a23[l].x, __fmul_rn(w4.z, xv));
+          a23[l].y = __fadd_rn(a23[l].y, __fmul_rn(w4.w, xv));
         }
   }
   float* out = y3 + static_cast<int64_t>(r) * FLAT;
+  float2 s01 = a01[0], s23 = a23[0];
 #pragma unroll
-  for (int o = 0; o < 4; o++) {
-    float sum = a[o][0];
-#pragma unroll
-    for (int l = 1; l < 8; l++) sum = __fadd_rn(sum, a[o][l]);
-    out[(og * CV3_OG + sub * 4 + o) * 20 + f] = fmaxf(sum, 0.0f);
+  for (int l = 1; l < 8; l++) {
+    s01 = make_float2(__fadd_rn(s01.x, a01[l].x), __fadd_rn(s01.y, a01[l].y));
+    s23 = make_float2(__fadd_rn(s23.x, a23[l].x), __fadd_rn(s23.y, a23[l].y));
   }
+  const int ob = og * CV3_OG + sub * 4;
+  out[(ob + 0) * 20 + f] = fmaxf(s01.x, 0.0f);
+  out[(ob + 1) * 20 + f] = fmaxf(s01.y, 0.0f);
+  out[(ob + 2) * 20 + f] = fmaxf(s23.x, 0.0f);
+  out[(ob + 3) * 20 + f] = fmaxf(s23.y, 0.0f);
 }
 
 // ------------------------------------------------------------------------ quant
@@ -355,6 +359,33 @@ __global__ void __launch_bounds__(256) gelu_quant_k(float* __restrict__ x, int m
   if (lane == 0) xs[row] = sc;
 }
 
+// GELU + per-row quant of a read-only [m][k] input (the FF1 GEMM output): the GELU values are
+// only needed to quantise, so they are staged in shared memory (one warp per row, 8 rows per
+// block) and never written back.  Same results as gelu in place followed by quant.
+constexpr int GQ_ROWS = 8;
+
+__global__ void __launch_bounds__(256) gelu_quant_ro_k(const float* __restrict__ y, int m, int k,
+                                                       int8_t* __restrict__ xq, float* __restrict__ xs) {
+  extern __shared__ float gsm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * GQ_ROWS + warp;
+  if (row >= m) return;
+  float* g = gsm + static_cast<size_t>(warp) * k;
+  const float* r = y + static_cast<int64_t>(row) * k;
+  float mx = 0.0f;
+#pragma unroll 1
+  for (int j = lane; j < k; j += 32) {
+    const float v = gelu_ref(__ldg(r + j));
+    g[j] = v;
+    mx = fmaxf(mx, fabsf(v));
+  }
+  mx = warp_max(mx);
+  const float sc = quant_scale(mx), inv = quant_inv(sc);
+  int8_t* q = xq + static_cast<int64_t>(row) * k;
+  for (int j = lane; j < k; j += 32) q[j] = quant_one(g[j], inv);
+  if (lane == 0) xs[row] = sc;
+}
+
 __global__ void add_k(float* __restrict__ h, const float* __restrict__ a, size_t n) {
   const size_t i = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
   if (i + 3 < n && ((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(a)) & 15) == 0) {
@@ -405,22 +436,35 @@ __global__ void keys_to_ids_k(const unsigned long long* __restrict__ keys, int m
 // 8-lane order of src/kernels.rs:172-183; softmax with e_j = exp(s_j - max) and the row sum z
 // folded sequentially (src/model.rs:723-728); p_j = e_j / z; o_i[d] = sum_j p_j v_j[d] folded
 // over j in order (src/model.rs:729-735).  The score tile stays in shared memory.
-constexpr int ATT_HDP = HD + 1;
+//
+// Every output element keeps the CPU's exact sequence of rounded multiplies and adds; the
+// speed comes from register blocking: a thread owns 2 query rows x 4 keys for the scores and
+// 2 query rows x 4 head dims for PV, so each shared-memory load feeds several products.
+// Shared layout: Q and S hold query rows in interleaved pairs (float2 = rows 2p, 2p+1).
+constexpr int ATT_KVS = HD + 1;  // padded K-chunk row
+
+__host__ __device__ inline int att_pair_stride(int max_t1) { return ((max_t1 + 15) / 16) * 16 + 1; }
 
 size_t attention_smem_bytes(int max_t1) {
-  const int sp = (max_t1 | 1);
-  return static_cast<size_t>(ATT_QT * ATT_HDP + 64 * ATT_HDP + ATT_QT * sp) * 4;
+  const int sp = att_pair_stride(max_t1);
+  return static_cast<size_t>(ATT_QT / 2 * HD * 2 + 64 * ATT_KVS + ATT_QT / 2 * sp * 2 + ATT_QT) * 4;
 }
+
+__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
+// component-wise exactly rounded multiply / add of a query-row pair
+__device__ __forceinline__ float2 pmul(float2 a, float2 b) { return make_float2(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y)); }
+__device__ __forceinline__ float2 padd(float2 a, float2 b) { return make_float2(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y)); }
 
 __global__ void __launch_bounds__(256) attn_k(const float* __restrict__ q, const float* __restrict__ k,
                                               const float* __restrict__ v, int ld, Segs s,
                                               const int* __restrict__ toff, int max_t1, float* __restrict__ out,
                                               int ldo) {
   extern __shared__ float sm[];
-  const int sp = max_t1 | 1;
-  float* qs = sm;                       // [32][65]
-  float* kv = qs + ATT_QT * ATT_HDP;    // [64][65]
-  float* S = kv + 64 * ATT_HDP;         // [32][sp]
+  const int sp = att_pair_stride(max_t1);
+  float2* Q2 = reinterpret_cast<float2*>(sm);          // [16][64] query row pairs
+  float* KV = sm + ATT_QT / 2 * HD * 2;                 // [64][65] K chunk / [64][64] V chunk
+  float2* S2 = reinterpret_cast<float2*>(KV + 64 * ATT_KVS);  // [16][sp] score row pairs
+  float* Z = reinterpret_cast<float*>(S2 + ATT_QT / 2 * sp);  // [32] row sums
   const int tile = blockIdx.x, h = blockIdx.y;
   int sw = 0;
   if (toff) {
@@ -437,88 +481,107 @@ __global__ void __launch_bounds__(256) attn_k(const float* __restrict__ q, const
   const int ni = min(ATT_QT, t - i0);
   if (ni <= 0 || t > max_t1) return;
   const int tid = threadIdx.x;
+  float* Qf = reinterpret_cast<float*>(Q2);
   for (int e = tid; e < ATT_QT * HD; e += 256) {
     const int i = e >> 6, d = e & 63;
-    qs[i * ATT_HDP + d] = i < ni ? q[static_cast<int64_t>(rb + i0 + i) * ld + h * HD + d] : 0.0f;
+    Qf[((i >> 1) * HD + d) * 2 + (i & 1)] = i < ni ? q[static_cast<int64_t>(rb + i0 + i) * ld + h * HD + d] : 0.0f;
   }
-  // ---- scores
-  for (int j0 = 0; j0 < t; j0 += 64) {
-    const int nj = min(64, t - j0);
-    __syncthreads();
-    for (int e = tid; e < 64 * HD; e += 256) {
-      const int j = e >> 6, d = e & 63;
-      kv[j * ATT_HDP + d] = j < nj ? k[static_cast<int64_t>(rb + j0 + j) * ld + h * HD + d] : 0.0f;
-    }
-    __syncthreads();
-    for (int e = tid; e < ATT_QT * 64; e += 256) {
-      const int i = e >> 6, jj = e & 63;
-      if (i < ni && jj < nj) {
-        const float* qi = qs + i * ATT_HDP;
-        const float* kj = kv + jj * ATT_HDP;
-        float a[8];
+  const int ip = tid >> 4;  // query row pair (rows 2ip, 2ip+1)
+  // ---- scores: thread = row pair ip x keys jq, jq+16, jq+32, jq+48 of each 64-key chunk
+  {
+    const int jq = tid & 15;
+    for (int j0 = 0; j0 < t; j0 += 64) {
+      const int nj = min(64, t - j0);
+      __syncthreads();
+      for (int e = tid; e < 64 * (HD / 4); e += 256) {
+        const int j = e >> 4, d4 = (e & 15) * 4;
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j < nj) x = *reinterpret_cast<const float4*>(k + static_cast<int64_t>(rb + j0 + j) * ld + h * HD + d4);
+        float* dst = KV + j * ATT_KVS + d4;
+        dst[0] = x.x; dst[1] = x.y; dst[2] = x.z; dst[3] = x.w;
+      }
+      __syncthreads();
+      float2 sc[4];
 #pragma unroll
-        for (int l = 0; l < 8; l++) a[l] = __fmul_rn(qi[l], kj[l]);
+      for (int l = 0; l < 8; l++) {
+        float2 acc[4];
 #pragma unroll
-        for (int c = 1; c < 8; c++)
+        for (int c = 0; c < 8; c++) {
+          const int d = 8 * c + l;
+          const float2 qv = Q2[ip * HD + d];
 #pragma unroll
-          for (int l = 0; l < 8; l++) a[l] = __fadd_rn(a[l], __fmul_rn(qi[c * 8 + l], kj[c * 8 + l]));
-        float sum = a[0];
+          for (int u = 0; u < 4; u++) {
+            const float2 p = pmul(qv, f2(KV[(jq + 16 * u) * ATT_KVS + d]));
+            acc[u] = c == 0 ? p : padd(acc[u], p);
+          }
+        }
 #pragma unroll
-        for (int l = 1; l < 8; l++) sum = __fadd_rn(sum, a[l]);
-        S[i * sp + j0 + jj] = __fmul_rn(sum, 0.125f);
+        for (int u = 0; u < 4; u++) sc[u] = l == 0 ? acc[u] : padd(sc[u], acc[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int j = jq + 16 * u;
+        if (j < nj) S2[ip * sp + j0 + j] = pmul(sc[u], f2(0.125f));
       }
     }
   }
   __syncthreads();
   // ---- softmax: row max (order-free, warp per row), exp (element-wise), sequential row sum
+  float* Sf = reinterpret_cast<float*>(S2);
   const int warp = tid >> 5, lane = tid & 31;
   for (int i = warp; i < ni; i += 8) {
-    float* row = S + i * sp;
+    float* row = Sf + (i >> 1) * sp * 2 + (i & 1);
     float m = -3.40282347e+38f;
-    for (int j = lane; j < t; j += 32) m = fmaxf(m, row[j]);
+    for (int j = lane; j < t; j += 32) m = fmaxf(m, row[2 * j]);
     m = warp_max(m);
-    for (int j = lane; j < t; j += 32) row[j] = expf_ref(__fsub_rn(row[j], m));
+    for (int j = lane; j < t; j += 32) row[2 * j] = expf_ref(__fsub_rn(row[2 * j], m));
   }
   __syncthreads();
   if (tid < ni) {
-    float* row = S + tid * sp;
+    const float* row = Sf + (tid >> 1) * sp * 2 + (tid & 1);
     float z = 0.0f;
-    for (int j = 0; j < t; j++) z = __fadd_rn(z, row[j]);
-    qs[tid * ATT_HDP] = z;  // q tile is no longer needed: reuse column 0 for z
+    for (int j = 0; j < t; j++) z = __fadd_rn(z, row[2 * j]);
+    Z[tid] = z;
   }
   __syncthreads();
   for (int e = tid; e < ni * t; e += 256) {
     const int i = e / t, j = e - i * t;
-    S[i * sp + j] = __fdiv_rn(S[i * sp + j], qs[i * ATT_HDP]);
+    float* x = Sf + (i >> 1) * sp * 2 + (i & 1) + 2 * j;
+    *x = __fdiv_rn(*x, Z[i]);
   }
-  // ---- PV: thread owns 8 (i, d) pairs; sum over j in order
-  float acc[8];
+  // ---- PV: thread = row pair ip x head dims 4dq..4dq+3; sum over keys in order
+  const int dq = tid & 15;
+  float2 o[4];
 #pragma unroll
-  for (int p = 0; p < 8; p++) acc[p] = 0.0f;
+  for (int u = 0; u < 4; u++) o[u] = make_float2(0.0f, 0.0f);
   for (int j0 = 0; j0 < t; j0 += 64) {
     const int nj = min(64, t - j0);
     __syncthreads();
-    for (int e = tid; e < 64 * HD; e += 256) {
-      const int j = e >> 6, d = e & 63;
-      kv[j * ATT_HDP + d] = j < nj ? v[static_cast<int64_t>(rb + j0 + j) * ld + h * HD + d] : 0.0f;
+    for (int e = tid; e < 64 * (HD / 4); e += 256) {
+      const int j = e >> 4, d4 = (e & 15) * 4;
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (j < nj) x = *reinterpret_cast<const float4*>(v + static_cast<int64_t>(rb + j0 + j) * ld + h * HD + d4);
+      *reinterpret_cast<float4*>(KV + j * HD + d4) = x;
     }
     __syncthreads();
-#pragma unroll
-    for (int p = 0; p < 8; p++) {
-      const int e = tid + 256 * p, i = e >> 6, d = e & 63;
-      if (i < ni) {
-        const float* prow = S + i * sp + j0;
-        float a = acc[p];
-        for (int jj = 0; jj < nj; jj++) a = __fadd_rn(a, __fmul_rn(prow[jj], kv[jj * ATT_HDP + d]));
-        acc[p] = a;
-      }
+    const float2* prow = S2 + ip * sp + j0;
+#pragma unroll 4
+    for (int jj = 0; jj < nj; jj++) {
+      const float2 p = prow[jj];
+      const float4 vv = *reinterpret_cast<const float4*>(KV + jj * HD + 4 * dq);
+      o[0] = padd(o[0], pmul(p, f2(vv.x)));
+      o[1] = padd(o[1], pmul(p, f2(vv.y)));
+      o[2] = padd(o[2], pmul(p, f2(vv.z)));
+      o[3] = padd(o[3], pmul(p, f2(vv.w)));
     }
   }
-#pragma unroll
-  for (int p = 0; p < 8; p++) {
-    const int e = tid + 256 * p, i = e >> 6, d = e & 63;
-    if (i < ni) out[static_cast<int64_t>(rb + i0 + i) * ldo + h * HD + d] = acc[p];
-  }
+  const int r0 = 2 * ip;
+  if (r0 < ni)
+    *reinterpret_cast<float4*>(out + static_cast<int64_t>(rb + i0 + r0) * ldo + h * HD + 4 * dq) =
+        make_float4(o[0].x, o[1].x, o[2].x, o[3].x);
+  if (r0 + 1 < ni)
+    *reinterpret_cast<float4*>(out + static_cast<int64_t>(rb + i0 + r0 + 1) * ldo + h * HD + 4 * dq) =
+        make_float4(o[0].y, o[1].y, o[2].y, o[3].y);
 }
 
 __global__ void eval_math_k(int fn, const float* __restrict__ x, float* __restrict__ y, int n) {
@@ -548,6 +611,7 @@ bool kern_prepare() {
   set_smem(reinterpret_cast<const void*>(conv3_k), CV3_SMEM);
   set_smem(reinterpret_cast<const void*>(ln_quant_k), LN_SMEM);
   set_smem(reinterpret_cast<const void*>(attn_k), 227 * 1024);
+  set_smem(reinterpret_cast<const void*>(gelu_quant_ro_k), 227 * 1024);
   return cudaGetLastError() == cudaSuccess;
 }
 
@@ -590,6 +654,14 @@ int launch_ln_quant(float* h, const float* o, const float* g, const float* b, in
 int launch_gelu_quant(float* x, int m, int k, int8_t* xq, float* xs, cudaStream_t st) {
   if (m <= 0 || k <= 0) return 0;
   gelu_quant_k<<<(m + 7) / 8, 256, 0, st>>>(x, m, k, xq, xs);
+  return launched();
+}
+int launch_gelu_quant_ro(const float* y, int m, int k, int8_t* xq, float* xs, cudaStream_t st) {
+  if (m <= 0 || k <= 0) return 0;
+  const size_t smem = static_cast<size_t>(GQ_ROWS) * k * sizeof(float);
+  if (smem > 227 * 1024) return -2;
+  set_smem(reinterpret_cast<const void*>(gelu_quant_ro_k), 227 * 1024);
+  gelu_quant_ro_k<<<(m + GQ_ROWS - 1) / GQ_ROWS, 32 * GQ_ROWS, smem, st>>>(y, m, k, xq, xs);
   return launched();
 }
 int launch_add(float* h, const float* a, size_t n, cudaStream_t st) {
