@@ -176,86 +176,72 @@ __device__ __forceinline__ int8_t quant_one(float v, float inv) {
 // cased below with glibc's values.
 __device__ __forceinline__ float f_from_bits(uint32_t u) { return __uint_as_float(u); }
 
+// expm1f, branch-free: every path of the fdlibm algorithm shares the argument reduction
+// (k = 0, +-1 or round(x/ln2); hi = x - k*ln2_hi, lo = k*ln2_lo) and the rational core, and
+// differs only in a few-operation reconstruction; all reconstructions are evaluated and the
+// right one selected, so the lanes of a warp never diverge.  Bit-identical to glibc's expm1f
+// on |x| < 88, as the branch-free tanhf built on it is to glibc's tanhf on every float input
+// (exhaustive host comparison).
 __device__ __forceinline__ float expm1f_ref(float x) {
   const float ln2_hi = 6.9313812256e-01f, ln2_lo = 9.0580006145e-06f, invln2 = 1.4426950216e+00f;
   const float Q1 = -3.3333335072e-02f, Q2 = 1.5873016091e-03f, Q3 = -7.9365076090e-05f, Q4 = 4.0082177293e-06f,
               Q5 = -2.0109921195e-07f;
   uint32_t hx = __float_as_uint(x);
-  const uint32_t xsb = hx & 0x80000000u;
+  const uint32_t xsb = hx >> 31;
   hx &= 0x7fffffffu;
-  if (hx >= 0x4195b844u && xsb) return -1.0f;  // x < -27 ln2 (callers never pass large positive x)
-  float hi, lo, c = 0.0f, t;
-  int k;
-  if (hx > 0x3eb17218u) {
-    if (hx < 0x3F851592u) {
-      if (xsb == 0) { hi = __fsub_rn(x, ln2_hi); lo = ln2_lo; k = 1; }
-      else { hi = __fadd_rn(x, ln2_hi); lo = -ln2_lo; k = -1; }
-    } else {
-      k = static_cast<int>(__fadd_rn(__fmul_rn(invln2, x), xsb == 0 ? 0.5f : -0.5f));
-      t = static_cast<float>(k);
-      hi = __fsub_rn(x, __fmul_rn(t, ln2_hi));
-      lo = __fmul_rn(t, ln2_lo);
-    }
-    x = __fsub_rn(hi, lo);
-    c = __fsub_rn(__fsub_rn(hi, x), lo);
-  } else if (hx < 0x33000000u) {
-    return x;
-  } else {
-    k = 0;
-  }
-  const float hfx = __fmul_rn(0.5f, x);
-  const float hxs = __fmul_rn(x, hfx);
+  const int kgen = static_cast<int>(__fadd_rn(__fmul_rn(invln2, x), xsb ? -0.5f : 0.5f));
+  const int k = hx > 0x3eb17218u ? (hx < 0x3F851592u ? (xsb ? -1 : 1) : kgen) : 0;
+  const float tk = static_cast<float>(k);
+  const float hi = __fsub_rn(x, __fmul_rn(tk, ln2_hi)), lo = __fmul_rn(tk, ln2_lo);
+  const float xr = __fsub_rn(hi, lo);
+  const float c = __fsub_rn(__fsub_rn(hi, xr), lo);
+  const float hfx = __fmul_rn(0.5f, xr);
+  const float hxs = __fmul_rn(xr, hfx);
   float r1 = __fmul_rn(hxs, Q5);
   r1 = __fmul_rn(hxs, __fadd_rn(Q4, r1));
   r1 = __fmul_rn(hxs, __fadd_rn(Q3, r1));
   r1 = __fmul_rn(hxs, __fadd_rn(Q2, r1));
   r1 = __fadd_rn(1.0f, __fmul_rn(hxs, __fadd_rn(Q1, r1)));
-  t = __fsub_rn(3.0f, __fmul_rn(r1, hfx));
-  float e = __fmul_rn(hxs, __fdiv_rn(__fsub_rn(r1, t), __fsub_rn(6.0f, __fmul_rn(x, t))));
-  if (k == 0) return __fsub_rn(x, __fsub_rn(__fmul_rn(x, e), hxs));
-  e = __fsub_rn(__fmul_rn(x, __fsub_rn(e, c)), c);
-  e = __fsub_rn(e, hxs);
-  if (k == -1) return __fsub_rn(__fmul_rn(0.5f, __fsub_rn(x, e)), 0.5f);
-  if (k == 1) {
-    if (x < -0.25f) return __fmul_rn(-2.0f, __fsub_rn(e, __fadd_rn(x, 0.5f)));
-    return __fadd_rn(1.0f, __fmul_rn(2.0f, __fsub_rn(x, e)));
-  }
-  float y;
-  if (k <= -2 || k > 56) {
-    y = __fsub_rn(1.0f, __fsub_rn(e, x));
-    y = f_from_bits(__float_as_uint(y) + (static_cast<uint32_t>(k) << 23));
-    return __fsub_rn(y, 1.0f);
-  }
-  if (k < 23) {
-    t = f_from_bits(0x3f800000u - (0x1000000u >> k));
-    y = __fsub_rn(t, __fsub_rn(e, x));
-  } else {
-    t = f_from_bits(static_cast<uint32_t>(0x7f - k) << 23);
-    y = __fsub_rn(x, __fadd_rn(e, t));
-    y = __fadd_rn(y, 1.0f);
-  }
-  return f_from_bits(__float_as_uint(y) + (static_cast<uint32_t>(k) << 23));
+  const float t = __fsub_rn(3.0f, __fmul_rn(r1, hfx));
+  const float e = __fmul_rn(hxs, __fdiv_rn(__fsub_rn(r1, t), __fsub_rn(6.0f, __fmul_rn(xr, t))));
+  const float res0 = __fsub_rn(xr, __fsub_rn(__fmul_rn(xr, e), hxs));
+  const float e2 = __fsub_rn(__fsub_rn(__fmul_rn(xr, __fsub_rn(e, c)), c), hxs);
+  const float resm1 = __fsub_rn(__fmul_rn(0.5f, __fsub_rn(xr, e2)), 0.5f);
+  const float resp1 = xr < -0.25f ? __fmul_rn(-2.0f, __fsub_rn(e2, __fadd_rn(xr, 0.5f)))
+                                  : __fadd_rn(1.0f, __fmul_rn(2.0f, __fsub_rn(xr, e2)));
+  const uint32_t kexp = static_cast<uint32_t>(k) << 23;
+  const float yA = __fsub_rn(1.0f, __fsub_rn(e2, xr));
+  const float resA = __fsub_rn(f_from_bits(__float_as_uint(yA) + kexp), 1.0f);
+  const int kb = k < 0 ? 0 : (k > 31 ? 31 : k);
+  const float yB = __fsub_rn(f_from_bits(0x3f800000u - (0x1000000u >> kb)), __fsub_rn(e2, xr));
+  const float resB = f_from_bits(__float_as_uint(yB) + kexp);
+  const int kc = k < 0 ? 0 : (k > 127 ? 127 : k);
+  float yC = __fsub_rn(xr, __fadd_rn(e2, f_from_bits(static_cast<uint32_t>(0x7f - kc) << 23)));
+  yC = __fadd_rn(yC, 1.0f);
+  const float resC = f_from_bits(__float_as_uint(yC) + kexp);
+  float r = k == 0 ? res0 : k == -1 ? resm1 : k == 1 ? resp1 : (k <= -2 || k > 56) ? resA : k < 23 ? resB : resC;
+  r = (hx >= 0x4195b844u && xsb) ? -1.0f : r;               // x < -27 ln2
+  r = (hx <= 0x3eb17218u && hx < 0x33000000u) ? x : r;      // |x| < 2^-25
+  return r;
 }
 
+// tanhf, branch-free: tanh(|x|) = 1 - 2/(expm1(2|x|)+2) for |x| >= 1, -t/(t+2) with
+// t = expm1(-2|x|) below 1, 1 - 1e-30 from 22 on; odd symmetry; the tiny / zero / non-finite
+// cases of the reference algorithm as selects.
 __device__ __forceinline__ float tanhf_ref(float x) {
   const uint32_t jx = __float_as_uint(x), ix = jx & 0x7fffffffu;
-  if (ix >= 0x7f800000u) return (jx >> 31) ? __fsub_rn(__fdiv_rn(1.0f, x), 1.0f) : __fadd_rn(__fdiv_rn(1.0f, x), 1.0f);
-  float z;
-  if (ix < 0x41b00000u) {  // |x| < 22
-    if (ix == 0) return x;
-    if (ix < 0x24000000u) return __fmul_rn(x, __fadd_rn(1.0f, x));
-    const float ax = fabsf(x);
-    if (ix >= 0x3f800000u) {
-      const float t = expm1f_ref(__fmul_rn(2.0f, ax));
-      z = __fsub_rn(1.0f, __fdiv_rn(2.0f, __fadd_rn(t, 2.0f)));
-    } else {
-      const float t = expm1f_ref(__fmul_rn(-2.0f, ax));
-      z = __fdiv_rn(-t, __fadd_rn(t, 2.0f));
-    }
-  } else {
-    z = __fsub_rn(1.0f, 1.0e-30f);
-  }
-  return (jx >> 31) ? -z : z;
+  const float ax = fabsf(x);
+  const bool ge1 = ix >= 0x3f800000u;
+  const float t = expm1f_ref(__fmul_rn(ge1 ? 2.0f : -2.0f, ax));
+  const float q = __fdiv_rn(ge1 ? 2.0f : -t, __fadd_rn(t, 2.0f));
+  float z = ge1 ? __fsub_rn(1.0f, q) : q;
+  z = ix >= 0x41b00000u ? __fsub_rn(1.0f, 1.0e-30f) : z;
+  float r = (jx >> 31) ? -z : z;
+  r = ix < 0x24000000u ? __fmul_rn(x, __fadd_rn(1.0f, x)) : r;
+  r = ix == 0 ? x : r;
+  if (ix >= 0x7f800000u)  // non-finite input: 1/x -+ 1 as in the reference
+    r = (jx >> 31) ? __fsub_rn(__fdiv_rn(1.0f, x), 1.0f) : __fadd_rn(__fdiv_rn(1.0f, x), 1.0f);
+  return r;
 }
 
 __constant__ static const unsigned long long kExp2Tab[32] = {

@@ -62,46 +62,50 @@ __global__ void __launch_bounds__(128) conv1_k(const float* __restrict__ x, cons
 // y2[r][o][f] = relu(dotf(c2[o], patch)) with patch[c*49+i*7+j] = y1[5r+i-1][c][f+j-3]
 // (src/model.rs:420-444); column 40 is 0.  Block = (row r, 16 output channels); thread =
 // (4 channels, one f).  dotf lane of tap idx = idx % 8 = (c + 7i + j) % 8 (49 = 1 mod 8), so
-// unrolling 8 channels makes every lane index a compile-time constant.
+// unrolling 8 channels makes every lane index a compile-time constant.  Input channels are
+// staged 8 at a time (in increasing order, so every lane still sees its taps in order), which
+// keeps shared memory at 35 KB per block and lets 5-6 blocks share an SM.
 constexpr int CV2_OG = 16;
 constexpr int CV2_PAD = 46;  // 40 + 3 + 3 zero columns
-constexpr int CV2_SMEM = (7 * C1 * CV2_PAD + K2 * CV2_OG) * 4;
+constexpr int CV2_CC = 8;    // input channels per stage
+constexpr int CV2_SMEM = (7 * CV2_CC * CV2_PAD + CV2_CC * 49 * CV2_OG) * 4;
 
 __global__ void __launch_bounds__(160) conv2_k(const float* __restrict__ y1, const float* __restrict__ c2, Segs s,
                                                float* __restrict__ y2) {
   extern __shared__ float sm[];
-  float* xin = sm;                       // [7][32][46]
-  float* wsm = sm + 7 * C1 * CV2_PAD;     // [1568][16]
+  float* xin = sm;                              // [7][8][46]
+  float* wsm = sm + 7 * CV2_CC * CV2_PAD;       // [392][16]
   const int r = blockIdx.x, og = blockIdx.y;
   const int sw = s.seg_of_row(r);
   const int fb = s.frame_begin(sw), t = s.frames(sw), ti = r - s.row_begin(sw);
-  for (int e = threadIdx.x; e < K2 * CV2_OG; e += blockDim.x) {
-    const int ol = e & (CV2_OG - 1), idx = e >> 4;
-    wsm[e] = c2[static_cast<int64_t>(og * CV2_OG + ol) * K2 + idx];
-  }
-  for (int e = threadIdx.x; e < 7 * C1 * CV2_PAD; e += blockDim.x) {
-    const int fp = e % CV2_PAD, c = (e / CV2_PAD) % C1, i = e / (CV2_PAD * C1);
-    const int tt = ti * 5 + i - 1, ff = fp - 3;
-    xin[e] = (tt >= 0 && tt < t && ff >= 0 && ff < DIM) ? y1[static_cast<int64_t>(fb + tt) * (C1 * DIM) + c * DIM + ff]
-                                                          : 0.0f;
-  }
-  __syncthreads();
   const int f = threadIdx.x % DIM, sub = threadIdx.x / DIM;  // 40 x 4 threads
   float2 a01[8], a23[8];
 #pragma unroll
   for (int l = 0; l < 8; l++) a01[l] = a23[l] = make_float2(0.0f, 0.0f);
 #pragma unroll 1
-  for (int c0 = 0; c0 < C1; c0 += 8) {
+  for (int c0 = 0; c0 < C1; c0 += CV2_CC) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < CV2_CC * 49 * CV2_OG; e += blockDim.x) {
+      const int ol = e & (CV2_OG - 1), li = e >> 4;
+      wsm[e] = c2[static_cast<int64_t>(og * CV2_OG + ol) * K2 + c0 * 49 + li];
+    }
+    for (int e = threadIdx.x; e < 7 * CV2_CC * CV2_PAD; e += blockDim.x) {
+      const int fp = e % CV2_PAD, cc = (e / CV2_PAD) % CV2_CC, i = e / (CV2_PAD * CV2_CC);
+      const int tt = ti * 5 + i - 1, ff = fp - 3;
+      xin[e] = (tt >= 0 && tt < t && ff >= 0 && ff < DIM)
+                   ? y1[static_cast<int64_t>(fb + tt) * (C1 * DIM) + (c0 + cc) * DIM + ff]
+                   : 0.0f;
+    }
+    __syncthreads();
 #pragma unroll
-    for (int cc = 0; cc < 8; cc++)
+    for (int cc = 0; cc < CV2_CC; cc++)
 #pragma unroll
       for (int i = 0; i < 7; i++)
 #pragma unroll
         for (int j = 0; j < 7; j++) {
           const int l = (cc + 7 * i + j) & 7;
-          const int idx = (c0 + cc) * 49 + i * 7 + j;
-          const float xv = xin[(i * C1 + c0 + cc) * CV2_PAD + f + j];
-          const float4 w4 = *reinterpret_cast<const float4*>(wsm + idx * CV2_OG + sub * 4);
+          const float xv = xin[(i * CV2_CC + cc) * CV2_PAD + f + j];
+          const float4 w4 = *reinterpret_cast<const float4*>(wsm + (cc * 49 + i * 7 + j) * CV2_OG + sub * 4);
           a01[l].x = __fadd_rn(a01[l].x, __fmul_rn(w4.x, xv));
           a01[l].y = __fadd_rn(a01[l].y, __fmul_rn(w4.y, xv));
           a23[l].x = __fadd_rn(a23[l].x, __fmul_rn(w4.z, xv));
@@ -125,44 +129,47 @@ __global__ void __launch_bounds__(160) conv2_k(const float* __restrict__ y1, con
 
 // ------------------------------------------------------------------------ conv3
 // y3[r][o*20+f] = relu(dotf(c3[o], patch)) with patch[c*9+i*3+j] = y2[r+i-1][c][2f+j]
-// (src/model.rs:446-468).  Lane of tap idx = (c + 3i + j) % 8 (9 = 1 mod 8).
+// (src/model.rs:446-468).  Lane of tap idx = (c + 3i + j) % 8 (9 = 1 mod 8).  Input channels
+// are staged 8 at a time in increasing order (13 KB of shared memory per block).
 constexpr int CV3_OG = 32;
-constexpr int CV3_SMEM = (3 * C2 * W2 + K3 * CV3_OG) * 4;
+constexpr int CV3_CC = 8;
+constexpr int CV3_SMEM = (3 * CV3_CC * W2 + CV3_CC * 9 * CV3_OG) * 4;
 
 __global__ void __launch_bounds__(160) conv3_k(const float* __restrict__ y2, const float* __restrict__ c3, Segs s,
                                                float* __restrict__ y3) {
   extern __shared__ float sm[];
-  float* xin = sm;                 // [3][64][41]
-  float* wsm = sm + 3 * C2 * W2;   // [576][32]
+  float* xin = sm;                    // [3][8][41]
+  float* wsm = sm + 3 * CV3_CC * W2;  // [72][32]
   const int r = blockIdx.x, og = blockIdx.y;
   const int sw = s.seg_of_row(r);
   const int rb = s.row_begin(sw), t1 = s.rows(sw), ti = r - rb;
-  for (int e = threadIdx.x; e < K3 * CV3_OG; e += blockDim.x) {
-    const int ol = e & (CV3_OG - 1), idx = e >> 5;
-    wsm[e] = c3[static_cast<int64_t>(og * CV3_OG + ol) * K3 + idx];
-  }
-  for (int e = threadIdx.x; e < 3 * C2 * W2; e += blockDim.x) {
-    const int i = e / (C2 * W2), rem = e - i * (C2 * W2);
-    const int tt = ti + i - 1;
-    xin[e] = (tt >= 0 && tt < t1) ? y2[static_cast<int64_t>(rb + tt) * (C2 * W2) + rem] : 0.0f;
-  }
-  __syncthreads();
   const int f = threadIdx.x % 20, sub = threadIdx.x / 20;  // 20 x 8 threads
   float2 a01[8], a23[8];
 #pragma unroll
   for (int l = 0; l < 8; l++) a01[l] = a23[l] = make_float2(0.0f, 0.0f);
 #pragma unroll 1
-  for (int c0 = 0; c0 < C2; c0 += 8) {
+  for (int c0 = 0; c0 < C2; c0 += CV3_CC) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < CV3_CC * 9 * CV3_OG; e += blockDim.x) {
+      const int ol = e & (CV3_OG - 1), li = e >> 5;
+      wsm[e] = c3[static_cast<int64_t>(og * CV3_OG + ol) * K3 + c0 * 9 + li];
+    }
+    for (int e = threadIdx.x; e < 3 * CV3_CC * W2; e += blockDim.x) {
+      const int i = e / (CV3_CC * W2), rem = e - i * (CV3_CC * W2);
+      const int cc = rem / W2, col = rem - cc * W2;
+      const int tt = ti + i - 1;
+      xin[e] = (tt >= 0 && tt < t1) ? y2[static_cast<int64_t>(rb + tt) * (C2 * W2) + (c0 + cc) * W2 + col] : 0.0f;
+    }
+    __syncthreads();
 #pragma unroll
-    for (int cc = 0; cc < 8; cc++)
+    for (int cc = 0; cc < CV3_CC; cc++)
 #pragma unroll
       for (int i = 0; i < 3; i++)
 #pragma unroll
         for (int j = 0; j < 3; j++) {
           const int l = (cc + 3 * i + j) & 7;
-          const int idx = (c0 + cc) * 9 + i * 3 + j;
-          const float xv = xin[(i * C2 + c0 + cc) * W2 + 2 * f + j];
-          const float4 w4 = *reinterpret_cast<const float4*>(wsm + idx * CV3_OG + sub * 4);
+          const float xv = xin[(i * CV3_CC + cc) * W2 + 2 * f + j];
+          const float4 w4 = *reinterpret_cast<const float4*>(wsm + (cc * 9 + i * 3 + j) * CV3_OG + sub * 4);
           a01[l].x = __fadd_rn(a01[l].x, __fmul_rn(w4.x, xv));
           a01[l].y = __fadd_rn(a01[l].y, __fmul_rn(w4.y, xv));
           a23[l].x = __fadd_rn(a23[l].x, __fmul_rn(w4.z, xv));
@@ -372,7 +379,28 @@ __global__ void __launch_bounds__(256) gelu_quant_ro_k(const float* __restrict__
   if (row >= m) return;
   float* g = gsm + static_cast<size_t>(warp) * k;
   const float* r = y + static_cast<int64_t>(row) * k;
+  int8_t* q = xq + static_cast<int64_t>(row) * k;
   float mx = 0.0f;
+  if ((k & 127) == 0 && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
+    // four independent GELUs per lane per step: the long exact tanh chains overlap
+#pragma unroll 1
+    for (int j = lane * 4; j < k; j += 128) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(r + j));
+      const float4 gv = make_float4(gelu_ref(v.x), gelu_ref(v.y), gelu_ref(v.z), gelu_ref(v.w));
+      *reinterpret_cast<float4*>(g + j) = gv;
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(gv.x), fabsf(gv.y)), fmaxf(fabsf(gv.z), fabsf(gv.w))));
+    }
+    mx = warp_max(mx);
+    const float sc = quant_scale(mx), inv = quant_inv(sc);
+    for (int j = lane * 4; j < k; j += 128) {
+      const float4 gv = *reinterpret_cast<const float4*>(g + j);
+      char4 c;
+      c.x = quant_one(gv.x, inv); c.y = quant_one(gv.y, inv); c.z = quant_one(gv.z, inv); c.w = quant_one(gv.w, inv);
+      *reinterpret_cast<char4*>(q + j) = c;
+    }
+    if (lane == 0) xs[row] = sc;
+    return;
+  }
 #pragma unroll 1
   for (int j = lane; j < k; j += 32) {
     const float v = gelu_ref(__ldg(r + j));
@@ -381,7 +409,6 @@ __global__ void __launch_bounds__(256) gelu_quant_ro_k(const float* __restrict__
   }
   mx = warp_max(mx);
   const float sc = quant_scale(mx), inv = quant_inv(sc);
-  int8_t* q = xq + static_cast<int64_t>(row) * k;
   for (int j = lane; j < k; j += 32) q[j] = quant_one(g[j], inv);
   if (lane == 0) xs[row] = sc;
 }
