@@ -150,6 +150,23 @@ int wp_gemm2_pc(WpCtx* c, const int8_t* xq, const float* xs, int t, int k, size_
 int wp_gemm_i32(WpCtx* c, const int8_t* xq, int t, int k, size_t w_off, int n, void* stream,
                 int32_t* acc);
 
+/* ---- additive: GEMM + per-row re-quantisation that allocates nothing ------------- */
+/* No counterpart in the reference.  Same result as wp_gemm_q, for callers that cannot
+ * allocate device memory when they run it, such as code that runs while a CUDA graph is being
+ * captured or a process whose device-memory budget is fixed up front.  wp_gemm_q may cudaMalloc
+ * a larger staging buffer on demand.  This entry point stages through one fixed device array
+ * inside the library instead, which every GPU that loads the library holds until the process
+ * exits (4 MiB + 16 KiB).  Limits: t <= WP_NOALLOC_MAX_ROWS and t*n <= WP_NOALLOC_MAX_ELEMS;
+ * larger calls return -22 and change nothing.  The first call on each device looks up the
+ * array's device address (cudaGetSymbolAddress; -23 if that fails).  Make that first call
+ * before any stream capture.  All calls share the one array, which keeps the last call's
+ * values (the per-row maxima are cleared by every call).  Calls that overlap on the GPU (on
+ * different streams) therefore race; serialise them. */
+#define WP_NOALLOC_MAX_ELEMS 1048576
+#define WP_NOALLOC_MAX_ROWS 4096
+int wp_gemm_q_noalloc(WpCtx* c, const int8_t* xq, const float* xs, int t, int k, size_t w_off, int n,
+                      float ws, const float* bias_dev, void* stream, int8_t* out_q, float* out_s);
+
 #ifdef __cplusplus
 }
 #endif

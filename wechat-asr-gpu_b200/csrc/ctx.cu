@@ -251,6 +251,84 @@ int wp_gemm_i32(WpCtx* c, const int8_t* xq, int t, int k, size_t w_off, int n, v
                    nullptr, nullptr, nullptr, acc, 3);
 }
 
+}  // extern "C"
+
+// ------------------------------------------------------------------------ no-allocation GEMM+quant
+// Some callers cannot call cudaMalloc at the time they run a GEMM: code running while a CUDA
+// graph is being captured (an allocation is not a capturable operation), or an embedding
+// process whose memory budget is fixed up front.  wp_gemm_q grows its fp32 staging buffer on
+// demand; wp_gemm_q_noalloc instead stages through this fixed array, which every GPU that loads
+// the library holds until the process exits: WP_NOALLOC_MAX_ELEMS fp32 values of GEMM output
+// (t*n <= 1,048,576, 4 MiB) followed by WP_NOALLOC_MAX_ROWS per-row maxima (t <= 4096).
+static __device__ __align__(256) float g_noalloc_scratch[WP_NOALLOC_MAX_ELEMS + WP_NOALLOC_MAX_ROWS];
+
+// Device address of g_noalloc_scratch per device.  In host code the array's name is only a
+// host-side stand-in, so the address is looked up with cudaGetSymbolAddress once per device,
+// with that device current.
+static std::mutex g_noalloc_mu;
+static float* g_noalloc_addr[64] = {};
+
+static int noalloc_scratch(float** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -23;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      fprintf(stderr, "[wasr] wp_gemm_q_noalloc: cudaGetSymbolAddress failed: %s\n", cudaGetErrorString(e));
+      cudaGetLastError();
+      return -23;
+    }
+    g_noalloc_addr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_addr[dev];
+  return 0;
+}
+
+extern "C" {
+
+int wp_gemm_q_noalloc(WpCtx* c, const int8_t* xq, const float* xs, int t, int k, size_t w_off, int n, float ws,
+                      const float* bias_dev, void* stream, int8_t* out_q, float* out_s) {
+  if (!c || !xq || !xs || !out_q || !out_s) return -1;
+  if (t <= 0 || k <= 0 || n <= 0) return 0;
+  if (static_cast<size_t>(n) * static_cast<size_t>(k) > c->w_bytes ||
+      w_off > c->w_bytes - static_cast<size_t>(n) * static_cast<size_t>(k))
+    return -2;
+  if (t > WP_NOALLOC_MAX_ROWS || static_cast<size_t>(t) * static_cast<size_t>(n) > WP_NOALLOC_MAX_ELEMS) {
+    fprintf(stderr,
+            "[wasr] wp_gemm_q_noalloc: t=%d, n=%d exceeds the static scratch (t <= %d, t*n <= %d); "
+            "use wp_gemm_q\n",
+            t, n, WP_NOALLOC_MAX_ROWS, WP_NOALLOC_MAX_ELEMS);
+    return -22;
+  }
+  float* scratch = nullptr;
+  if (const int rc = noalloc_scratch(&scratch)) return rc;
+  unsigned* rowmax = reinterpret_cast<unsigned*>(scratch + WP_NOALLOC_MAX_ELEMS);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  std::lock_guard<std::mutex> lock(c->mu);
+  // the array keeps the previous call's values: the row maxima must start from zero
+  if (cudaMemsetAsync(rowmax, 0, static_cast<size_t>(t) * sizeof(unsigned), st) != cudaSuccess) return -4;
+  GemmArgs g{};
+  g.a = xq;
+  g.b = reinterpret_cast<const int8_t*>(c->w + w_off);
+  g.M = t;
+  g.N = n;
+  g.K = k;
+  g.n_store = n;
+  g.xs = xs;
+  g.ws = ws;
+  g.bias = bias_dev;
+  g.ldo = n;
+  g.err = c->err_dev;
+  g.out = scratch;
+  g.rowmax = rowmax;
+  g.epi = EPI_F32_ROWMAX;
+  const int rc = gemm_run(g, st);
+  if (rc) return rc;
+  return launch_quant_rows_max(scratch, t, n, rowmax, out_q, out_s, st);
+}
+
 int wp_quant_rows(const float* y, int t, int n, void* stream, int8_t* out_q, float* out_s) {
   if (!y || !out_q || !out_s) return -1;
   if (t <= 0 || n <= 0) return 0;
