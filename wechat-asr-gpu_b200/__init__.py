@@ -14,7 +14,7 @@ that ABI:
 
 There is no CPU fallback anywhere on this path: if the library is missing, loading fails.
 """
-from . import abi, synth  # noqa: F401
+from . import abi, dist, synth  # noqa: F401
 from .host import Engine, Gpu, WindowModel, fbank, ctc_collapse  # noqa: F401
 
-__all__ = ["abi", "synth", "Engine", "Gpu", "WindowModel", "fbank", "ctc_collapse"]
+__all__ = ["abi", "dist", "synth", "Engine", "Gpu", "WindowModel", "fbank", "ctc_collapse"]
