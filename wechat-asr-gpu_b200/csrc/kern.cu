@@ -4,8 +4,9 @@
 // Bit-exactness: the conv frontend, LayerNorm and quantisation reproduce the CPU path's
 // operation order (src/kernels.rs dotf / quant, src/model.rs norm / frontend) with
 // explicitly rounded intrinsics, so their outputs equal the CPU's bit for bit.  Attention
-// keeps the CPU's order too (8-lane dot, sequential softmax sum, sequential PV sum); only
-// expf/tanhf may differ from glibc in the last place.
+// keeps the CPU's order too (8-lane dot, sequential softmax sum, sequential PV sum), and the
+// softmax exp and the GELU tanh are restatements of glibc's algorithms (common.cuh), so they
+// are bit-exact as well.
 #include <cstdio>
 #include <mutex>
 #include <set>
@@ -58,136 +59,188 @@ __global__ void __launch_bounds__(128) conv1_k(const float* __restrict__ x, cons
   }
 }
 
-// ------------------------------------------------------------------------ conv2
-// y2[r][o][f] = relu(dotf(c2[o], patch)) with patch[c*49+i*7+j] = y1[5r+i-1][c][f+j-3]
-// (src/model.rs:420-444); column 40 is 0.  Block = (row r, 16 output channels); thread =
-// (4 channels, one f).  dotf lane of tap idx = idx % 8 = (c + 7i + j) % 8 (49 = 1 mod 8), so
-// unrolling 8 channels makes every lane index a compile-time constant.  Input channels are
-// staged 8 at a time (in increasing order, so every lane still sees its taps in order), which
-// keeps shared memory at 35 KB per block and lets 5-6 blocks share an SM.
-constexpr int CV2_OG = 16;
-constexpr int CV2_PAD = 46;  // 40 + 3 + 3 zero columns
-constexpr int CV2_CC = 8;    // input channels per stage
-constexpr int CV2_SMEM = (7 * CV2_CC * CV2_PAD + CV2_CC * 49 * CV2_OG) * 4;
+// ------------------------------------------------------------------------ conv2 / conv3
+// Both are dotf products of a weight row with a zero-padded patch (src/kernels.rs dotf: 8
+// lane accumulators, lane l takes taps l, l+8, l+16, ... in order, then the lanes are folded
+// l0 + l1 + ... + l7).  For conv2 and conv3 the patch length (1568, 576) is a multiple of 8,
+// and the lane of tap idx = c*49 + i*7 + j (conv2) or c*9 + i*3 + j (conv3) is (c + rest) % 8
+// because 49 = 9 = 1 mod 8.
+//
+// Lane-pair layout.  Taps 2m and 2m+1 land in lanes (2q, 2q+1) for one q in 0..3, so the
+// 256 threads of a block form 4 groups, group q accumulating lanes 2q and 2q+1 of every
+// output it owns as one float2.  For a tap pair the two weights are adjacent in memory and
+// the two inputs are staged interleaved (X2[m][f] = (patch[2m](f), patch[2m+1](f))), so a
+// product pair is one packed multiply of two register pairs and the accumulate one packed
+// add -- every element still rounds exactly like the scalar sequence.  A thread owns
+// 5 positions x 4 output channels (40 accumulator registers).  After the last stage the
+// partial lanes go through shared memory and are folded in lane order.
+constexpr int TP_THREADS = 256;
+constexpr int TP_P = 5, TP_C = 4;  // positions x channels per thread
 
-__global__ void __launch_bounds__(160) conv2_k(const float* __restrict__ y1, const float* __restrict__ c2, Segs s,
-                                               float* __restrict__ y2) {
-  extern __shared__ float sm[];
-  float* xin = sm;                              // [7][8][46]
-  float* wsm = sm + 7 * CV2_CC * CV2_PAD;       // [392][16]
-  const int r = blockIdx.x, og = blockIdx.y;
+constexpr int CV2_CH = 32;                 // output channels per block
+constexpr int CV2_CC = 4;                  // input channels per stage
+constexpr int CV2_MP = CV2_CC * 49 / 2;    // tap pairs per stage (98)
+constexpr int CV2_WS = CV2_CH + 2;         // W2 row stride in float2 (16-byte rows, 4-way staging stores)
+constexpr int cmax(int a, int b) { return a > b ? a : b; }
+constexpr int CV2_SMEM = cmax(CV2_MP * (DIM + CV2_WS) * 8, 4 * CV2_CH * DIM * 8);
+
+constexpr int CV3_CH = 64;
+constexpr int CV3_CC = 8;
+constexpr int CV3_MP = CV3_CC * 9 / 2;     // 36
+constexpr int CV3_WS = CV3_CH + 2;
+constexpr int CV3_SMEM = cmax(CV3_MP * (20 + CV3_WS) * 8, 4 * CV3_CH * 20 * 8);
+
+__device__ __forceinline__ float2 mulp(float2 a, float2 b) {
+  return make_float2(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y));
+}
+
+// acc[p][c] += X2[m][f0+p] * W2[m][o0+c] for this group's tap pairs m = m0, m0+4, ... < mp
+template <int XS, int WS, int UNROLL>
+__device__ __forceinline__ void tp_accumulate(const float2* __restrict__ X2, const float2* __restrict__ W2, int mp,
+                                              int m0, int f0, int o0, float2 (&acc)[TP_P][TP_C]) {
+#pragma unroll UNROLL
+  for (int m = m0; m < mp; m += 4) {
+    const float2* xr = X2 + m * XS + f0;
+    const float4* wr = reinterpret_cast<const float4*>(W2 + m * WS + o0);
+    float2 xv[TP_P];
+#pragma unroll
+    for (int p = 0; p < TP_P; p++) xv[p] = xr[p];
+    const float4 wa = wr[0], wb = wr[1];
+    const float2 wv[TP_C] = {make_float2(wa.x, wa.y), make_float2(wa.z, wa.w), make_float2(wb.x, wb.y),
+                             make_float2(wb.z, wb.w)};
+#pragma unroll
+    for (int p = 0; p < TP_P; p++)
+#pragma unroll
+      for (int c = 0; c < TP_C; c++) acc[p][c] = add2_rn(acc[p][c], mulp(xv[p], wv[c]));
+  }
+}
+
+// Fold the 4 groups' lane pairs of output (o, f) in lane order; part = [4][nch][npos].
+__device__ __forceinline__ float tp_fold(const float2* part, int nch, int npos, int o, int f) {
+  const float2 a0 = part[(0 * nch + o) * npos + f], a1 = part[(1 * nch + o) * npos + f];
+  const float2 a2 = part[(2 * nch + o) * npos + f], a3 = part[(3 * nch + o) * npos + f];
+  float s = __fadd_rn(a0.x, a0.y);
+  s = __fadd_rn(s, a1.x);
+  s = __fadd_rn(s, a1.y);
+  s = __fadd_rn(s, a2.x);
+  s = __fadd_rn(s, a2.y);
+  s = __fadd_rn(s, a3.x);
+  return __fadd_rn(s, a3.y);
+}
+
+// y2[r][o][f] = relu(dotf(c2[o], patch)), patch[c*49+i*7+j] = y1[5r+i-1][c][f+j-3] (zero
+// outside the segment / the 40 columns), column 40 = 0 -- src/model.rs:420-444.
+// Block = (row r, 32 output channels); stages of 4 input channels.
+__global__ void __launch_bounds__(TP_THREADS, 3) conv2_k(const float* __restrict__ y1, const float* __restrict__ c2,
+                                                      Segs s, float* __restrict__ y2) {
+  extern __shared__ __align__(16) float sm[];
+  float2* X2 = reinterpret_cast<float2*>(sm);    // [98][40]
+  float2* Wt = X2 + CV2_MP * DIM;                 // [98][34]
+  const int r = blockIdx.x, og = blockIdx.y, tid = threadIdx.x;
   const int sw = s.seg_of_row(r);
   const int fb = s.frame_begin(sw), t = s.frames(sw), ti = r - s.row_begin(sw);
-  const int f = threadIdx.x % DIM, sub = threadIdx.x / DIM;  // 40 x 4 threads
-  float2 a01[8], a23[8];
+  const int q = tid >> 6, idx = tid & 63;
+  const int f0 = (idx & 7) * TP_P, o0 = (idx >> 3) * TP_C;
+  float2 acc[TP_P][TP_C];
 #pragma unroll
-  for (int l = 0; l < 8; l++) a01[l] = a23[l] = make_float2(0.0f, 0.0f);
+  for (int p = 0; p < TP_P; p++)
+#pragma unroll
+    for (int c = 0; c < TP_C; c++) acc[p][c] = make_float2(0.0f, 0.0f);
 #pragma unroll 1
   for (int c0 = 0; c0 < C1; c0 += CV2_CC) {
     __syncthreads();
-    for (int e = threadIdx.x; e < CV2_CC * 49 * CV2_OG; e += blockDim.x) {
-      const int ol = e & (CV2_OG - 1), li = e >> 4;
-      wsm[e] = c2[static_cast<int64_t>(og * CV2_OG + ol) * K2 + c0 * 49 + li];
+#pragma unroll 1
+    for (int e = tid; e < CV2_MP * CV2_CH; e += TP_THREADS) {
+      const int o = e / CV2_MP, m = e - o * CV2_MP;
+      const float* w = c2 + static_cast<int64_t>(og * CV2_CH + o) * K2 + c0 * 49 + 2 * m;
+      Wt[m * CV2_WS + o] = make_float2(__ldg(w), __ldg(w + 1));
     }
-    for (int e = threadIdx.x; e < 7 * CV2_CC * CV2_PAD; e += blockDim.x) {
-      const int fp = e % CV2_PAD, cc = (e / CV2_PAD) % CV2_CC, i = e / (CV2_PAD * CV2_CC);
-      const int tt = ti * 5 + i - 1, ff = fp - 3;
-      xin[e] = (tt >= 0 && tt < t && ff >= 0 && ff < DIM)
-                   ? y1[static_cast<int64_t>(fb + tt) * (C1 * DIM) + (c0 + cc) * DIM + ff]
+#pragma unroll 1
+    for (int e = tid; e < CV2_MP * DIM; e += TP_THREADS) {
+      const int m = e / DIM, f = e - m * DIM;
+      float v[2];
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int tp = 2 * m + h, cl = tp / 49, rem = tp - cl * 49, i = rem / 7, j = rem - i * 7;
+        const int tt = ti * 5 + i - 1, ff = f + j - 3;
+        v[h] = (tt >= 0 && tt < t && ff >= 0 && ff < DIM)
+                   ? __ldg(y1 + static_cast<int64_t>(fb + tt) * (C1 * DIM) + (c0 + cl) * DIM + ff)
                    : 0.0f;
+      }
+      X2[e] = make_float2(v[0], v[1]);
     }
     __syncthreads();
-#pragma unroll
-    for (int cc = 0; cc < CV2_CC; cc++)
-#pragma unroll
-      for (int i = 0; i < 7; i++)
-#pragma unroll
-        for (int j = 0; j < 7; j++) {
-          const int l = (cc + 7 * i + j) & 7;
-          const float xv = xin[(i * CV2_CC + cc) * CV2_PAD + f + j];
-          const float4 w4 = *reinterpret_cast<const float4*>(wsm + (cc * 49 + i * 7 + j) * CV2_OG + sub * 4);
-          a01[l].x = __fadd_rn(a01[l].x, __fmul_rn(w4.x, xv));
-          a01[l].y = __fadd_rn(a01[l].y, __fmul_rn(w4.y, xv));
-          a23[l].x = __fadd_rn(a23[l].x, __fmul_rn(w4.z, xv));
-          a23[l].y = __fadd_rn(a23[l].y, __fmul_rn(w4.w, xv));
-        }
+    tp_accumulate<DIM, CV2_WS, 2>(X2, Wt, CV2_MP, (q - (c0 >> 1)) & 3, f0, o0, acc);
   }
-  float* out = y2 + static_cast<int64_t>(r) * (C2 * W2);
-  float2 s01 = a01[0], s23 = a23[0];
+  __syncthreads();
+  float2* part = reinterpret_cast<float2*>(sm);  // [4][32][40]
 #pragma unroll
-  for (int l = 1; l < 8; l++) {
-    s01 = make_float2(__fadd_rn(s01.x, a01[l].x), __fadd_rn(s01.y, a01[l].y));
-    s23 = make_float2(__fadd_rn(s23.x, a23[l].x), __fadd_rn(s23.y, a23[l].y));
+  for (int p = 0; p < TP_P; p++)
+#pragma unroll
+    for (int c = 0; c < TP_C; c++) part[(q * CV2_CH + o0 + c) * DIM + f0 + p] = acc[p][c];
+  __syncthreads();
+  float* out = y2 + static_cast<int64_t>(r) * (C2 * W2) + og * CV2_CH * W2;
+  for (int e = tid; e < CV2_CH * DIM; e += TP_THREADS) {
+    const int o = e / DIM, f = e - o * DIM;
+    out[o * W2 + f] = fmaxf(tp_fold(part, CV2_CH, DIM, o, f), 0.0f);
   }
-  const int ob = og * CV2_OG + sub * 4;
-  out[(ob + 0) * W2 + f] = fmaxf(s01.x, 0.0f);
-  out[(ob + 1) * W2 + f] = fmaxf(s01.y, 0.0f);
-  out[(ob + 2) * W2 + f] = fmaxf(s23.x, 0.0f);
-  out[(ob + 3) * W2 + f] = fmaxf(s23.y, 0.0f);
-  if (threadIdx.x < CV2_OG) out[(og * CV2_OG + threadIdx.x) * W2 + DIM] = 0.0f;
+  if (tid < CV2_CH) out[tid * W2 + DIM] = 0.0f;
 }
 
-// ------------------------------------------------------------------------ conv3
-// y3[r][o*20+f] = relu(dotf(c3[o], patch)) with patch[c*9+i*3+j] = y2[r+i-1][c][2f+j]
-// (src/model.rs:446-468).  Lane of tap idx = (c + 3i + j) % 8 (9 = 1 mod 8).  Input channels
-// are staged 8 at a time in increasing order (13 KB of shared memory per block).
-constexpr int CV3_OG = 32;
-constexpr int CV3_CC = 8;
-constexpr int CV3_SMEM = (3 * CV3_CC * W2 + CV3_CC * 9 * CV3_OG) * 4;
-
-__global__ void __launch_bounds__(160) conv3_k(const float* __restrict__ y2, const float* __restrict__ c3, Segs s,
-                                               float* __restrict__ y3) {
-  extern __shared__ float sm[];
-  float* xin = sm;                    // [3][8][41]
-  float* wsm = sm + 3 * CV3_CC * W2;  // [72][32]
-  const int r = blockIdx.x, og = blockIdx.y;
+// y3[r][o*20+f] = relu(dotf(c3[o], patch)), patch[c*9+i*3+j] = y2[r+i-1][c][2f+j] (zero
+// outside the segment) -- src/model.rs:446-468.  Block = (row r, 64 output channels);
+// stages of 8 input channels.
+__global__ void __launch_bounds__(TP_THREADS, 3) conv3_k(const float* __restrict__ y2, const float* __restrict__ c3,
+                                                      Segs s, float* __restrict__ y3) {
+  extern __shared__ __align__(16) float sm[];
+  float2* X2 = reinterpret_cast<float2*>(sm);    // [36][20]
+  float2* Wt = X2 + CV3_MP * 20;                  // [36][66]
+  const int r = blockIdx.x, og = blockIdx.y, tid = threadIdx.x;
   const int sw = s.seg_of_row(r);
   const int rb = s.row_begin(sw), t1 = s.rows(sw), ti = r - rb;
-  const int f = threadIdx.x % 20, sub = threadIdx.x / 20;  // 20 x 8 threads
-  float2 a01[8], a23[8];
+  const int q = tid >> 6, idx = tid & 63;
+  const int f0 = (idx & 3) * TP_P, o0 = (idx >> 2) * TP_C;
+  float2 acc[TP_P][TP_C];
 #pragma unroll
-  for (int l = 0; l < 8; l++) a01[l] = a23[l] = make_float2(0.0f, 0.0f);
+  for (int p = 0; p < TP_P; p++)
+#pragma unroll
+    for (int c = 0; c < TP_C; c++) acc[p][c] = make_float2(0.0f, 0.0f);
 #pragma unroll 1
   for (int c0 = 0; c0 < C2; c0 += CV3_CC) {
     __syncthreads();
-    for (int e = threadIdx.x; e < CV3_CC * 9 * CV3_OG; e += blockDim.x) {
-      const int ol = e & (CV3_OG - 1), li = e >> 5;
-      wsm[e] = c3[static_cast<int64_t>(og * CV3_OG + ol) * K3 + c0 * 9 + li];
+#pragma unroll 1
+    for (int e = tid; e < CV3_MP * CV3_CH; e += TP_THREADS) {
+      const int o = e / CV3_MP, m = e - o * CV3_MP;
+      const float* w = c3 + static_cast<int64_t>(og * CV3_CH + o) * K3 + c0 * 9 + 2 * m;
+      Wt[m * CV3_WS + o] = make_float2(__ldg(w), __ldg(w + 1));
     }
-    for (int e = threadIdx.x; e < 3 * CV3_CC * W2; e += blockDim.x) {
-      const int i = e / (CV3_CC * W2), rem = e - i * (CV3_CC * W2);
-      const int cc = rem / W2, col = rem - cc * W2;
-      const int tt = ti + i - 1;
-      xin[e] = (tt >= 0 && tt < t1) ? y2[static_cast<int64_t>(rb + tt) * (C2 * W2) + (c0 + cc) * W2 + col] : 0.0f;
+    for (int e = tid; e < CV3_MP * 20; e += TP_THREADS) {
+      const int m = e / 20, f = e - m * 20;
+      float v[2];
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int tp = 2 * m + h, cl = tp / 9, rem = tp - cl * 9, i = rem / 3, j = rem - i * 3;
+        const int tt = ti + i - 1;
+        v[h] = (tt >= 0 && tt < t1) ? __ldg(y2 + static_cast<int64_t>(rb + tt) * (C2 * W2) + (c0 + cl) * W2 + 2 * f + j)
+                                    : 0.0f;
+      }
+      X2[e] = make_float2(v[0], v[1]);
     }
     __syncthreads();
-#pragma unroll
-    for (int cc = 0; cc < CV3_CC; cc++)
-#pragma unroll
-      for (int i = 0; i < 3; i++)
-#pragma unroll
-        for (int j = 0; j < 3; j++) {
-          const int l = (cc + 3 * i + j) & 7;
-          const float xv = xin[(i * CV3_CC + cc) * W2 + 2 * f + j];
-          const float4 w4 = *reinterpret_cast<const float4*>(wsm + (cc * 9 + i * 3 + j) * CV3_OG + sub * 4);
-          a01[l].x = __fadd_rn(a01[l].x, __fmul_rn(w4.x, xv));
-          a01[l].y = __fadd_rn(a01[l].y, __fmul_rn(w4.y, xv));
-          a23[l].x = __fadd_rn(a23[l].x, __fmul_rn(w4.z, xv));
-          a23[l].y = __fadd_rn(a23[l].y, __fmul_rn(w4.w, xv));
-        }
+    tp_accumulate<20, CV3_WS, 1>(X2, Wt, CV3_MP, (q - (c0 >> 1)) & 3, f0, o0, acc);
   }
-  float* out = y3 + static_cast<int64_t>(r) * FLAT;
-  float2 s01 = a01[0], s23 = a23[0];
+  __syncthreads();
+  float2* part = reinterpret_cast<float2*>(sm);  // [4][64][20]
 #pragma unroll
-  for (int l = 1; l < 8; l++) {
-    s01 = make_float2(__fadd_rn(s01.x, a01[l].x), __fadd_rn(s01.y, a01[l].y));
-    s23 = make_float2(__fadd_rn(s23.x, a23[l].x), __fadd_rn(s23.y, a23[l].y));
+  for (int p = 0; p < TP_P; p++)
+#pragma unroll
+    for (int c = 0; c < TP_C; c++) part[(q * CV3_CH + o0 + c) * 20 + f0 + p] = acc[p][c];
+  __syncthreads();
+  float* out = y3 + static_cast<int64_t>(r) * FLAT + og * CV3_CH * 20;
+  for (int e = tid; e < CV3_CH * 20; e += TP_THREADS) {
+    const int o = e / 20, f = e - o * 20;
+    out[o * 20 + f] = fmaxf(tp_fold(part, CV3_CH, 20, o, f), 0.0f);
   }
-  const int ob = og * CV3_OG + sub * 4;
-  out[(ob + 0) * 20 + f] = fmaxf(s01.x, 0.0f);
-  out[(ob + 1) * 20 + f] = fmaxf(s01.y, 0.0f);
-  out[(ob + 2) * 20 + f] = fmaxf(s23.x, 0.0f);
-  out[(ob + 3) * 20 + f] = fmaxf(s23.y, 0.0f);
 }
 
 // ------------------------------------------------------------------------ quant
@@ -459,14 +512,16 @@ __global__ void keys_to_ids_k(const unsigned long long* __restrict__ keys, int m
 }
 
 // ------------------------------------------------------------------------ attention
-// One block per (segment, 32-query tile, head).  Scores s_ij = dotf(q_i, k_j) * 0.125 with the
+// One block per (segment, 64-query tile, head).  Scores s_ij = dotf(q_i, k_j) * 0.125 with the
 // 8-lane order of src/kernels.rs:172-183; softmax with e_j = exp(s_j - max) and the row sum z
 // folded sequentially (src/model.rs:723-728); p_j = e_j / z; o_i[d] = sum_j p_j v_j[d] folded
 // over j in order (src/model.rs:729-735).  The score tile stays in shared memory.
 //
-// Every output element keeps the CPU's exact sequence of rounded multiplies and adds; the
-// speed comes from register blocking: a thread owns 2 query rows x 4 keys for the scores and
-// 2 query rows x 4 head dims for PV, so each shared-memory load feeds several products.
+// Every output element keeps the CPU's exact sequence of rounded multiplies and adds.  The
+// speed comes from register blocking: a thread owns 4 query rows x 4 keys for the scores and
+// 4 query rows x 4 head dims for PV (16 independent chains, ~6 shared loads per 32 FP ops),
+// from prefetching the next 64-key K/V chunk into registers while the current one is used, and
+// from warps whose query rows all lie past the end of a short tile skipping the math.
 // Shared layout: Q and S hold query rows in interleaved pairs (float2 = rows 2p, 2p+1).
 constexpr int ATT_KVS = HD + 1;  // padded K-chunk row
 
@@ -482,16 +537,27 @@ __device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
 __device__ __forceinline__ float2 pmul(float2 a, float2 b) { return make_float2(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y)); }
 __device__ __forceinline__ float2 padd(float2 a, float2 b) { return make_float2(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y)); }
 
+// one 64-key chunk of K or V rows [j0, j0+nj) of head h: 4 float4 per thread (zeros past nj)
+__device__ __forceinline__ void att_fetch(const float* __restrict__ src, int ld, int rb, int j0, int nj, int h,
+                                          int tid, float4 (&r)[4]) {
+#pragma unroll
+  for (int u = 0; u < 4; u++) {
+    const int e = tid + 256 * u, j = e >> 4, d4 = (e & 15) * 4;
+    r[u] = j < nj ? __ldg(reinterpret_cast<const float4*>(src + static_cast<int64_t>(rb + j0 + j) * ld + h * HD + d4))
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
 __global__ void __launch_bounds__(256) attn_k(const float* __restrict__ q, const float* __restrict__ k,
                                               const float* __restrict__ v, int ld, Segs s,
                                               const int* __restrict__ toff, int max_t1, float* __restrict__ out,
                                               int ldo) {
   extern __shared__ float sm[];
   const int sp = att_pair_stride(max_t1);
-  float2* Q2 = reinterpret_cast<float2*>(sm);          // [16][64] query row pairs
-  float* KV = sm + ATT_QT / 2 * HD * 2;                 // [64][65] K chunk / [64][64] V chunk
-  float2* S2 = reinterpret_cast<float2*>(KV + 64 * ATT_KVS);  // [16][sp] score row pairs
-  float* Z = reinterpret_cast<float*>(S2 + ATT_QT / 2 * sp);  // [32] row sums
+  float2* Q2 = reinterpret_cast<float2*>(sm);                 // [32][64] query row pairs
+  float* KV = sm + ATT_QT / 2 * HD * 2;                        // [64][65] K chunk / [64][64] V chunk
+  float2* S2 = reinterpret_cast<float2*>(KV + 64 * ATT_KVS);   // [32][sp] score row pairs
+  float* Z = reinterpret_cast<float*>(S2 + ATT_QT / 2 * sp);   // [64] row sums
   const int tile = blockIdx.x, h = blockIdx.y;
   int sw = 0;
   if (toff) {
@@ -513,45 +579,59 @@ __global__ void __launch_bounds__(256) attn_k(const float* __restrict__ q, const
     const int i = e >> 6, d = e & 63;
     Qf[((i >> 1) * HD + d) * 2 + (i & 1)] = i < ni ? q[static_cast<int64_t>(rb + i0 + i) * ld + h * HD + d] : 0.0f;
   }
-  const int ip = tid >> 4;  // query row pair (rows 2ip, 2ip+1)
-  // ---- scores: thread = row pair ip x keys jq, jq+16, jq+32, jq+48 of each 64-key chunk
-  {
-    const int jq = tid & 15;
-    for (int j0 = 0; j0 < t; j0 += 64) {
-      const int nj = min(64, t - j0);
-      __syncthreads();
-      for (int e = tid; e < 64 * (HD / 4); e += 256) {
-        const int j = e >> 4, d4 = (e & 15) * 4;
-        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (j < nj) x = *reinterpret_cast<const float4*>(k + static_cast<int64_t>(rb + j0 + j) * ld + h * HD + d4);
-        float* dst = KV + j * ATT_KVS + d4;
-        dst[0] = x.x; dst[1] = x.y; dst[2] = x.z; dst[3] = x.w;
-      }
-      __syncthreads();
-      float2 sc[4];
+  const int ig = tid >> 4;            // query rows 4ig..4ig+3 = pairs 2ig, 2ig+1
+  const int sub = tid & 15;           // keys sub+16u (scores) / head dims 4sub..4sub+3 (PV)
+  const bool rows_live = 4 * ig < ni;  // uniform over each half-warp
+  const int nchunks = (t + 63) / 64;
+  // ---- scores
+  float4 pre[4];
+  att_fetch(k, ld, rb, 0, min(64, t), h, tid, pre);
+  for (int ch = 0; ch < nchunks; ch++) {
+    const int j0 = ch * 64, nj = min(64, t - j0);
+    __syncthreads();  // previous chunk fully consumed
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int e = tid + 256 * u, j = e >> 4, d4 = (e & 15) * 4;
+      float* dst = KV + j * ATT_KVS + d4;
+      dst[0] = pre[u].x; dst[1] = pre[u].y; dst[2] = pre[u].z; dst[3] = pre[u].w;
+    }
+    if (ch + 1 < nchunks) att_fetch(k, ld, rb, j0 + 64, min(64, t - j0 - 64), h, tid, pre);
+    __syncthreads();
+    if (rows_live) {
+      float2 sc[2][4];
 #pragma unroll
       for (int l = 0; l < 8; l++) {
-        float2 acc[4];
+        float2 acc[2][4];
 #pragma unroll
         for (int c = 0; c < 8; c++) {
           const int d = 8 * c + l;
-          const float2 qv = Q2[ip * HD + d];
+          const float2 qa = Q2[(2 * ig) * HD + d], qb = Q2[(2 * ig + 1) * HD + d];
 #pragma unroll
           for (int u = 0; u < 4; u++) {
-            const float2 p = pmul(qv, f2(KV[(jq + 16 * u) * ATT_KVS + d]));
-            acc[u] = c == 0 ? p : padd(acc[u], p);
+            const float kv = KV[(sub + 16 * u) * ATT_KVS + d];
+            const float2 pa = pmul(qa, f2(kv)), pb = pmul(qb, f2(kv));
+            acc[0][u] = c == 0 ? pa : padd(acc[0][u], pa);
+            acc[1][u] = c == 0 ? pb : padd(acc[1][u], pb);
           }
         }
 #pragma unroll
-        for (int u = 0; u < 4; u++) sc[u] = l == 0 ? acc[u] : padd(sc[u], acc[u]);
+        for (int u = 0; u < 4; u++) {
+          sc[0][u] = l == 0 ? acc[0][u] : padd(sc[0][u], acc[0][u]);
+          sc[1][u] = l == 0 ? acc[1][u] : padd(sc[1][u], acc[1][u]);
+        }
       }
 #pragma unroll
       for (int u = 0; u < 4; u++) {
-        const int j = jq + 16 * u;
-        if (j < nj) S2[ip * sp + j0 + j] = pmul(sc[u], f2(0.125f));
+        const int j = sub + 16 * u;
+        if (j < nj) {
+          S2[(2 * ig) * sp + j0 + j] = pmul(sc[0][u], f2(0.125f));
+          S2[(2 * ig + 1) * sp + j0 + j] = pmul(sc[1][u], f2(0.125f));
+        }
       }
     }
   }
+  // prefetch the first V chunk while the softmax runs
+  att_fetch(v, ld, rb, 0, min(64, t), h, tid, pre);
   __syncthreads();
   // ---- softmax: row max (order-free, warp per row), exp (element-wise), sequential row sum
   float* Sf = reinterpret_cast<float*>(S2);
@@ -576,39 +656,48 @@ __global__ void __launch_bounds__(256) attn_k(const float* __restrict__ q, const
     float* x = Sf + (i >> 1) * sp * 2 + (i & 1) + 2 * j;
     *x = __fdiv_rn(*x, Z[i]);
   }
-  // ---- PV: thread = row pair ip x head dims 4dq..4dq+3; sum over keys in order
-  const int dq = tid & 15;
-  float2 o[4];
+  // ---- PV: thread = query rows 4ig..4ig+3 x head dims 4sub..4sub+3; keys summed in order
+  float2 o[2][4];
 #pragma unroll
-  for (int u = 0; u < 4; u++) o[u] = make_float2(0.0f, 0.0f);
-  for (int j0 = 0; j0 < t; j0 += 64) {
-    const int nj = min(64, t - j0);
+  for (int u = 0; u < 4; u++) o[0][u] = o[1][u] = make_float2(0.0f, 0.0f);
+  for (int ch = 0; ch < nchunks; ch++) {
+    const int j0 = ch * 64, nj = min(64, t - j0);
     __syncthreads();
-    for (int e = tid; e < 64 * (HD / 4); e += 256) {
-      const int j = e >> 4, d4 = (e & 15) * 4;
-      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (j < nj) x = *reinterpret_cast<const float4*>(v + static_cast<int64_t>(rb + j0 + j) * ld + h * HD + d4);
-      *reinterpret_cast<float4*>(KV + j * HD + d4) = x;
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int e = tid + 256 * u, j = e >> 4, d4 = (e & 15) * 4;
+      *reinterpret_cast<float4*>(KV + j * HD + d4) = pre[u];
     }
+    if (ch + 1 < nchunks) att_fetch(v, ld, rb, j0 + 64, min(64, t - j0 - 64), h, tid, pre);
     __syncthreads();
-    const float2* prow = S2 + ip * sp + j0;
+    if (rows_live) {
+      const float2* pa_row = S2 + (2 * ig) * sp + j0;
+      const float2* pb_row = S2 + (2 * ig + 1) * sp + j0;
 #pragma unroll 4
-    for (int jj = 0; jj < nj; jj++) {
-      const float2 p = prow[jj];
-      const float4 vv = *reinterpret_cast<const float4*>(KV + jj * HD + 4 * dq);
-      o[0] = padd(o[0], pmul(p, f2(vv.x)));
-      o[1] = padd(o[1], pmul(p, f2(vv.y)));
-      o[2] = padd(o[2], pmul(p, f2(vv.z)));
-      o[3] = padd(o[3], pmul(p, f2(vv.w)));
+      for (int jj = 0; jj < nj; jj++) {
+        const float2 pa = pa_row[jj], pb = pb_row[jj];
+        const float4 vv = *reinterpret_cast<const float4*>(KV + jj * HD + 4 * sub);
+        o[0][0] = padd(o[0][0], pmul(pa, f2(vv.x)));
+        o[0][1] = padd(o[0][1], pmul(pa, f2(vv.y)));
+        o[0][2] = padd(o[0][2], pmul(pa, f2(vv.z)));
+        o[0][3] = padd(o[0][3], pmul(pa, f2(vv.w)));
+        o[1][0] = padd(o[1][0], pmul(pb, f2(vv.x)));
+        o[1][1] = padd(o[1][1], pmul(pb, f2(vv.y)));
+        o[1][2] = padd(o[1][2], pmul(pb, f2(vv.z)));
+        o[1][3] = padd(o[1][3], pmul(pb, f2(vv.w)));
+      }
     }
   }
-  const int r0 = 2 * ip;
-  if (r0 < ni)
-    *reinterpret_cast<float4*>(out + static_cast<int64_t>(rb + i0 + r0) * ldo + h * HD + 4 * dq) =
-        make_float4(o[0].x, o[1].x, o[2].x, o[3].x);
-  if (r0 + 1 < ni)
-    *reinterpret_cast<float4*>(out + static_cast<int64_t>(rb + i0 + r0 + 1) * ldo + h * HD + 4 * dq) =
-        make_float4(o[0].y, o[1].y, o[2].y, o[3].y);
+#pragma unroll
+  for (int pr = 0; pr < 2; pr++) {
+    const int r0 = 4 * ig + 2 * pr;
+    if (r0 < ni)
+      *reinterpret_cast<float4*>(out + static_cast<int64_t>(rb + i0 + r0) * ldo + h * HD + 4 * sub) =
+          make_float4(o[pr][0].x, o[pr][1].x, o[pr][2].x, o[pr][3].x);
+    if (r0 + 1 < ni)
+      *reinterpret_cast<float4*>(out + static_cast<int64_t>(rb + i0 + r0 + 1) * ldo + h * HD + 4 * sub) =
+          make_float4(o[pr][0].y, o[pr][1].y, o[pr][2].y, o[pr][3].y);
+  }
 }
 
 __global__ void eval_math_k(int fn, const float* __restrict__ x, float* __restrict__ y, int n) {
@@ -651,13 +740,13 @@ int launch_conv1(const float* x, const float* c1, Segs s, int total_frames, floa
 int launch_conv2(const float* y1, const float* c2, Segs s, int total_rows, float* y2, cudaStream_t st) {
   if (total_rows <= 0) return 0;
   set_smem(reinterpret_cast<const void*>(conv2_k), CV2_SMEM);
-  conv2_k<<<dim3(total_rows, C2 / CV2_OG), 160, CV2_SMEM, st>>>(y1, c2, s, y2);
+  conv2_k<<<dim3(total_rows, C2 / CV2_CH), TP_THREADS, CV2_SMEM, st>>>(y1, c2, s, y2);
   return launched();
 }
 int launch_conv3(const float* y2, const float* c3, Segs s, int total_rows, float* y3, cudaStream_t st) {
   if (total_rows <= 0) return 0;
   set_smem(reinterpret_cast<const void*>(conv3_k), CV3_SMEM);
-  conv3_k<<<dim3(total_rows, C3 / CV3_OG), 160, CV3_SMEM, st>>>(y2, c3, s, y3);
+  conv3_k<<<dim3(total_rows, C3 / CV3_CH), TP_THREADS, CV3_SMEM, st>>>(y2, c3, s, y3);
   return launched();
 }
 int launch_quant_rows(const float* x, int m, int k, int ldx, int8_t* xq, float* xs, cudaStream_t st) {

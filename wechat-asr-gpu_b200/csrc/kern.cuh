@@ -60,7 +60,7 @@ int launch_keys_to_ids(const unsigned long long* keys, int m, uint32_t* ids, cud
 // attention over segments; q/k/v rows of stride ld floats (head h at column h*64).
 // toff: [n+1] prefix of per-segment query tiles (ceil(t1/ATT_QT)), or nullptr for the inline
 // segment; max_t1 bounds every segment's length (sizes the on-chip score tile).
-constexpr int ATT_QT = 32;
+constexpr int ATT_QT = 64;
 int launch_attention(const float* q, const float* k, const float* v, int ld, Segs s, const int* toff,
                      int total_tiles, int max_t1, float* out, int ldo, cudaStream_t st);
 size_t attention_smem_bytes(int max_t1);
