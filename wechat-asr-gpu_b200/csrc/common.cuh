@@ -255,7 +255,10 @@ __constant__ static const unsigned long long kExp2Tab[32] = {
     0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull};
 
 // tab[i] above = bits(2^(i/32)) - (i << 47): adding k << 47 to tab[k % 32] yields 2^(k/32).
-__device__ __forceinline__ float expf_ref(float x) {
+// `lookup(i)` returns tab[i]: from constant memory (expf_ref) or from a shared-memory copy
+// (expf_ref_smem; indexed constant loads serialise when the lanes of a warp differ).
+template <typename Lookup>
+__device__ __forceinline__ float expf_body(float x, Lookup lookup) {
   const uint32_t ux = __float_as_uint(x);
   if (ux == 0x4202422fu) return f_from_bits(0x56fc9f1cu);  // the two inputs where glibc's result
   if (ux == 0xc27c65d9u) return f_from_bits(0x11fa2993u);  // is the other float neighbour
@@ -276,7 +279,7 @@ __device__ __forceinline__ float expf_ref(float x) {
   const unsigned long long ki = static_cast<unsigned long long>(__double_as_longlong(kd));
   kd = __dsub_rn(kd, shift);
   const double r = __dsub_rn(z, kd);
-  const unsigned long long t = kExp2Tab[ki & 31] + (ki << 47);
+  const unsigned long long t = lookup(static_cast<int>(ki & 31)) + (ki << 47);
   const double s = __longlong_as_double(static_cast<long long>(t));
   const double zz = __dadd_rn(__dmul_rn(c0, r), c1);
   const double r2 = __dmul_rn(r, r);
@@ -284,6 +287,13 @@ __device__ __forceinline__ float expf_ref(float x) {
   y = __dadd_rn(__dmul_rn(zz, r2), y);
   y = __dmul_rn(y, s);
   return __double2float_rn(y);
+}
+__device__ __forceinline__ float expf_ref(float x) {
+  return expf_body(x, [](int i) { return kExp2Tab[i]; });
+}
+// tab: a shared-memory copy of kExp2Tab
+__device__ __forceinline__ float expf_ref_smem(float x, const unsigned long long* tab) {
+  return expf_body(x, [tab](int i) { return tab[i]; });
 }
 
 // GELU of src/model.rs:710-712, evaluated left to right like rustc:

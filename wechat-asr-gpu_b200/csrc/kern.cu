@@ -512,53 +512,60 @@ __global__ void keys_to_ids_k(const unsigned long long* __restrict__ keys, int m
 }
 
 // ------------------------------------------------------------------------ attention
-// One block per (segment, 64-query tile, head).  Scores s_ij = dotf(q_i, k_j) * 0.125 with the
-// 8-lane order of src/kernels.rs:172-183; softmax with e_j = exp(s_j - max) and the row sum z
-// folded sequentially (src/model.rs:723-728); p_j = e_j / z; o_i[d] = sum_j p_j v_j[d] folded
-// over j in order (src/model.rs:729-735).  The score tile stays in shared memory.
+// One block per (query tile, head).  A segment of t rows is cut into ceil(t/64) tiles of
+// equal size (at most 64 rows), so short last tiles do not waste work.  Scores
+// s_ij = dotf(q_i, k_j) * 0.125 (src/kernels.rs:172-183 order); softmax e_j = exp(s_j - max),
+// z = sequential sum, p_j = e_j / z; o_i[d] = sum over j in order of p_j * v_j[d] from 0
+// (src/model.rs:714-738).  Every element keeps the reference's exact sequence of rounded
+// multiplies and adds.
 //
-// Every output element keeps the CPU's exact sequence of rounded multiplies and adds.  The
-// speed comes from register blocking: a thread owns 4 query rows x 4 keys for the scores and
-// 4 query rows x 4 head dims for PV (16 independent chains, ~6 shared loads per 32 FP ops),
-// from prefetching the next 64-key K/V chunk into registers while the current one is used, and
-// from warps whose query rows all lie past the end of a short tile skipping the math.
-// Shared layout: Q and S hold query rows in interleaved pairs (float2 = rows 2p, 2p+1).
-constexpr int ATT_KVS = HD + 1;  // padded K-chunk row
+// Packed pairs.  Scores: a thread owns query rows (2r, 2r+1) x keys (kt + 8u, u < 4) of a
+// 32-key chunk and keeps all 8 dotf lanes of each score as 4 float2 (lanes 2l, 2l+1 take
+// dims 8c+2l, 8c+2l+1), so a product pair is q[d..d+1] * k[d..d+1] -- two register pairs.
+// PV: a thread owns row pairs (2p, 2p+1) for p = r, r+16 x head dims d0..d0+3; the
+// accumulators pair (row 2p, dim d) with (row 2p+1, dim d^1), so the products are
+// (p_2p, p_2p+1) x (v[d], v[d^1]) from V and a pair-swapped copy of V.
+// Shared layout: exp table | Q [64][68] + K [32][68] (scores) / V, Vs [32][64] (PV) |
+// S2 [32 row pairs][sp] float2 | Z [64].
+constexpr int ATT_KC = 32;   // keys per chunk
+constexpr int ATT_RS = 68;   // Q / K row stride in floats (16-byte rows, conflict-free tiles)
+constexpr int ATT_A = (ATT_QT + ATT_KC) * ATT_RS;  // floats of the Q/K (and V/Vs) region
 
 __host__ __device__ inline int att_pair_stride(int max_t1) { return ((max_t1 + 15) / 16) * 16 + 1; }
 
 size_t attention_smem_bytes(int max_t1) {
   const int sp = att_pair_stride(max_t1);
-  return static_cast<size_t>(ATT_QT / 2 * HD * 2 + 64 * ATT_KVS + ATT_QT / 2 * sp * 2 + ATT_QT) * 4;
+  return 32 * 8 + static_cast<size_t>(ATT_A) * 4 + static_cast<size_t>(ATT_QT / 2) * sp * 8 + ATT_QT * 4;
 }
 
-__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
-// component-wise exactly rounded multiply / add of a query-row pair
-__device__ __forceinline__ float2 pmul(float2 a, float2 b) { return make_float2(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y)); }
-__device__ __forceinline__ float2 padd(float2 a, float2 b) { return make_float2(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y)); }
+__device__ __forceinline__ float2 lo2(float4 a) { return make_float2(a.x, a.y); }
+__device__ __forceinline__ float2 hi2(float4 a) { return make_float2(a.z, a.w); }
 
-// one 64-key chunk of K or V rows [j0, j0+nj) of head h: 4 float4 per thread (zeros past nj)
+// rows [j0, j0+8*ATT_KC/... ) of K or V for head h: 2 float4 per thread (zeros past nj)
 __device__ __forceinline__ void att_fetch(const float* __restrict__ src, int ld, int rb, int j0, int nj, int h,
-                                          int tid, float4 (&r)[4]) {
+                                          int tid, float4 (&r)[2]) {
 #pragma unroll
-  for (int u = 0; u < 4; u++) {
+  for (int u = 0; u < 2; u++) {
     const int e = tid + 256 * u, j = e >> 4, d4 = (e & 15) * 4;
     r[u] = j < nj ? __ldg(reinterpret_cast<const float4*>(src + static_cast<int64_t>(rb + j0 + j) * ld + h * HD + d4))
                   : make_float4(0.f, 0.f, 0.f, 0.f);
   }
 }
 
-__global__ void __launch_bounds__(256) attn_k(const float* __restrict__ q, const float* __restrict__ k,
-                                              const float* __restrict__ v, int ld, Segs s,
-                                              const int* __restrict__ toff, int max_t1, float* __restrict__ out,
-                                              int ldo) {
-  extern __shared__ float sm[];
+__global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, const float* __restrict__ k,
+                                                 const float* __restrict__ v, int ld, Segs s,
+                                                 const int* __restrict__ toff, int max_t1, float* __restrict__ out,
+                                                 int ldo) {
+  extern __shared__ __align__(16) float sm[];
   const int sp = att_pair_stride(max_t1);
-  float2* Q2 = reinterpret_cast<float2*>(sm);                 // [32][64] query row pairs
-  float* KV = sm + ATT_QT / 2 * HD * 2;                        // [64][65] K chunk / [64][64] V chunk
-  float2* S2 = reinterpret_cast<float2*>(KV + 64 * ATT_KVS);   // [32][sp] score row pairs
-  float* Z = reinterpret_cast<float*>(S2 + ATT_QT / 2 * sp);   // [64] row sums
-  const int tile = blockIdx.x, h = blockIdx.y;
+  unsigned long long* tab = reinterpret_cast<unsigned long long*>(sm);
+  float* Q = sm + 64;                 // [64][68]
+  float* K = Q + ATT_QT * ATT_RS;     // [32][68]
+  float* V = Q;                       // [32][64] (PV phase)
+  float* Vs = Q + ATT_KC * HD;        // [32][64] pair-swapped V
+  float2* S2 = reinterpret_cast<float2*>(Q + ATT_A);  // [32][sp]
+  float* Z = reinterpret_cast<float*>(S2 + (ATT_QT / 2) * sp);
+  const int tile = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
   int sw = 0;
   if (toff) {
     int lo = 0, hi = s.n - 1;
@@ -570,78 +577,100 @@ __global__ void __launch_bounds__(256) attn_k(const float* __restrict__ q, const
   }
   const int qt = toff ? tile - toff[sw] : tile;
   const int rb = s.row_begin(sw), t = s.rows(sw);
-  const int i0 = qt * ATT_QT;
-  const int ni = min(ATT_QT, t - i0);
+  const int ntile = (t + ATT_QT - 1) / ATT_QT, rpt = ntile > 0 ? (t + ntile - 1) / ntile : 0;
+  const int i0 = qt * rpt;
+  const int ni = min(rpt, t - i0);
   if (ni <= 0 || t > max_t1) return;
-  const int tid = threadIdx.x;
-  float* Qf = reinterpret_cast<float*>(Q2);
-  for (int e = tid; e < ATT_QT * HD; e += 256) {
-    const int i = e >> 6, d = e & 63;
-    Qf[((i >> 1) * HD + d) * 2 + (i & 1)] = i < ni ? q[static_cast<int64_t>(rb + i0 + i) * ld + h * HD + d] : 0.0f;
+  if (tid < 32) tab[tid] = kExp2Tab[tid];
+  for (int e = tid; e < ATT_QT * 16; e += 256) {
+    const int i = e >> 4, d4 = (e & 15) * 4;
+    *reinterpret_cast<float4*>(Q + i * ATT_RS + d4) =
+        i < ni ? __ldg(reinterpret_cast<const float4*>(q + static_cast<int64_t>(rb + i0 + i) * ld + h * HD + d4))
+               : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  const int ig = tid >> 4;            // query rows 4ig..4ig+3 = pairs 2ig, 2ig+1
-  const int sub = tid & 15;           // keys sub+16u (scores) / head dims 4sub..4sub+3 (PV)
-  const bool rows_live = 4 * ig < ni;  // uniform over each half-warp
-  const int nchunks = (t + 63) / 64;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int nchunks = (t + ATT_KC - 1) / ATT_KC;
   // ---- scores
-  float4 pre[4];
-  att_fetch(k, ld, rb, 0, min(64, t), h, tid, pre);
-  for (int ch = 0; ch < nchunks; ch++) {
-    const int j0 = ch * 64, nj = min(64, t - j0);
-    __syncthreads();  // previous chunk fully consumed
+  {
+    const int rt = 8 * (warp & 3) + (lane & 7), kt = 4 * (warp >> 2) + (lane >> 3);
+    const bool live = 16 * (warp & 3) < ni;  // warp-uniform
+    const float* qa = Q + (2 * rt) * ATT_RS;
+    const float* qb = qa + ATT_RS;
+    float4 pre[2];
+    att_fetch(k, ld, rb, 0, min(ATT_KC, t), h, tid, pre);
+    for (int ch = 0; ch < nchunks; ch++) {
+      const int j0 = ch * ATT_KC, nj = min(ATT_KC, t - j0);
+      __syncthreads();  // previous chunk consumed (and Q staged)
 #pragma unroll
-    for (int u = 0; u < 4; u++) {
-      const int e = tid + 256 * u, j = e >> 4, d4 = (e & 15) * 4;
-      float* dst = KV + j * ATT_KVS + d4;
-      dst[0] = pre[u].x; dst[1] = pre[u].y; dst[2] = pre[u].z; dst[3] = pre[u].w;
-    }
-    if (ch + 1 < nchunks) att_fetch(k, ld, rb, j0 + 64, min(64, t - j0 - 64), h, tid, pre);
-    __syncthreads();
-    if (rows_live) {
-      float2 sc[2][4];
+      for (int u = 0; u < 2; u++) {
+        const int e = tid + 256 * u, j = e >> 4, d4 = (e & 15) * 4;
+        *reinterpret_cast<float4*>(K + j * ATT_RS + d4) = pre[u];
+      }
+      if (ch + 1 < nchunks) att_fetch(k, ld, rb, j0 + ATT_KC, min(ATT_KC, t - j0 - ATT_KC), h, tid, pre);
+      __syncthreads();
+      if (live) {
+        float2 acc[2][4][4];
 #pragma unroll
-      for (int l = 0; l < 8; l++) {
-        float2 acc[2][4];
+        for (int r = 0; r < 2; r++)
+#pragma unroll
+          for (int u = 0; u < 4; u++)
+#pragma unroll
+            for (int l = 0; l < 4; l++) acc[r][u][l] = make_float2(0.0f, 0.0f);
 #pragma unroll
         for (int c = 0; c < 8; c++) {
-          const int d = 8 * c + l;
-          const float2 qa = Q2[(2 * ig) * HD + d], qb = Q2[(2 * ig + 1) * HD + d];
+          const float4 a0 = *reinterpret_cast<const float4*>(qa + 8 * c);
+          const float4 a1 = *reinterpret_cast<const float4*>(qa + 8 * c + 4);
+          const float4 b0 = *reinterpret_cast<const float4*>(qb + 8 * c);
+          const float4 b1 = *reinterpret_cast<const float4*>(qb + 8 * c + 4);
 #pragma unroll
           for (int u = 0; u < 4; u++) {
-            const float kv = KV[(sub + 16 * u) * ATT_KVS + d];
-            const float2 pa = pmul(qa, f2(kv)), pb = pmul(qb, f2(kv));
-            acc[0][u] = c == 0 ? pa : padd(acc[0][u], pa);
-            acc[1][u] = c == 0 ? pb : padd(acc[1][u], pb);
+            const float* kr = K + (kt + 8 * u) * ATT_RS + 8 * c;
+            const float4 k0 = *reinterpret_cast<const float4*>(kr);
+            const float4 k1 = *reinterpret_cast<const float4*>(kr + 4);
+            acc[0][u][0] = add2_rn(acc[0][u][0], mulp(lo2(a0), lo2(k0)));
+            acc[0][u][1] = add2_rn(acc[0][u][1], mulp(hi2(a0), hi2(k0)));
+            acc[0][u][2] = add2_rn(acc[0][u][2], mulp(lo2(a1), lo2(k1)));
+            acc[0][u][3] = add2_rn(acc[0][u][3], mulp(hi2(a1), hi2(k1)));
+            acc[1][u][0] = add2_rn(acc[1][u][0], mulp(lo2(b0), lo2(k0)));
+            acc[1][u][1] = add2_rn(acc[1][u][1], mulp(hi2(b0), hi2(k0)));
+            acc[1][u][2] = add2_rn(acc[1][u][2], mulp(lo2(b1), lo2(k1)));
+            acc[1][u][3] = add2_rn(acc[1][u][3], mulp(hi2(b1), hi2(k1)));
           }
         }
 #pragma unroll
         for (int u = 0; u < 4; u++) {
-          sc[0][u] = l == 0 ? acc[0][u] : padd(sc[0][u], acc[0][u]);
-          sc[1][u] = l == 0 ? acc[1][u] : padd(sc[1][u], acc[1][u]);
-        }
-      }
+          const int j = kt + 8 * u;
+          if (j < nj) {
+            float sc[2];
 #pragma unroll
-      for (int u = 0; u < 4; u++) {
-        const int j = sub + 16 * u;
-        if (j < nj) {
-          S2[(2 * ig) * sp + j0 + j] = pmul(sc[0][u], f2(0.125f));
-          S2[(2 * ig + 1) * sp + j0 + j] = pmul(sc[1][u], f2(0.125f));
+            for (int r = 0; r < 2; r++) {
+              float x = __fadd_rn(acc[r][u][0].x, acc[r][u][0].y);
+              x = __fadd_rn(x, acc[r][u][1].x);
+              x = __fadd_rn(x, acc[r][u][1].y);
+              x = __fadd_rn(x, acc[r][u][2].x);
+              x = __fadd_rn(x, acc[r][u][2].y);
+              x = __fadd_rn(x, acc[r][u][3].x);
+              x = __fadd_rn(x, acc[r][u][3].y);
+              sc[r] = __fmul_rn(x, 0.125f);
+            }
+            S2[rt * sp + j0 + j] = make_float2(sc[0], sc[1]);
+          }
         }
       }
     }
   }
   // prefetch the first V chunk while the softmax runs
-  att_fetch(v, ld, rb, 0, min(64, t), h, tid, pre);
+  float4 pre[2];
+  att_fetch(v, ld, rb, 0, min(ATT_KC, t), h, tid, pre);
   __syncthreads();
   // ---- softmax: row max (order-free, warp per row), exp (element-wise), sequential row sum
   float* Sf = reinterpret_cast<float*>(S2);
-  const int warp = tid >> 5, lane = tid & 31;
   for (int i = warp; i < ni; i += 8) {
     float* row = Sf + (i >> 1) * sp * 2 + (i & 1);
     float m = -3.40282347e+38f;
     for (int j = lane; j < t; j += 32) m = fmaxf(m, row[2 * j]);
     m = warp_max(m);
-    for (int j = lane; j < t; j += 32) row[2 * j] = expf_ref(__fsub_rn(row[2 * j], m));
+    for (int j = lane; j < t; j += 32) row[2 * j] = expf_ref_smem(__fsub_rn(row[2 * j], m), tab);
   }
   __syncthreads();
   if (tid < ni) {
@@ -656,47 +685,68 @@ __global__ void __launch_bounds__(256) attn_k(const float* __restrict__ q, const
     float* x = Sf + (i >> 1) * sp * 2 + (i & 1) + 2 * j;
     *x = __fdiv_rn(*x, Z[i]);
   }
-  // ---- PV: thread = query rows 4ig..4ig+3 x head dims 4sub..4sub+3; keys summed in order
+  // ---- PV
+  const int pr = 8 * (warp & 1) + (lane & 7), dt = 4 * (warp >> 1) + (lane >> 3);
+  const bool live0 = 16 * (warp & 1) < ni, live1 = 32 + 16 * (warp & 1) < ni;  // warp-uniform
   float2 o[2][4];
 #pragma unroll
-  for (int u = 0; u < 4; u++) o[0][u] = o[1][u] = make_float2(0.0f, 0.0f);
+  for (int a = 0; a < 2; a++)
+#pragma unroll
+    for (int u = 0; u < 4; u++) o[a][u] = make_float2(0.0f, 0.0f);
   for (int ch = 0; ch < nchunks; ch++) {
-    const int j0 = ch * 64, nj = min(64, t - j0);
+    const int j0 = ch * ATT_KC, nj = min(ATT_KC, t - j0);
     __syncthreads();
 #pragma unroll
-    for (int u = 0; u < 4; u++) {
+    for (int u = 0; u < 2; u++) {
       const int e = tid + 256 * u, j = e >> 4, d4 = (e & 15) * 4;
-      *reinterpret_cast<float4*>(KV + j * HD + d4) = pre[u];
+      const float4 x = pre[u];
+      *reinterpret_cast<float4*>(V + j * HD + d4) = x;
+      *reinterpret_cast<float4*>(Vs + j * HD + d4) = make_float4(x.y, x.x, x.w, x.z);
     }
-    if (ch + 1 < nchunks) att_fetch(v, ld, rb, j0 + 64, min(64, t - j0 - 64), h, tid, pre);
+    if (ch + 1 < nchunks) att_fetch(v, ld, rb, j0 + ATT_KC, min(ATT_KC, t - j0 - ATT_KC), h, tid, pre);
     __syncthreads();
-    if (rows_live) {
-      const float2* pa_row = S2 + (2 * ig) * sp + j0;
-      const float2* pb_row = S2 + (2 * ig + 1) * sp + j0;
+    const float2* p0 = S2 + pr * sp + j0;
+    const float2* p1 = S2 + (pr + 16) * sp + j0;
+    const float* vr = V + 4 * dt;
+    const float* vsr = Vs + 4 * dt;
+    if (live1) {
 #pragma unroll 4
       for (int jj = 0; jj < nj; jj++) {
-        const float2 pa = pa_row[jj], pb = pb_row[jj];
-        const float4 vv = *reinterpret_cast<const float4*>(KV + jj * HD + 4 * sub);
-        o[0][0] = padd(o[0][0], pmul(pa, f2(vv.x)));
-        o[0][1] = padd(o[0][1], pmul(pa, f2(vv.y)));
-        o[0][2] = padd(o[0][2], pmul(pa, f2(vv.z)));
-        o[0][3] = padd(o[0][3], pmul(pa, f2(vv.w)));
-        o[1][0] = padd(o[1][0], pmul(pb, f2(vv.x)));
-        o[1][1] = padd(o[1][1], pmul(pb, f2(vv.y)));
-        o[1][2] = padd(o[1][2], pmul(pb, f2(vv.z)));
-        o[1][3] = padd(o[1][3], pmul(pb, f2(vv.w)));
+        const float2 pa = p0[jj], pb = p1[jj];
+        const float4 x = *reinterpret_cast<const float4*>(vr + jj * HD);
+        const float4 y = *reinterpret_cast<const float4*>(vsr + jj * HD);
+        o[0][0] = add2_rn(o[0][0], mulp(pa, lo2(x)));
+        o[0][1] = add2_rn(o[0][1], mulp(pa, lo2(y)));
+        o[0][2] = add2_rn(o[0][2], mulp(pa, hi2(x)));
+        o[0][3] = add2_rn(o[0][3], mulp(pa, hi2(y)));
+        o[1][0] = add2_rn(o[1][0], mulp(pb, lo2(x)));
+        o[1][1] = add2_rn(o[1][1], mulp(pb, lo2(y)));
+        o[1][2] = add2_rn(o[1][2], mulp(pb, hi2(x)));
+        o[1][3] = add2_rn(o[1][3], mulp(pb, hi2(y)));
+      }
+    } else if (live0) {
+#pragma unroll 4
+      for (int jj = 0; jj < nj; jj++) {
+        const float2 pa = p0[jj];
+        const float4 x = *reinterpret_cast<const float4*>(vr + jj * HD);
+        const float4 y = *reinterpret_cast<const float4*>(vsr + jj * HD);
+        o[0][0] = add2_rn(o[0][0], mulp(pa, lo2(x)));
+        o[0][1] = add2_rn(o[0][1], mulp(pa, lo2(y)));
+        o[0][2] = add2_rn(o[0][2], mulp(pa, hi2(x)));
+        o[0][3] = add2_rn(o[0][3], mulp(pa, hi2(y)));
       }
     }
   }
+  // o[a][0] = (row 2p d0, row 2p+1 d0+1), o[a][1] = (2p d0+1, 2p+1 d0), [2],[3] likewise at d0+2
 #pragma unroll
-  for (int pr = 0; pr < 2; pr++) {
-    const int r0 = 4 * ig + 2 * pr;
+  for (int a = 0; a < 2; a++) {
+    const int r0 = 2 * (pr + 16 * a);
     if (r0 < ni)
-      *reinterpret_cast<float4*>(out + static_cast<int64_t>(rb + i0 + r0) * ldo + h * HD + 4 * sub) =
-          make_float4(o[pr][0].x, o[pr][1].x, o[pr][2].x, o[pr][3].x);
+      *reinterpret_cast<float4*>(out + static_cast<int64_t>(rb + i0 + r0) * ldo + h * HD + 4 * dt) =
+          make_float4(o[a][0].x, o[a][1].x, o[a][2].x, o[a][3].x);
     if (r0 + 1 < ni)
-      *reinterpret_cast<float4*>(out + static_cast<int64_t>(rb + i0 + r0 + 1) * ldo + h * HD + 4 * sub) =
-          make_float4(o[pr][0].y, o[pr][1].y, o[pr][2].y, o[pr][3].y);
+      *reinterpret_cast<float4*>(out + static_cast<int64_t>(rb + i0 + r0 + 1) * ldo + h * HD + 4 * dt) =
+          make_float4(o[a][1].y, o[a][0].y, o[a][3].y, o[a][2].y);
   }
 }
 
