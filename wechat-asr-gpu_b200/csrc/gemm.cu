@@ -5,6 +5,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstring>
 #include <cstdio>
 #include <mutex>
 #include <unordered_map>
@@ -31,23 +32,29 @@ namespace {
 
 struct MapKey {
   uintptr_t p;
-  int rows, k, box;
-  bool operator==(const MapKey& o) const { return p == o.p && rows == o.rows && k == o.k && box == o.box; }
+  int rows, cols, ld, box_rows, kind;  // kind 0: int8 operand, 1: fp32 / int32 output
+  bool operator==(const MapKey& o) const {
+    return p == o.p && rows == o.rows && cols == o.cols && ld == o.ld && box_rows == o.box_rows && kind == o.kind;
+  }
 };
 struct MapKeyHash {
   size_t operator()(const MapKey& k) const {
     return std::hash<uintptr_t>()(k.p) ^ (static_cast<size_t>(k.rows) * 0x9E3779B97F4A7C15ull) ^
-           (static_cast<size_t>(k.k) << 20) ^ static_cast<size_t>(k.box);
+           (static_cast<size_t>(k.cols) << 20) ^ (static_cast<size_t>(k.ld) << 40) ^
+           static_cast<size_t>(k.box_rows * 2 + k.kind);
   }
 };
 
 std::mutex g_map_mu;
 std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
 
-// Tensor map of an int8 [rows][k] row-major matrix, box = 128 bytes of K x `box` rows,
-// 128-byte swizzle (the UMMA K-major SW128 canonical layout), zero fill out of bounds.
-bool tensor_map(const void* p, int rows, int k, int box, CUtensorMap* out) {
-  MapKey key{reinterpret_cast<uintptr_t>(p), rows, k, box};
+// Tensor maps, cached by (pointer, shape, kind).  Both kinds use 128-byte boxes with 128-byte
+// swizzle and zero fill out of bounds:
+//   kind 0: int8 operand [rows][cols = K], box 128 (K) x box_rows -- the UMMA K-major SW128 layout;
+//   kind 1: 32-bit output [rows][cols] with row stride ld elements, box 32 x 32 -- the epilogue's
+//           staging layout (stores are clipped to rows x cols).
+bool tensor_map(const void* p, int rows, int cols, int ld, int box_rows, int kind, CUtensorMap* out) {
+  MapKey key{reinterpret_cast<uintptr_t>(p), rows, cols, ld, box_rows, kind};
   {
     std::lock_guard<std::mutex> lk(g_map_mu);
     auto it = g_maps.find(key);
@@ -56,13 +63,15 @@ bool tensor_map(const void* p, int rows, int k, int box, CUtensorMap* out) {
       return true;
     }
   }
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(k)};
-  cuuint32_t boxd[2] = {128u, static_cast<cuuint32_t>(box)};
+  const int esize = kind == 0 ? 1 : 4;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * esize};
+  cuuint32_t boxd[2] = {static_cast<cuuint32_t>(128 / esize), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1u, 1u};
   CUtensorMap m;
-  CUresult r = g_encode(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(p), dims, strides, boxd, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+  CUresult r = g_encode(&m, kind == 0 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                        const_cast<void*>(p), dims, strides, boxd, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return false;
   std::lock_guard<std::mutex> lk(g_map_mu);
@@ -92,7 +101,7 @@ bool ensure_attr() {
   int dev = 0;
   cudaGetDevice(&dev);
   if (done & (1u << (dev & 31))) return true;
-  if (cudaFuncSetAttribute(gemm_i8_tc<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<BN>::SMEM) !=
+  if (cudaFuncSetAttribute(gemm_i8_tc<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<BN, EPI>::SMEM) !=
       cudaSuccess)
     return false;
   done |= 1u << (dev & 31);
@@ -105,13 +114,19 @@ bool prepare_epi() {
 }
 
 template <int BN, int EPI>
-int launch_tc(const GemmArgs& g, cudaStream_t s) {
-  CUtensorMap ta, tb;
-  if (!tensor_map(g.a, g.M, g.K, 128, &ta) || !tensor_map(g.b, g.N, g.K, BN, &tb)) return -4;
-  constexpr int smem = TcCfg<BN>::SMEM;
+int launch_tc(const GemmArgs& g0, cudaStream_t s) {
+  CUtensorMap ta, tb, to;
+  if (!tensor_map(g0.a, g0.M, g0.K, g0.K, 128, 0, &ta) || !tensor_map(g0.b, g0.N, g0.K, g0.K, BN, 0, &tb)) return -4;
+  GemmArgs g = g0;
+  // output blocks move by TMA when the output rows are 16-byte aligned
+  void* obase = EPI == EPI_I32 ? static_cast<void*>(g.out_i32) : static_cast<void*>(g.out);
+  g.tma_out = EPI != EPI_ARGMAX && obase && (reinterpret_cast<uintptr_t>(obase) % 16 == 0) && (g.ldo % 4 == 0) &&
+              tensor_map(obase, g.M, g.n_store, g.ldo, 32, 1, &to);
+  if (!g.tma_out) memset(&to, 0, sizeof(to));
+  constexpr int smem = TcCfg<BN, EPI>::SMEM;
   if (!ensure_attr<BN, EPI>()) return -4;
   const int tiles = ((g.n_store + BN - 1) / BN) * ((g.M + 127) / 128);
-  gemm_i8_tc<BN, EPI><<<std::min(tiles, num_sms()), TcCfg<BN>::THREADS, smem, s>>>(ta, tb, g);
+  gemm_i8_tc<BN, EPI><<<std::min(tiles, num_sms()), TcCfg<BN, EPI>::THREADS, smem, s>>>(ta, tb, to, g);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 
@@ -127,7 +142,8 @@ int launch_epi(const GemmArgs& g, cudaStream_t s) {
   // widest N tile that still fills every SM once; narrow tiles for small (per-window) M
   const int tm = (g.M + 127) / 128, sms = num_sms();
   auto ctas = [&](int bn) { return tm * ((g.n_store + bn - 1) / bn); };
-  if (ctas(256) >= sms) return launch_tc<256, EPI>(g, s);
+  // (the residual epilogue keeps 3 staging blocks per warp: at BN=256 only 2 ring stages fit)
+  if (EPI != EPI_F32_ADD && ctas(256) >= sms) return launch_tc<256, EPI>(g, s);
   if (ctas(128) >= sms) return launch_tc<128, EPI>(g, s);
   return launch_tc<64, EPI>(g, s);
 }

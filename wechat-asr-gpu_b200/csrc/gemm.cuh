@@ -10,7 +10,8 @@
 //   warp 0      : TMA producer (one elected lane), STAGES-deep smem ring
 //   warp 1      : TMEM allocator + MMA issuer (one lane issues tcgen05.mma, M=128, N=BN, K=32)
 //   warps 2..9  : epilogue; warp w reads TMEM lanes 32*(w%4).. with tcgen05.ld (thread = row),
-//                 stages through shared memory and stores 128-byte row segments
+//                 writes each 32 x 32 block into a 128-byte-swizzled staging buffer and TMA-stores
+//                 it (residual epilogue: the h block arrives by TMA load two blocks ahead)
 // Every spin-wait is bounded (common.cuh); a timeout sets the context's error word.
 #pragma once
 
@@ -43,6 +44,7 @@ struct GemmArgs {
   unsigned long long* keys;  // EPI_ARGMAX: per-row packed keys (zeroed by caller)
   int* err;            // device error word
   int epi;             // Epi kind
+  int tma_out;         // 1: out / out_i32 blocks move by TMA (tensor map passed to the kernel)
 };
 
 template <int EPI>
@@ -112,7 +114,7 @@ __device__ __forceinline__ void epi_finish_row(const GemmArgs& g, int row, float
   }
 }
 
-template <int BN>
+template <int BN, int EPI>
 struct TcCfg {
   static_assert(BN == 64 || BN == 128 || BN == 256, "tile width");
   static constexpr int BM = 128;
@@ -120,12 +122,18 @@ struct TcCfg {
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = BN * BK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = BN >= 256 ? 3 : 4;
+  // staging buffers per epilogue warp: 2 for stores, 3 when h blocks are loaded ahead as well
+  static constexpr int NBUF = EPI == EPI_F32_ADD ? 3 : 2;
+  static constexpr int STAGES = BN >= 256 ? (EPI == EPI_F32_ADD ? 2 : 3) : (EPI == EPI_F32_ADD && BN == 128 ? 3 : 4);
   static constexpr int EPI_WARPS = 8;                 // two per TMEM lane quarter, half the columns each
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int TMEM_COLS = 2 * BN;            // two accumulator buffers
-  static constexpr int STG_FLOATS = 32 * 32;          // per epilogue warp
-  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_WARPS * STG_FLOATS * 4 + (2 * STAGES + 4) * 8 + 16;
+  static constexpr int STG_FLOATS = 32 * 32;          // one 32 x 32 block (4 KB, 1024-byte aligned)
+  static constexpr int COLC = 64;                     // per epilogue warp: 32 column scales + 32 biases
+  static constexpr int NBAR = 2 * STAGES + 4 + EPI_WARPS * NBUF;
+  static constexpr int SMEM =
+      1024 + STAGES * STAGE_BYTES + EPI_WARPS * (NBUF * STG_FLOATS + COLC) * 4 + NBAR * 8 + 16;
+  static_assert(SMEM <= 232448, "shared memory");
 };
 
 // Epilogue staging: a warp's 32 rows x 32 columns, stored so that row-per-thread float4
@@ -234,31 +242,90 @@ __device__ __forceinline__ void epi_chunk(const GemmArgs& g, float* stg, int lan
   }
 }
 
+// One 32 x 32 block on the TMA path: thread `lane` owns row `row` (columns col0..col0+31).
+// On entry `buf` holds the block's h values (EPI_F32_ADD); on exit it holds the output block
+// in the 128-byte-swizzled layout of the output tensor map.  Columns >= n_store and rows
+// >= M are computed from zero scales and clipped by the store.
+template <int EPI>
+__device__ __forceinline__ void epi_block_tma(const GemmArgs& g, float* buf, const float* colc, float xs, int lane,
+                                              int col0, const uint32_t (&r)[32], float& rmax) {
+  // colc[0..31] / colc[32..63]: per-channel scale / bias of columns col0.. (0 past n_store)
+  const int ncols = min(32, g.n_store - col0);
+  float v[32];
+  if constexpr (EPI == EPI_I32) {
+#pragma unroll
+    for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+  } else {
+    const bool has_wv = g.ws_vec != nullptr, has_b = g.bias != nullptr;
+#pragma unroll
+    for (int j4 = 0; j4 < 8; j4++) {
+      const float4 w4 = has_wv ? *reinterpret_cast<const float4*>(colc + 4 * j4) : make_float4(g.ws, g.ws, g.ws, g.ws);
+      const float4 b4 = has_b ? *reinterpret_cast<const float4*>(colc + 32 + 4 * j4) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float wk[4] = {w4.x, w4.y, w4.z, w4.w}, bk[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const int j = 4 * j4 + k;
+        const bool in = j < ncols;
+        v[j] = dequant(static_cast<int32_t>(r[j]), xs, in ? wk[k] : 0.0f, bk[k]);
+        if constexpr (EPI == EPI_F32_ROWMAX) {
+          if (in) rmax = fmaxf(rmax, fabsf(v[j]));
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int c4 = 0; c4 < 8; c4++) {
+    float4* p = reinterpret_cast<float4*>(buf + stg_off(lane, c4));
+    float4 w = make_float4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
+    if constexpr (EPI == EPI_F32_ADD) {
+      const float4 h = *p;  // h + o, src/model.rs:493,496
+      w = make_float4(__fadd_rn(h.x, w.x), __fadd_rn(h.y, w.y), __fadd_rn(h.z, w.z), __fadd_rn(h.w, w.w));
+    }
+    *p = w;
+  }
+  if constexpr (EPI == EPI_GELU_ROWMAX) {
+#pragma unroll 1
+    for (int j = 0; j < 32; j++) {
+      const int off = stg_off(lane, j >> 2) + (j & 3);
+      const float gv = gelu_ref(buf[off]);
+      buf[off] = gv;
+      if (j < ncols) rmax = fmaxf(rmax, fabsf(gv));
+    }
+  }
+}
+
 // Persistent, warp-specialised tcgen05 GEMM.  CTAs walk the 128 x BN output tiles in a
 // static round robin.  Warp 0 (one lane) streams A/B k-blocks through a STAGES-deep TMA ring;
 // warp 1 (one lane) issues tcgen05.mma into one of two TMEM accumulators; warps 2..9 drain the
-// other accumulator, so a tile's epilogue overlaps the next tile's MMAs.
+// other accumulator, so a tile's epilogue overlaps the next tile's MMAs.  Each epilogue warp
+// walks its sequence of 32 x 32 output blocks (BN/64 per tile); on the TMA path block cc is
+// staged in buffer cc % NBUF and stored with one bulk tensor store, and for the residual
+// epilogue lane 0 loads the h block of cc+2 as soon as its buffer's last store has read it.
 template <int BN, int EPI>
-__global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
-    gemm_i8_tc(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, GemmArgs g) {
-  using Cfg = TcCfg<BN>;
+__global__ void __launch_bounds__(TcCfg<BN, EPI>::THREADS, 1)
+    gemm_i8_tc(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+               const __grid_constant__ CUtensorMap tma_o, GemmArgs g) {
+  using Cfg = TcCfg<BN, EPI>;
   constexpr int ST = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + ST * Cfg::A_BYTES;
   float* stg_all = reinterpret_cast<float*>(sB + ST * Cfg::B_BYTES);
-  uint64_t* full = reinterpret_cast<uint64_t*>(stg_all + Cfg::EPI_WARPS * Cfg::STG_FLOATS);
+  float* colc_all = stg_all + Cfg::EPI_WARPS * Cfg::NBUF * Cfg::STG_FLOATS;  // [EPI_WARPS][64]
+  uint64_t* full = reinterpret_cast<uint64_t*>(colc_all + Cfg::EPI_WARPS * Cfg::COLC);
   uint64_t* empty = full + ST;
   uint64_t* tfull = empty + ST;   // [2] accumulator ready (MMA -> epilogue)
   uint64_t* tempty = tfull + 2;   // [2] accumulator drained (epilogue -> MMA)
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* hbar = tempty + 2;    // [EPI_WARPS][NBUF] h block landed (TMA -> epilogue warp)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(hbar + Cfg::EPI_WARPS * Cfg::NBUF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles = (g.n_store + BN - 1) / BN;
   const int tiles = n_tiles * ((g.M + Cfg::BM - 1) / Cfg::BM);
   const int nk = (g.K + Cfg::BK - 1) / Cfg::BK;
+  const bool tma_out = g.tma_out != 0 && EPI != EPI_ARGMAX;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < ST; s++) {
@@ -269,10 +336,12 @@ __global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
       mbar_init(tfull + b, 1);
       mbar_init(tempty + b, Cfg::EPI_WARPS);
     }
+    for (int b = 0; b < Cfg::EPI_WARPS * Cfg::NBUF; b++) mbar_init(hbar + b, 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tma_a);
     tma_prefetch_desc(&tma_b);
+    if (tma_out) tma_prefetch_desc(&tma_o);
   }
   if (warp == 1) {
     tmem_alloc(tslot, Cfg::TMEM_COLS);
@@ -336,11 +405,53 @@ __global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
     }
   } else {
     const int e = warp - 2, q = warp & 3, half = e >> 2;  // TMEM lane quarter = warp % 4
-    float* stg = stg_all + e * Cfg::STG_FLOATS;
-    int it = 0;
+    float* wb = stg_all + e * Cfg::NBUF * Cfg::STG_FLOATS;
+    float* colc = colc_all + e * Cfg::COLC;
+    uint64_t* hb = hbar + e * Cfg::NBUF;
+    constexpr int CPT = BN / 64;  // 32-column blocks per tile for this warp
+    // block cc of this warp's sequence -> (first row, first column); false past the last tile
+    // or past n_store
+    auto block_at = [&](int cc, int& row, int& col) {
+      const int k = cc / CPT;
+      const int tile = blockIdx.x + k * gridDim.x;
+      if (tile >= tiles) return false;
+      row = (tile / n_tiles) * Cfg::BM + q * 32;
+      col = (tile % n_tiles) * BN + half * (BN / 2) + 32 * (cc - k * CPT);
+      return col < g.n_store;
+    };
+    uint32_t hpar = 0, pend = 0;  // per-buffer phase parity (all lanes); loads in flight (lane 0)
+    auto load_h = [&](int cc) {   // lane 0 only
+      int row, col;
+      if (!block_at(cc, row, col)) return;
+      const int bi = cc % Cfg::NBUF;
+      mbar_arrive_expect_tx(hb + bi, Cfg::STG_FLOATS * 4);
+      tma_load_2d(wb + bi * Cfg::STG_FLOATS, &tma_o, hb + bi, col, row);
+      pend |= 1u << bi;
+    };
+    if constexpr (EPI == EPI_F32_ADD) {
+      if (tma_out && lane == 0) {
+        load_h(0);
+        load_h(1);
+      }
+    }
+    // column constants (per-channel scale, bias) of the next block, one per lane, fetched a
+    // block ahead so the loads never stall the dequant
+    const bool colconst = tma_out && EPI != EPI_I32 && (g.ws_vec || g.bias);
+    float nws = 0.0f, nbias = 0.0f;
+    auto fetch_cols = [&](int cc) {
+      int row, col;
+      nws = nbias = 0.0f;
+      if (!block_at(cc, row, col) || col + lane >= g.n_store) return;
+      if (g.ws_vec) nws = __ldg(g.ws_vec + col + lane);
+      if (g.bias) nbias = __ldg(g.bias + col + lane);
+    };
+    if (colconst) fetch_cols(0);
+    int it = 0, cc = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, it++) {
       const int b = it & 1, u = it >> 1;
       const int m0 = (tile / n_tiles) * Cfg::BM, n0 = (tile % n_tiles) * BN;
+      // this thread's row scale, loaded while the accumulator is still being computed
+      const float xs_row = (EPI != EPI_I32 && m0 + q * 32 + lane < g.M) ? g.xs[m0 + q * 32 + lane] : 0.0f;
       const bool ok = mbar_wait(tfull + b, u & 1);
       if (!ok) {
         atomicExch(g.err, ERR_WAIT_ACC);
@@ -354,15 +465,60 @@ __global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
       float rmax = 0.0f, best = -3.40282347e+38f;
       uint32_t bidx = 0xFFFFFFFFu;
 #pragma unroll 1
-      for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 32) {
+      for (int c = 0; c < CPT; c++, cc++) {
+        const int c0 = half * (BN / 2) + 32 * c;
+        const int col = n0 + c0;
         uint32_t r[32];
         tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * BN + c0), r);
-        if (n0 + c0 < g.n_store) epi_chunk<EPI>(g, stg, lane, rowbase, n0 + c0, r, rmax, best, bidx);
+        if (colconst) {
+          colc[lane] = nws;
+          colc[32 + lane] = nbias;
+          __syncwarp();
+          fetch_cols(cc + 1);
+        }
+        if (col < g.n_store) {
+          if (tma_out) {
+            const int bi = cc % Cfg::NBUF;
+            float* buf = wb + bi * Cfg::STG_FLOATS;
+            if constexpr (EPI == EPI_F32_ADD) {
+              if (!mbar_wait(hb + bi, (hpar >> bi) & 1)) {
+                atomicExch(g.err, ERR_WAIT_FULL);
+                *abort_flag = 1;
+              }
+              hpar ^= 1u << bi;
+              if (lane == 0) pend &= ~(1u << bi);
+            } else {
+              if (lane == 0) bulk_wait_read<Cfg::NBUF - 1>();  // the store of block cc-NBUF has read buf
+              __syncwarp();
+            }
+            epi_block_tma<EPI>(g, buf, colc, xs_row, lane, col, r, rmax);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tma_o, buf, col, rowbase);
+              bulk_commit();
+            }
+          } else {
+            epi_chunk<EPI>(g, wb, lane, rowbase, col, r, rmax, best, bidx);
+          }
+        }
+        if constexpr (EPI == EPI_F32_ADD) {
+          if (tma_out && lane == 0) {
+            bulk_wait_read<1>();  // buffer (cc+2) % 3 was last read by the store of block cc-1
+            load_h(cc + 2);
+          }
+        }
       }
       if (rowbase + lane < g.M) epi_finish_row<EPI>(g, rowbase + lane, rmax, best, bidx);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty + b);
+    }
+    if (tma_out && lane == 0) {
+      bulk_wait_all();
+      // h loads issued ahead but never consumed (abort): let them land before the CTA exits
+      for (int bi = 0; bi < Cfg::NBUF; bi++)
+        if ((pend >> bi) & 1u) mbar_wait(hb + bi, (hpar >> bi) & 1);
     }
   }
   tc_fence_before();

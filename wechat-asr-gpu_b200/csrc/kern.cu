@@ -291,69 +291,142 @@ __global__ void __launch_bounds__(256) quant_rows_k(const float* __restrict__ x,
 
 // ------------------------------------------------------------------------ LayerNorm + quant
 // src/model.rs:693-704 (+ the residual add of :493 / csrc/wtl_kern.cu:170-216 when o != 0).
-// Mean and variance are sequential left folds on the CPU; here thread `lane` of warp 0 folds
-// row `lane` of a 32-row tile staged in shared memory (stride 513: conflict-free), in the same
-// order.  Normalisation and quantisation are element-wise and run on all 8 warps.
-constexpr int LN_ROWS = 32;
-constexpr int LN_STRIDE = D + 1;
-constexpr int LN_SMEM = (LN_ROWS * LN_STRIDE + 2 * LN_ROWS) * 4;
+// Mean and variance are sequential left folds on the CPU, i.e. chains of 512 dependent
+// rounded adds per row, so a block keeps 128 rows folding at once: the rows stream through
+// shared memory in column chunks (coalesced cp.async, double-buffered), and thread i folds row
+// i over each chunk in column order -- pass 1 the sum, pass 2 the squared deviations.  Then 16
+// warps normalise, write the residual and quantise one row each at a time, coalesced, with
+// gamma / beta in registers.  The residual h + o is recomputed wherever it is needed (the same
+// rounded add every time).
+constexpr int LN_ROWS = 128;
+constexpr int LN_THREADS = 512;
+template <bool RES>
+struct LnCfg {
+  static constexpr int CW = RES ? 64 : 128;  // columns per chunk
+  static constexpr int NCH = D / CW;         // chunks per pass
+  static constexpr int RS = CW + 4;          // shared row stride in floats (conflict-free float4 rows)
+  static constexpr int NSRC = RES ? 2 : 1;   // h (+ o)
+  static constexpr int BUF = NSRC * LN_ROWS * RS;
+  static constexpr int SMEM = 2 * BUF * 4 + 2 * LN_ROWS * 4;
+};
 
-__global__ void __launch_bounds__(256) ln_quant_k(float* __restrict__ h, const float* __restrict__ o,
-                                                  const float* __restrict__ g, const float* __restrict__ b, int m,
-                                                  int8_t* __restrict__ xq, float* __restrict__ xs) {
-  extern __shared__ float sm[];
-  float* rows = sm;
-  float* mean = sm + LN_ROWS * LN_STRIDE;
+__device__ __forceinline__ float4 add4_rn(float4 a, float4 b) {
+  return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <bool RES>
+__global__ void __launch_bounds__(LN_THREADS) ln_quant_k(float* __restrict__ h, const float* __restrict__ o,
+                                                         const float* __restrict__ g, const float* __restrict__ b,
+                                                         int m, int8_t* __restrict__ xq, float* __restrict__ xs) {
+  using C = LnCfg<RES>;
+  extern __shared__ __align__(16) float sm[];
+  float* mean = sm + 2 * C::BUF;
   float* rinv = mean + LN_ROWS;
   const int r0 = blockIdx.x * LN_ROWS;
   const int nr = min(LN_ROWS, m - r0);
-  for (int e = threadIdx.x; e < nr * (D / 4); e += blockDim.x) {
-    const int rr = e / (D / 4), c4 = e - rr * (D / 4);
-    float4* hp = reinterpret_cast<float4*>(h + static_cast<int64_t>(r0 + rr) * D) + c4;
-    float4 v = *hp;
-    if (o) {
-      const float4 a = *(reinterpret_cast<const float4*>(o + static_cast<int64_t>(r0 + rr) * D) + c4);
-      v = make_float4(__fadd_rn(v.x, a.x), __fadd_rn(v.y, a.y), __fadd_rn(v.z, a.z), __fadd_rn(v.w, a.w));
-      *hp = v;
+  const int tid = threadIdx.x;
+  // chunk k (0 .. 2*NCH-1: both passes) -> buffer k & 1
+  auto load = [&](int k) {
+    float* dst = sm + (k & 1) * C::BUF;
+    const int col0 = (k % C::NCH) * C::CW;
+    for (int e = tid; e < nr * (C::CW / 4); e += LN_THREADS) {
+      const int rr = e / (C::CW / 4), c4 = e - rr * (C::CW / 4);
+      const int64_t src = static_cast<int64_t>(r0 + rr) * D + col0 + 4 * c4;
+      cp_async16(dst + rr * C::RS + 4 * c4, h + src);
+      if constexpr (RES) cp_async16(dst + LN_ROWS * C::RS + rr * C::RS + 4 * c4, o + src);
     }
-    float* d = rows + rr * LN_STRIDE + c4 * 4;
-    d[0] = v.x; d[1] = v.y; d[2] = v.z; d[3] = v.w;
+    cp_async_commit();
+  };
+  load(0);
+  float sum = 0.0f, s2 = 0.0f, mu = 0.0f;
+#pragma unroll 1
+  for (int k = 0; k < 2 * C::NCH; k++) {
+    if (k + 1 < 2 * C::NCH) {
+      load(k + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    if (tid < nr) {
+      const float4* hr = reinterpret_cast<const float4*>(sm + (k & 1) * C::BUF + tid * C::RS);
+      const float4* orow = reinterpret_cast<const float4*>(sm + (k & 1) * C::BUF + LN_ROWS * C::RS + tid * C::RS);
+      if (k < C::NCH) {
+#pragma unroll 8
+        for (int c = 0; c < C::CW / 4; c++) {
+          float4 v = hr[c];
+          if constexpr (RES) v = add4_rn(v, orow[c]);
+          sum = __fadd_rn(sum, v.x);
+          sum = __fadd_rn(sum, v.y);
+          sum = __fadd_rn(sum, v.z);
+          sum = __fadd_rn(sum, v.w);
+        }
+        if (k == C::NCH - 1) mu = __fdiv_rn(sum, static_cast<float>(D));
+      } else {
+#pragma unroll 8
+        for (int c = 0; c < C::CW / 4; c++) {
+          float4 v = hr[c];
+          if constexpr (RES) v = add4_rn(v, orow[c]);
+          const float dx = __fsub_rn(v.x, mu), dy = __fsub_rn(v.y, mu), dz = __fsub_rn(v.z, mu),
+                      dw = __fsub_rn(v.w, mu);
+          s2 = __fadd_rn(s2, __fmul_rn(dx, dx));
+          s2 = __fadd_rn(s2, __fmul_rn(dy, dy));
+          s2 = __fadd_rn(s2, __fmul_rn(dz, dz));
+          s2 = __fadd_rn(s2, __fmul_rn(dw, dw));
+        }
+      }
+    }
+    __syncthreads();  // buffer k & 1 is reloaded by the next iteration
   }
-  __syncthreads();
-  if (threadIdx.x < LN_ROWS && threadIdx.x < nr) {
-    const float* x = rows + threadIdx.x * LN_STRIDE;
-    float sum = 0.0f;
-#pragma unroll 16
-    for (int j = 0; j < D; j++) sum = __fadd_rn(sum, x[j]);
-    const float mu = __fdiv_rn(sum, static_cast<float>(D));
-    float s2 = 0.0f;
-#pragma unroll 16
-    for (int j = 0; j < D; j++) {
-      const float dd = __fsub_rn(x[j], mu);
-      s2 = __fadd_rn(s2, __fmul_rn(dd, dd));
-    }
+  if (tid < nr) {
     const float var = __fdiv_rn(s2, static_cast<float>(D));
-    mean[threadIdx.x] = mu;
-    rinv[threadIdx.x] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-6f)));
+    mean[tid] = mu;
+    rinv[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-6f)));
   }
   __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int rr = warp; rr < nr; rr += 8) {
-    const float mu = mean[rr], iv = rinv[rr];
-    const float* x = rows + rr * LN_STRIDE;
-    float y[D / 32];
+  const int warp = tid >> 5, lane = tid & 31;
+  float4 gg[4], bb[4];
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    gg[k] = __ldg(reinterpret_cast<const float4*>(g) + lane + 32 * k);
+    bb[k] = __ldg(reinterpret_cast<const float4*>(b) + lane + 32 * k);
+  }
+  for (int rr = warp; rr < nr; rr += LN_THREADS / 32) {
+    const float mu_r = mean[rr], iv = rinv[rr];
+    float4* hr = reinterpret_cast<float4*>(h + static_cast<int64_t>(r0 + rr) * D);
+    const float4* orow = RES ? reinterpret_cast<const float4*>(o + static_cast<int64_t>(r0 + rr) * D) : nullptr;
+    float4 y[4];
     float mx = 0.0f;
 #pragma unroll
-    for (int c = 0; c < D / 32; c++) {
-      const int j = lane + 32 * c;
-      y[c] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x[j], mu), iv), __ldg(g + j)), __ldg(b + j));
-      mx = fmaxf(mx, fabsf(y[c]));
+    for (int k = 0; k < 4; k++) {
+      float4 v = hr[lane + 32 * k];
+      if constexpr (RES) {
+        v = add4_rn(v, orow[lane + 32 * k]);
+        hr[lane + 32 * k] = v;
+      }
+      y[k].x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.x, mu_r), iv), gg[k].x), bb[k].x);
+      y[k].y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.y, mu_r), iv), gg[k].y), bb[k].y);
+      y[k].z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.z, mu_r), iv), gg[k].z), bb[k].z);
+      y[k].w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.w, mu_r), iv), gg[k].w), bb[k].w);
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(y[k].x), fabsf(y[k].y)), fmaxf(fabsf(y[k].z), fabsf(y[k].w))));
     }
     mx = warp_max(mx);
     const float sc = quant_scale(mx), inv = quant_inv(sc);
-    int8_t* q = xq + static_cast<int64_t>(r0 + rr) * D;
+    char4* q = reinterpret_cast<char4*>(xq + static_cast<int64_t>(r0 + rr) * D);
 #pragma unroll
-    for (int c = 0; c < D / 32; c++) q[lane + 32 * c] = quant_one(y[c], inv);
+    for (int k = 0; k < 4; k++) {
+      char4 c;
+      c.x = quant_one(y[k].x, inv); c.y = quant_one(y[k].y, inv); c.z = quant_one(y[k].z, inv); c.w = quant_one(y[k].w, inv);
+      q[lane + 32 * k] = c;
+    }
     if (lane == 0) xs[r0 + rr] = sc;
   }
 }
@@ -775,9 +848,10 @@ static void set_smem(const void* kern, int bytes) {
 bool kern_prepare() {
   set_smem(reinterpret_cast<const void*>(conv2_k), CV2_SMEM);
   set_smem(reinterpret_cast<const void*>(conv3_k), CV3_SMEM);
-  set_smem(reinterpret_cast<const void*>(ln_quant_k), LN_SMEM);
   set_smem(reinterpret_cast<const void*>(attn_k), 227 * 1024);
   set_smem(reinterpret_cast<const void*>(gelu_quant_ro_k), 227 * 1024);
+  set_smem(reinterpret_cast<const void*>(ln_quant_k<false>), LnCfg<false>::SMEM);
+  set_smem(reinterpret_cast<const void*>(ln_quant_k<true>), LnCfg<true>::SMEM);
   return cudaGetLastError() == cudaSuccess;
 }
 
@@ -813,8 +887,14 @@ int launch_quant_rows_max(const float* x, int m, int k, const unsigned* rowmax, 
 int launch_ln_quant(float* h, const float* o, const float* g, const float* b, int m, int8_t* xq, float* xs,
                     cudaStream_t st) {
   if (m <= 0) return 0;
-  set_smem(reinterpret_cast<const void*>(ln_quant_k), LN_SMEM);
-  ln_quant_k<<<(m + LN_ROWS - 1) / LN_ROWS, 256, LN_SMEM, st>>>(h, o, g, b, m, xq, xs);
+  const int blocks = (m + LN_ROWS - 1) / LN_ROWS;
+  if (o) {
+    set_smem(reinterpret_cast<const void*>(ln_quant_k<true>), LnCfg<true>::SMEM);
+    ln_quant_k<true><<<blocks, LN_THREADS, LnCfg<true>::SMEM, st>>>(h, o, g, b, m, xq, xs);
+  } else {
+    set_smem(reinterpret_cast<const void*>(ln_quant_k<false>), LnCfg<false>::SMEM);
+    ln_quant_k<false><<<blocks, LN_THREADS, LnCfg<false>::SMEM, st>>>(h, o, g, b, m, xq, xs);
+  }
   return launched();
 }
 int launch_gelu_quant(float* x, int m, int k, int8_t* xq, float* xs, cudaStream_t st) {
@@ -883,11 +963,18 @@ void wk_front(void* stream, const float* x, const float* c1, const float* c2, co
   launch_conv3(y2, c3, s, t1, y3, st);
 }
 
+// the 512-wide kernel moves rows as float4 / char4
+static bool ln_aligned(const float* h, const float* o, const float* g, const float* b, const int8_t* xq) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(o) |
+                      reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(b);
+  return (a & 15) == 0 && (reinterpret_cast<uintptr_t>(xq) & 3) == 0;
+}
+
 void wk_norm_quant(void* stream, const float* h, const float* g, const float* b, int t, int d, int8_t* xq,
                    float* xs) {
   if (!h || !g || !b || !xq || !xs || t <= 0 || d <= 0) return;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (d == D && (reinterpret_cast<uintptr_t>(h) & 15) == 0)
+  if (d == D && ln_aligned(h, h, g, b, xq))
     launch_ln_quant(const_cast<float*>(h), nullptr, g, b, t, xq, xs, st);
   else
     ln_quant_any_k<<<t, 256, 0, st>>>(const_cast<float*>(h), nullptr, g, b, d, xq, xs);
@@ -897,7 +984,7 @@ void wk_add_norm_quant(void* stream, float* h, const float* o, const float* g, c
                        int8_t* xq, float* xs) {
   if (!h || !o || !g || !b || !xq || !xs || t <= 0 || d <= 0) return;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (d == D && ((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(o)) & 15) == 0)
+  if (d == D && ln_aligned(h, o, g, b, xq))
     launch_ln_quant(h, o, g, b, t, xq, xs, st);
   else
     ln_quant_any_k<<<t, 256, 0, st>>>(h, o, g, b, d, xq, xs);
