@@ -77,18 +77,25 @@ __global__ void __launch_bounds__(128) conv1_k(const float* __restrict__ x, cons
 constexpr int TP_THREADS = 256;
 constexpr int TP_P = 5, TP_C = 4;  // positions x channels per thread
 
+// Staging of a stage: every copy is issued at once with cp.async (weight pairs straight from
+// the [out][tap] layout, 8 bytes each; the stage's raw input rows), waited for once, and the
+// interleaved X2 is then built from shared memory through a per-block table of tap offsets.
 constexpr int CV2_CH = 32;                 // output channels per block
 constexpr int CV2_CC = 4;                  // input channels per stage
 constexpr int CV2_MP = CV2_CC * 49 / 2;    // tap pairs per stage (98)
-constexpr int CV2_WS = CV2_CH + 2;         // W2 row stride in float2 (16-byte rows, 4-way staging stores)
+constexpr int CV2_WS = CV2_CH + 2;         // W2 row stride in float2 (16-byte rows)
+constexpr int CV2_RW = 48;                 // raw row: 4 zeros | 40 values | 4 zeros (16-byte aligned data)
+constexpr int CV2_RAW = 7 * CV2_CC * CV2_RW;
 constexpr int cmax(int a, int b) { return a > b ? a : b; }
-constexpr int CV2_SMEM = cmax(CV2_MP * (DIM + CV2_WS) * 8, 4 * CV2_CH * DIM * 8);
+constexpr int CV2_SMEM = cmax(CV2_MP * (DIM + CV2_WS) * 8 + CV2_RAW * 4 + 2 * CV2_MP * 4, 4 * CV2_CH * DIM * 8);
 
 constexpr int CV3_CH = 64;
 constexpr int CV3_CC = 8;
 constexpr int CV3_MP = CV3_CC * 9 / 2;     // 36
 constexpr int CV3_WS = CV3_CH + 2;
-constexpr int CV3_SMEM = cmax(CV3_MP * (20 + CV3_WS) * 8, 4 * CV3_CH * 20 * 8);
+constexpr int CV3_RW = 44;                 // raw row: the 41 values of a channel (+ unused pad)
+constexpr int CV3_RAW = 3 * CV3_CC * CV3_RW;
+constexpr int CV3_SMEM = cmax(CV3_MP * (20 + CV3_WS) * 8 + CV3_RAW * 4 + 2 * CV3_MP * 4, 4 * CV3_CH * 20 * 8);
 
 __device__ __forceinline__ float2 mulp(float2 a, float2 b) {
   return make_float2(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y));
@@ -136,11 +143,26 @@ __global__ void __launch_bounds__(TP_THREADS, 3) conv2_k(const float* __restrict
   extern __shared__ __align__(16) float sm[];
   float2* X2 = reinterpret_cast<float2*>(sm);    // [98][40]
   float2* Wt = X2 + CV2_MP * DIM;                 // [98][34]
+  float* raw = reinterpret_cast<float*>(Wt + CV2_MP * CV2_WS);  // [7 rows][4 channels][48]
+  int* tapoff = reinterpret_cast<int*>(raw + CV2_RAW);          // [196] tap -> raw offset (+ f)
   const int r = blockIdx.x, og = blockIdx.y, tid = threadIdx.x;
   const int sw = s.seg_of_row(r);
   const int fb = s.frame_begin(sw), t = s.frames(sw), ti = r - s.row_begin(sw);
   const int q = tid >> 6, idx = tid & 63;
   const int f0 = (idx & 7) * TP_P, o0 = (idx >> 3) * TP_C;
+  // tap c*49 + i*7 + j of a stage reads raw row (i, c) at column f + j + 1 (= x column f+j-3, +4)
+  for (int e = tid; e < 2 * CV2_MP; e += TP_THREADS) {
+    const int cl = e / 49, rem = e - cl * 49, i = rem / 7, j = rem - i * 7;
+    tapoff[e] = (i * CV2_CC + cl) * CV2_RW + j + 1;
+  }
+  // zeros that no copy overwrites: the pad columns, and whole rows outside the segment
+  for (int e = tid; e < CV2_RAW; e += TP_THREADS) {
+    const int col = e % CV2_RW, i = e / (CV2_RW * CV2_CC);
+    const int tt = ti * 5 + i - 1;
+    if (col < 4 || col >= 4 + DIM || tt < 0 || tt >= t) raw[e] = 0.0f;
+  }
+  const bool w8 = (reinterpret_cast<uintptr_t>(c2) & 7) == 0;
+  const bool x16 = (reinterpret_cast<uintptr_t>(y1) & 15) == 0;
   float2 acc[TP_P][TP_C];
 #pragma unroll
   for (int p = 0; p < TP_P; p++)
@@ -148,26 +170,38 @@ __global__ void __launch_bounds__(TP_THREADS, 3) conv2_k(const float* __restrict
     for (int c = 0; c < TP_C; c++) acc[p][c] = make_float2(0.0f, 0.0f);
 #pragma unroll 1
   for (int c0 = 0; c0 < C1; c0 += CV2_CC) {
-    __syncthreads();
-#pragma unroll 1
+    __syncthreads();  // the previous stage is consumed (and the zeros / offsets are visible)
     for (int e = tid; e < CV2_MP * CV2_CH; e += TP_THREADS) {
       const int o = e / CV2_MP, m = e - o * CV2_MP;
       const float* w = c2 + static_cast<int64_t>(og * CV2_CH + o) * K2 + c0 * 49 + 2 * m;
-      Wt[m * CV2_WS + o] = make_float2(__ldg(w), __ldg(w + 1));
+      float2* d = Wt + m * CV2_WS + o;
+      if (w8) {
+        cp_async8(d, w);
+      } else {
+        cp_async4(d, w);
+        cp_async4(reinterpret_cast<float*>(d) + 1, w + 1);
+      }
     }
-#pragma unroll 1
+    for (int e = tid; e < 7 * CV2_CC * (DIM / 4); e += TP_THREADS) {
+      const int row = e / (DIM / 4), p4 = e - row * (DIM / 4), i = row / CV2_CC, cl = row - i * CV2_CC;
+      const int tt = ti * 5 + i - 1;
+      if (tt >= 0 && tt < t) {
+        const float* src = y1 + static_cast<int64_t>(fb + tt) * (C1 * DIM) + (c0 + cl) * DIM + 4 * p4;
+        float* d = raw + row * CV2_RW + 4 + 4 * p4;
+        if (x16) {
+          cp_async16(d, src);
+        } else {
+#pragma unroll
+          for (int u = 0; u < 4; u++) cp_async4(d + u, src + u);
+        }
+      }
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
     for (int e = tid; e < CV2_MP * DIM; e += TP_THREADS) {
       const int m = e / DIM, f = e - m * DIM;
-      float v[2];
-#pragma unroll
-      for (int h = 0; h < 2; h++) {
-        const int tp = 2 * m + h, cl = tp / 49, rem = tp - cl * 49, i = rem / 7, j = rem - i * 7;
-        const int tt = ti * 5 + i - 1, ff = f + j - 3;
-        v[h] = (tt >= 0 && tt < t && ff >= 0 && ff < DIM)
-                   ? __ldg(y1 + static_cast<int64_t>(fb + tt) * (C1 * DIM) + (c0 + cl) * DIM + ff)
-                   : 0.0f;
-      }
-      X2[e] = make_float2(v[0], v[1]);
+      X2[e] = make_float2(raw[tapoff[2 * m] + f], raw[tapoff[2 * m + 1] + f]);
     }
     __syncthreads();
     tp_accumulate<DIM, CV2_WS, 2>(X2, Wt, CV2_MP, (q - (c0 >> 1)) & 3, f0, o0, acc);
@@ -195,11 +229,23 @@ __global__ void __launch_bounds__(TP_THREADS, 3) conv3_k(const float* __restrict
   extern __shared__ __align__(16) float sm[];
   float2* X2 = reinterpret_cast<float2*>(sm);    // [36][20]
   float2* Wt = X2 + CV3_MP * 20;                  // [36][66]
+  float* raw = reinterpret_cast<float*>(Wt + CV3_MP * CV3_WS);  // [3 rows][8 channels][44]
+  int* tapoff = reinterpret_cast<int*>(raw + CV3_RAW);          // [72] tap -> raw offset (+ 2f)
   const int r = blockIdx.x, og = blockIdx.y, tid = threadIdx.x;
   const int sw = s.seg_of_row(r);
   const int rb = s.row_begin(sw), t1 = s.rows(sw), ti = r - rb;
   const int q = tid >> 6, idx = tid & 63;
   const int f0 = (idx & 3) * TP_P, o0 = (idx >> 2) * TP_C;
+  // tap c*9 + i*3 + j of a stage reads raw row (i, c) at column 2f + j
+  for (int e = tid; e < 2 * CV3_MP; e += TP_THREADS) {
+    const int cl = e / 9, rem = e - cl * 9, i = rem / 3, j = rem - i * 3;
+    tapoff[e] = (i * CV3_CC + cl) * CV3_RW + j;
+  }
+  for (int e = tid; e < CV3_RAW; e += TP_THREADS) {  // rows outside the segment stay zero
+    const int i = e / (CV3_RW * CV3_CC), tt = ti + i - 1;
+    if (tt < 0 || tt >= t1) raw[e] = 0.0f;
+  }
+  const bool w8 = (reinterpret_cast<uintptr_t>(c3) & 7) == 0;
   float2 acc[TP_P][TP_C];
 #pragma unroll
   for (int p = 0; p < TP_P; p++)
@@ -208,23 +254,29 @@ __global__ void __launch_bounds__(TP_THREADS, 3) conv3_k(const float* __restrict
 #pragma unroll 1
   for (int c0 = 0; c0 < C2; c0 += CV3_CC) {
     __syncthreads();
-#pragma unroll 1
     for (int e = tid; e < CV3_MP * CV3_CH; e += TP_THREADS) {
       const int o = e / CV3_MP, m = e - o * CV3_MP;
       const float* w = c3 + static_cast<int64_t>(og * CV3_CH + o) * K3 + c0 * 9 + 2 * m;
-      Wt[m * CV3_WS + o] = make_float2(__ldg(w), __ldg(w + 1));
+      float2* d = Wt + m * CV3_WS + o;
+      if (w8) {
+        cp_async8(d, w);
+      } else {
+        cp_async4(d, w);
+        cp_async4(reinterpret_cast<float*>(d) + 1, w + 1);
+      }
     }
+    for (int e = tid; e < 3 * CV3_CC * W2; e += TP_THREADS) {
+      const int row = e / W2, col = e - row * W2, i = row / CV3_CC, cl = row - i * CV3_CC;
+      const int tt = ti + i - 1;
+      if (tt >= 0 && tt < t1)
+        cp_async4(raw + row * CV3_RW + col, y2 + static_cast<int64_t>(rb + tt) * (C2 * W2) + (c0 + cl) * W2 + col);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
     for (int e = tid; e < CV3_MP * 20; e += TP_THREADS) {
       const int m = e / 20, f = e - m * 20;
-      float v[2];
-#pragma unroll
-      for (int h = 0; h < 2; h++) {
-        const int tp = 2 * m + h, cl = tp / 9, rem = tp - cl * 9, i = rem / 3, j = rem - i * 3;
-        const int tt = ti + i - 1;
-        v[h] = (tt >= 0 && tt < t1) ? __ldg(y2 + static_cast<int64_t>(rb + tt) * (C2 * W2) + (c0 + cl) * W2 + 2 * f + j)
-                                    : 0.0f;
-      }
-      X2[e] = make_float2(v[0], v[1]);
+      X2[e] = make_float2(raw[tapoff[2 * m] + 2 * f], raw[tapoff[2 * m + 1] + 2 * f]);
     }
     __syncthreads();
     tp_accumulate<20, CV3_WS, 1>(X2, Wt, CV3_MP, (q - (c0 >> 1)) & 3, f0, o0, acc);
@@ -312,14 +364,6 @@ struct LnCfg {
 
 __device__ __forceinline__ float4 add4_rn(float4 a, float4 b) {
   return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
-}
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 template <bool RES>
@@ -738,25 +782,55 @@ __global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, co
   __syncthreads();
   // ---- softmax: row max (order-free, warp per row), exp (element-wise), sequential row sum
   float* Sf = reinterpret_cast<float*>(S2);
+  // (element loops run 4 independent elements per lane: the exp is a long dependent chain)
   for (int i = warp; i < ni; i += 8) {
     float* row = Sf + (i >> 1) * sp * 2 + (i & 1);
-    float m = -3.40282347e+38f;
-    for (int j = lane; j < t; j += 32) m = fmaxf(m, row[2 * j]);
-    m = warp_max(m);
-    for (int j = lane; j < t; j += 32) row[2 * j] = expf_ref_smem(__fsub_rn(row[2 * j], m), tab);
+    float m4[4] = {-3.40282347e+38f, -3.40282347e+38f, -3.40282347e+38f, -3.40282347e+38f};
+    int j = lane;
+    for (; j + 96 < t; j += 128) {
+#pragma unroll
+      for (int u = 0; u < 4; u++) m4[u] = fmaxf(m4[u], row[2 * (j + 32 * u)]);
+    }
+    for (; j < t; j += 32) m4[0] = fmaxf(m4[0], row[2 * j]);
+    const float m = warp_max(fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
+    j = lane;
+    for (; j + 96 < t; j += 128) {
+      float a[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) a[u] = row[2 * (j + 32 * u)];
+#pragma unroll
+      for (int u = 0; u < 4; u++) row[2 * (j + 32 * u)] = expf_ref_smem(__fsub_rn(a[u], m), tab);
+    }
+    for (; j < t; j += 32) row[2 * j] = expf_ref_smem(__fsub_rn(row[2 * j], m), tab);
   }
   __syncthreads();
-  if (tid < ni) {
+  if (tid < ni) {  // z: a left fold over j, loads issued 8 at a time ahead of the adds
     const float* row = Sf + (tid >> 1) * sp * 2 + (tid & 1);
     float z = 0.0f;
-    for (int j = 0; j < t; j++) z = __fadd_rn(z, row[2 * j]);
+    int j = 0;
+    for (; j + 8 <= t; j += 8) {
+      float x[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) x[u] = row[2 * (j + u)];
+#pragma unroll
+      for (int u = 0; u < 8; u++) z = __fadd_rn(z, x[u]);
+    }
+    for (; j < t; j++) z = __fadd_rn(z, row[2 * j]);
     Z[tid] = z;
   }
   __syncthreads();
-  for (int e = tid; e < ni * t; e += 256) {
-    const int i = e / t, j = e - i * t;
-    float* x = Sf + (i >> 1) * sp * 2 + (i & 1) + 2 * j;
-    *x = __fdiv_rn(*x, Z[i]);
+  for (int i = warp; i < ni; i += 8) {  // p_j = e_j / z, warp per row
+    float* row = Sf + (i >> 1) * sp * 2 + (i & 1);
+    const float z = Z[i];
+    int j = lane;
+    for (; j + 96 < t; j += 128) {
+      float a[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) a[u] = row[2 * (j + 32 * u)];
+#pragma unroll
+      for (int u = 0; u < 4; u++) row[2 * (j + 32 * u)] = __fdiv_rn(a[u], z);
+    }
+    for (; j < t; j += 32) row[2 * j] = __fdiv_rn(row[2 * j], z);
   }
   // ---- PV
   const int pr = 8 * (warp & 1) + (lane & 7), dt = 4 * (warp >> 1) + (lane >> 3);
