@@ -77,7 +77,7 @@ struct WasrModel {
   unsigned* rowmax = nullptr;
   unsigned long long* keys = nullptr;
   uint32_t* ids = nullptr;
-  int* seg = nullptr;  // segment tables of eager runs: foff | roff | toff
+  int* seg = nullptr;  // segment tables of eager runs: foff | roff | toff | tord
   int seg_cap = 0;
   int* err_host = nullptr;
   int* err_dev = nullptr;
@@ -193,7 +193,7 @@ struct Launcher {
 };
 
 // Enqueue the whole forward of one chunk on m->stream.  The chunk's frames are at m->feats;
-// seg points at its device segment tables [foff n+1 | roff n+1 | toff n+1].
+// seg points at its device segment tables [foff n+1 | roff n+1 | toff n+1 | tord tiles].
 int enqueue_chunk(WasrModel* m, const Chunk& c, const int* seg, float* logits, Launcher& K) {
   cudaStream_t st = m->stream;
   const int n = c.w1 - c.w0;
@@ -202,6 +202,7 @@ int enqueue_chunk(WasrModel* m, const Chunk& c, const int* seg, float* logits, L
   s.roff = seg + (n + 1);
   s.n = n;
   const int* toff = seg + 2 * (n + 1);
+  const int* tord = seg + 3 * (n + 1);
   const int M = c.rows;
   const WasrPlan& P = m->plan;
   // conv frontend -> y3 -> int8 -> linear (src/model.rs:389-478,489)
@@ -228,7 +229,7 @@ int enqueue_chunk(WasrModel* m, const Chunk& c, const int* seg, float* logits, L
         }));
     }
     // attention -> quant -> o projection, residual fused (src/model.rs:493)
-    TRY(K(WASR_K_ATTN, [&] { return launch_attention(m->qkv, m->qkv + D, m->qkv + 2 * D, 3 * D, s, toff, c.tiles, c.max_t1, m->att, D, st); }));
+    TRY(K(WASR_K_ATTN, [&] { return launch_attention(m->qkv, m->qkv + D, m->qkv + 2 * D, 3 * D, s, toff, tord, c.tiles, c.max_t1, m->att, D, st); }));
     TRY(K(WASR_K_QUANT, [&] { return launch_quant_rows(m->att, M, D, D, m->xq, m->xs, st); }));
     TRY(K(WASR_K_GEMM_O, [&] { return gemm_run(gemm_args(m, m->xq, m->xs, M, D, L.o, D, L.ob, EPI_F32_ADD, m->h, D), st); }));
     // middle norm -> f1 + bias + GELU (+ row max) -> quant -> f2 + bias, residual fused
@@ -255,12 +256,15 @@ int enqueue_chunk(WasrModel* m, const Chunk& c, const int* seg, float* logits, L
   return 0;
 }
 
-// segment tables of windows [w0, w1): foff | roff | toff, each n+1 ints
+// segment tables of windows [w0, w1): foff | roff | toff (each n+1 ints) | tord (one int per
+// attention tile: the tiles in launch order, longest segment first, so the longest blocks
+// start in the first wave)
 void build_seg(const int32_t* t, int w0, int w1, int* out) {
   const int n = w1 - w0;
   int* fo = out;
   int* ro = out + n + 1;
   int* to = out + 2 * (n + 1);
+  int* tord = out + 3 * (n + 1);
   fo[0] = ro[0] = to[0] = 0;
   for (int i = 0; i < n; i++) {
     const int tt = std::max(0, t[w0 + i]);
@@ -269,6 +273,12 @@ void build_seg(const int32_t* t, int w0, int w1, int* out) {
     ro[i + 1] = ro[i] + t1;
     to[i + 1] = to[i] + (t1 + ATT_QT - 1) / ATT_QT;
   }
+  std::vector<int> order(n);
+  for (int i = 0; i < n; i++) order[i] = i;
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return ro[a + 1] - ro[a] > ro[b + 1] - ro[b]; });
+  int k = 0;
+  for (int i : order)
+    for (int tl = to[i]; tl < to[i + 1]; tl++) tord[k++] = tl;
 }
 
 // split windows into chunks that fit the activation buffers
@@ -315,7 +325,7 @@ void free_graphs(WasrModel* m) {
 // else capture it (graphs on) or run it eagerly.
 int run_chunk(WasrModel* m, const int32_t* t, const Chunk& c, float* logits) {
   const int n = c.w1 - c.w0;
-  const size_t seg_ints = 3 * static_cast<size_t>(n + 1);
+  const size_t seg_ints = 3 * static_cast<size_t>(n + 1) + static_cast<size_t>(c.tiles);
   if (!hgrow(&m->h_seg, &m->h_seg_cap, seg_ints)) return -5;
   cudaStream_t st = m->stream;
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;

@@ -630,23 +630,23 @@ __global__ void keys_to_ids_k(const unsigned long long* __restrict__ keys, int m
 
 // ------------------------------------------------------------------------ attention
 // One block per (query tile, head).  A segment of t rows is cut into ceil(t/64) tiles of
-// equal size (at most 64 rows), so short last tiles do not waste work.  Scores
-// s_ij = dotf(q_i, k_j) * 0.125 (src/kernels.rs:172-183 order); softmax e_j = exp(s_j - max),
-// z = sequential sum, p_j = e_j / z; o_i[d] = sum over j in order of p_j * v_j[d] from 0
-// (src/model.rs:714-738).  Every element keeps the reference's exact sequence of rounded
-// multiplies and adds.
+// equal size (at most 64 rows), so short last tiles do not waste work; `tord` (optional)
+// lists the tiles longest segment first, so the longest blocks start in the first wave.
+// Scores s_ij = dotf(q_i, k_j) * 0.125 (src/kernels.rs:172-183 order); softmax
+// e_j = exp(s_j - max), z = sequential sum, p_j = e_j / z; o_i[d] = sum over j in order of
+// p_j * v_j[d] from 0 (src/model.rs:714-738).  Every element keeps the reference's exact
+// sequence of rounded multiplies and adds.
 //
-// Packed pairs.  Scores: a thread owns query rows (2r, 2r+1) x keys (kt + 8u, u < 4) of a
+// Register tiles.  Scores: a thread owns query rows (2r, 2r+1) x keys (kt + 8u, u < 4) of a
 // 32-key chunk and keeps all 8 dotf lanes of each score as 4 float2 (lanes 2l, 2l+1 take
-// dims 8c+2l, 8c+2l+1), so a product pair is q[d..d+1] * k[d..d+1] -- two register pairs.
-// PV: a thread owns row pairs (2p, 2p+1) for p = r, r+16 x head dims d0..d0+3; the
-// accumulators pair (row 2p, dim d) with (row 2p+1, dim d^1), so the products are
-// (p_2p, p_2p+1) x (v[d], v[d^1]) from V and a pair-swapped copy of V.
-// Shared layout: exp table | Q [64][68] + K [32][68] (scores) / V, Vs [32][64] (PV) |
-// S2 [32 row pairs][sp] float2 | Z [64].
+// dims 8c+2l, 8c+2l+1), so a product pair is q[d..d+1] * k[d..d+1].  PV: a thread owns row
+// pairs (2p, 2p+1) for p = r, r+16 x head dims d0..d0+3; the accumulators pair (row 2p, dim d)
+// with (row 2p+1, dim d^1).  K and V chunks stream through two shared buffers by cp.async,
+// one barrier per chunk.  Shared layout: exp table | Q [64][68] + K [2][32][68] (scores) /
+// V [2][32][64] (PV) | S2 [32 row pairs][sp] float2 | Z [64].
 constexpr int ATT_KC = 32;   // keys per chunk
 constexpr int ATT_RS = 68;   // Q / K row stride in floats (16-byte rows, conflict-free tiles)
-constexpr int ATT_A = (ATT_QT + ATT_KC) * ATT_RS;  // floats of the Q/K (and V/Vs) region
+constexpr int ATT_A = (ATT_QT + 2 * ATT_KC) * ATT_RS;  // floats of the Q/K (and V) region
 
 __host__ __device__ inline int att_pair_stride(int max_t1) { return ((max_t1 + 15) / 16) * 16 + 1; }
 
@@ -658,31 +658,37 @@ size_t attention_smem_bytes(int max_t1) {
 __device__ __forceinline__ float2 lo2(float4 a) { return make_float2(a.x, a.y); }
 __device__ __forceinline__ float2 hi2(float4 a) { return make_float2(a.z, a.w); }
 
-// rows [j0, j0+8*ATT_KC/... ) of K or V for head h: 2 float4 per thread (zeros past nj)
-__device__ __forceinline__ void att_fetch(const float* __restrict__ src, int ld, int rb, int j0, int nj, int h,
-                                          int tid, float4 (&r)[2]) {
+// rows [j0, j0+nj) of K / V / Q for head h into dst (row stride ds floats); rows past nj are
+// left as they are (never used).  16-byte copies when the source rows allow them.
+__device__ __forceinline__ void att_copy_rows(float* dst, int ds, const float* __restrict__ src, int ld, int r0,
+                                              int nj, int h, int tid, bool a16) {
+  for (int e = tid; e < nj * 16; e += 256) {
+    const int j = e >> 4, d4 = (e & 15) * 4;
+    const float* g = src + static_cast<int64_t>(r0 + j) * ld + h * HD + d4;
+    float* d = dst + j * ds + d4;
+    if (a16) {
+      cp_async16(d, g);
+    } else {
 #pragma unroll
-  for (int u = 0; u < 2; u++) {
-    const int e = tid + 256 * u, j = e >> 4, d4 = (e & 15) * 4;
-    r[u] = j < nj ? __ldg(reinterpret_cast<const float4*>(src + static_cast<int64_t>(rb + j0 + j) * ld + h * HD + d4))
-                  : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int u = 0; u < 4; u++) cp_async4(d + u, g + u);
+    }
   }
+  cp_async_commit();
 }
 
 __global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, const float* __restrict__ k,
                                                  const float* __restrict__ v, int ld, Segs s,
-                                                 const int* __restrict__ toff, int max_t1, float* __restrict__ out,
-                                                 int ldo) {
+                                                 const int* __restrict__ toff, const int* __restrict__ tord,
+                                                 int max_t1, float* __restrict__ out, int ldo) {
   extern __shared__ __align__(16) float sm[];
   const int sp = att_pair_stride(max_t1);
   unsigned long long* tab = reinterpret_cast<unsigned long long*>(sm);
-  float* Q = sm + 64;                 // [64][68]
-  float* K = Q + ATT_QT * ATT_RS;     // [32][68]
-  float* V = Q;                       // [32][64] (PV phase)
-  float* Vs = Q + ATT_KC * HD;        // [32][64] pair-swapped V
+  float* Q = sm + 64;                     // [64][68]
+  float* Kb = Q + ATT_QT * ATT_RS;        // [2][32][68]
+  float* Vb = Q;                          // [2][32][64] (PV phase)
   float2* S2 = reinterpret_cast<float2*>(Q + ATT_A);  // [32][sp]
   float* Z = reinterpret_cast<float*>(S2 + (ATT_QT / 2) * sp);
-  const int tile = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  const int tile = tord ? tord[blockIdx.x] : blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
   int sw = 0;
   if (toff) {
     int lo = 0, hi = s.n - 1;
@@ -698,33 +704,28 @@ __global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, co
   const int i0 = qt * rpt;
   const int ni = min(rpt, t - i0);
   if (ni <= 0 || t > max_t1) return;
+  const bool a16 = ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) &
+                    15) == 0 &&
+                   (ld & 3) == 0;
   if (tid < 32) tab[tid] = kExp2Tab[tid];
-  for (int e = tid; e < ATT_QT * 16; e += 256) {
-    const int i = e >> 4, d4 = (e & 15) * 4;
-    *reinterpret_cast<float4*>(Q + i * ATT_RS + d4) =
-        i < ni ? __ldg(reinterpret_cast<const float4*>(q + static_cast<int64_t>(rb + i0 + i) * ld + h * HD + d4))
-               : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
   const int warp = tid >> 5, lane = tid & 31;
   const int nchunks = (t + ATT_KC - 1) / ATT_KC;
   // ---- scores
+  att_copy_rows(Q, ATT_RS, q, ld, rb + i0, ni, h, tid, a16);
+  att_copy_rows(Kb, ATT_RS, k, ld, rb, min(ATT_KC, t), h, tid, a16);
   {
     const int rt = 8 * (warp & 3) + (lane & 7), kt = 4 * (warp >> 2) + (lane >> 3);
     const bool live = 16 * (warp & 3) < ni;  // warp-uniform
     const float* qa = Q + (2 * rt) * ATT_RS;
     const float* qb = qa + ATT_RS;
-    float4 pre[2];
-    att_fetch(k, ld, rb, 0, min(ATT_KC, t), h, tid, pre);
     for (int ch = 0; ch < nchunks; ch++) {
       const int j0 = ch * ATT_KC, nj = min(ATT_KC, t - j0);
-      __syncthreads();  // previous chunk consumed (and Q staged)
-#pragma unroll
-      for (int u = 0; u < 2; u++) {
-        const int e = tid + 256 * u, j = e >> 4, d4 = (e & 15) * 4;
-        *reinterpret_cast<float4*>(K + j * ATT_RS + d4) = pre[u];
-      }
-      if (ch + 1 < nchunks) att_fetch(k, ld, rb, j0 + ATT_KC, min(ATT_KC, t - j0 - ATT_KC), h, tid, pre);
-      __syncthreads();
+      cp_async_wait<0>();
+      __syncthreads();  // chunk ch (and Q) visible; chunk ch-1 consumed by every warp
+      if (ch + 1 < nchunks)
+        att_copy_rows(Kb + ((ch + 1) & 1) * ATT_KC * ATT_RS, ATT_RS, k, ld, rb + j0 + ATT_KC,
+                      min(ATT_KC, t - j0 - ATT_KC), h, tid, a16);
+      const float* K = Kb + (ch & 1) * ATT_KC * ATT_RS;
       if (live) {
         float2 acc[2][4][4];
 #pragma unroll
@@ -776,10 +777,9 @@ __global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, co
       }
     }
   }
-  // prefetch the first V chunk while the softmax runs
-  float4 pre[2];
-  att_fetch(v, ld, rb, 0, min(ATT_KC, t), h, tid, pre);
-  __syncthreads();
+  __syncthreads();  // scores complete; the Q/K region is free
+  // the first V chunk streams in while the softmax runs
+  att_copy_rows(Vb, HD, v, ld, rb, min(ATT_KC, t), h, tid, a16);
   // ---- softmax: row max (order-free, warp per row), exp (element-wise), sequential row sum
   float* Sf = reinterpret_cast<float*>(S2);
   // (element loops run 4 independent elements per lane: the exp is a long dependent chain)
@@ -842,45 +842,37 @@ __global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, co
     for (int u = 0; u < 4; u++) o[a][u] = make_float2(0.0f, 0.0f);
   for (int ch = 0; ch < nchunks; ch++) {
     const int j0 = ch * ATT_KC, nj = min(ATT_KC, t - j0);
-    __syncthreads();
-#pragma unroll
-    for (int u = 0; u < 2; u++) {
-      const int e = tid + 256 * u, j = e >> 4, d4 = (e & 15) * 4;
-      const float4 x = pre[u];
-      *reinterpret_cast<float4*>(V + j * HD + d4) = x;
-      *reinterpret_cast<float4*>(Vs + j * HD + d4) = make_float4(x.y, x.x, x.w, x.z);
-    }
-    if (ch + 1 < nchunks) att_fetch(v, ld, rb, j0 + ATT_KC, min(ATT_KC, t - j0 - ATT_KC), h, tid, pre);
-    __syncthreads();
+    cp_async_wait<0>();
+    __syncthreads();  // V chunk ch and all probabilities visible; chunk ch-1 consumed
+    if (ch + 1 < nchunks)
+      att_copy_rows(Vb + ((ch + 1) & 1) * ATT_KC * HD, HD, v, ld, rb + j0 + ATT_KC, min(ATT_KC, t - j0 - ATT_KC), h,
+                    tid, a16);
     const float2* p0 = S2 + pr * sp + j0;
     const float2* p1 = S2 + (pr + 16) * sp + j0;
-    const float* vr = V + 4 * dt;
-    const float* vsr = Vs + 4 * dt;
+    const float* vr = Vb + (ch & 1) * ATT_KC * HD + 4 * dt;
     if (live1) {
 #pragma unroll 4
       for (int jj = 0; jj < nj; jj++) {
         const float2 pa = p0[jj], pb = p1[jj];
         const float4 x = *reinterpret_cast<const float4*>(vr + jj * HD);
-        const float4 y = *reinterpret_cast<const float4*>(vsr + jj * HD);
         o[0][0] = add2_rn(o[0][0], mulp(pa, lo2(x)));
-        o[0][1] = add2_rn(o[0][1], mulp(pa, lo2(y)));
+        o[0][1] = add2_rn(o[0][1], mulp(pa, make_float2(x.y, x.x)));
         o[0][2] = add2_rn(o[0][2], mulp(pa, hi2(x)));
-        o[0][3] = add2_rn(o[0][3], mulp(pa, hi2(y)));
+        o[0][3] = add2_rn(o[0][3], mulp(pa, make_float2(x.w, x.z)));
         o[1][0] = add2_rn(o[1][0], mulp(pb, lo2(x)));
-        o[1][1] = add2_rn(o[1][1], mulp(pb, lo2(y)));
+        o[1][1] = add2_rn(o[1][1], mulp(pb, make_float2(x.y, x.x)));
         o[1][2] = add2_rn(o[1][2], mulp(pb, hi2(x)));
-        o[1][3] = add2_rn(o[1][3], mulp(pb, hi2(y)));
+        o[1][3] = add2_rn(o[1][3], mulp(pb, make_float2(x.w, x.z)));
       }
     } else if (live0) {
 #pragma unroll 4
       for (int jj = 0; jj < nj; jj++) {
         const float2 pa = p0[jj];
         const float4 x = *reinterpret_cast<const float4*>(vr + jj * HD);
-        const float4 y = *reinterpret_cast<const float4*>(vsr + jj * HD);
         o[0][0] = add2_rn(o[0][0], mulp(pa, lo2(x)));
-        o[0][1] = add2_rn(o[0][1], mulp(pa, lo2(y)));
+        o[0][1] = add2_rn(o[0][1], mulp(pa, make_float2(x.y, x.x)));
         o[0][2] = add2_rn(o[0][2], mulp(pa, hi2(x)));
-        o[0][3] = add2_rn(o[0][3], mulp(pa, hi2(y)));
+        o[0][3] = add2_rn(o[0][3], mulp(pa, make_float2(x.w, x.z)));
       }
     }
   }
@@ -1001,12 +993,12 @@ int launch_keys_to_ids(const unsigned long long* keys, int m, uint32_t* ids, cud
   return launched();
 }
 int launch_attention(const float* q, const float* k, const float* v, int ld, Segs s, const int* toff,
-                     int total_tiles, int max_t1, float* out, int ldo, cudaStream_t st) {
+                     const int* tord, int total_tiles, int max_t1, float* out, int ldo, cudaStream_t st) {
   if (total_tiles <= 0) return 0;
   const size_t smem = attention_smem_bytes(max_t1);
   if (smem > 227 * 1024) return -2;
   set_smem(reinterpret_cast<const void*>(attn_k), 227 * 1024);  // the largest opt-in size; each launch passes its own
-  attn_k<<<dim3(total_tiles, HEADS), 256, smem, st>>>(q, k, v, ld, s, toff, max_t1, out, ldo);
+  attn_k<<<dim3(total_tiles, HEADS), 256, smem, st>>>(q, k, v, ld, s, toff, tord, max_t1, out, ldo);
   return launched();
 }
 
@@ -1096,7 +1088,7 @@ static int attention_abi(void* stream, const float* q, const float* k, const flo
   if (heads != HEADS) return -2;
   if (attention_smem_bytes(t) > 227 * 1024) return -2;
   const Segs s = one_seg(t * 5, t);  // only the row count matters to attention
-  return launch_attention(q, k, v, d, s, nullptr, (t + ATT_QT - 1) / ATT_QT, t, out, d,
+  return launch_attention(q, k, v, d, s, nullptr, nullptr, (t + ATT_QT - 1) / ATT_QT, t, out, d,
                           static_cast<cudaStream_t>(stream));
 }
 

@@ -59,10 +59,11 @@ int launch_argmax_rows(const float* x, int m, int n, uint32_t* out, cudaStream_t
 int launch_keys_to_ids(const unsigned long long* keys, int m, uint32_t* ids, cudaStream_t st);
 // attention over segments; q/k/v rows of stride ld floats (head h at column h*64).
 // toff: [n+1] prefix of per-segment query tiles (ceil(t1/ATT_QT)), or nullptr for the inline
-// segment; max_t1 bounds every segment's length (sizes the on-chip score tile).
+// segment; tord: optional [total_tiles] launch order of the tiles (longest segments first);
+// max_t1 bounds every segment's length (sizes the on-chip score tile).
 constexpr int ATT_QT = 64;
 int launch_attention(const float* q, const float* k, const float* v, int ld, Segs s, const int* toff,
-                     int total_tiles, int max_t1, float* out, int ldo, cudaStream_t st);
+                     const int* tord, int total_tiles, int max_t1, float* out, int ldo, cudaStream_t st);
 size_t attention_smem_bytes(int max_t1);
 // Set the kernels' shared-memory attributes on the current device (call outside capture).
 bool kern_prepare();
