@@ -102,7 +102,52 @@ def algorithmic_work(t1_list, n_layers=40, vocab=10502):
         "quant": rows * ((FLAT + n_layers * (D + FF) + D) * 5),
     }
     flops = {"attention": n_layers * 4.0 * sq * D}
-    return ops, byts, flops, rows
+    # exactly rounded fp32 multiply-adds (one FMUL + one FADD each on the CUDA-core pipe): the
+    # bound of the kernels that must reproduce the CPU's sequential float sums
+    macs = {
+        "attention": n_layers * sq * 8 * 64 * 2,      # QK^T and PV, 8 heads of 64
+        "conv2": rows * 64 * 40 * 32 * 49,
+        "conv3": rows * 192 * 20 * 64 * 9,
+    }
+    return ops, byts, flops, rows, macs
+
+
+# ---------------------------------------------------------------- int8 GEMM probe
+def gemm_probe(pkg, local, stream, peak_tops, M=16384, N=2048, K=2048, reps=20):
+    """The tcgen05 int8 GEMM alone on a compute-bound shape (int32 accumulators out, through
+    wp_gemm_i32), timed with CUDA events on the launching stream: the "int8 GEMM TOPS vs
+    peak" half of the metric.  A 256-row slice is checked against an int64 matmul."""
+    import torch
+    L = pkg.abi.load()
+    rng = np.random.default_rng(7)
+    w = rng.integers(-127, 128, size=(N, K), dtype=np.int8)
+    blob = np.ascontiguousarray(w).view(np.uint8).reshape(-1).copy()
+    ctx = L.wp_create(blob.ctypes.data, blob.size)
+    if not ctx:
+        return {"error": "wp_create failed"}
+    try:
+        a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=f"cuda:{local}")
+        out = torch.empty((M, N), dtype=torch.int32, device=f"cuda:{local}")
+        torch.cuda.synchronize()  # the operands were made on the default stream
+        L.wp_set_stream(ctx, stream.cuda_stream)
+        for _ in range(3):
+            L.wp_gemm_i32(ctx, a.data_ptr(), M, K, 0, N, stream.cuda_stream, out.data_ptr())
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            rc = L.wp_gemm_i32(ctx, a.data_ptr(), M, K, 0, N, stream.cuda_stream, out.data_ptr())
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        ref = a[:256].cpu().numpy().astype(np.int64) @ w.astype(np.int64).T
+        exact = bool(np.array_equal(out[:256].cpu().numpy(), ref.astype(np.int32)))
+        tops = 2.0 * M * N * K / (ms / 1e3) / 1e12
+        return {"M": M, "N": N, "K": K, "epilogue": "int32 accumulators", "rc": int(rc), "ms": round(ms, 4),
+                "tops": round(tops, 1), "peak": round(peak_tops, 1), "frac": round(tops / peak_tops, 4),
+                "exact_slice": exact, "unit": "TOPS"}
+    finally:
+        L.wp_destroy(ctx)
 
 
 # ---------------------------------------------------------------- clocks
@@ -233,6 +278,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-gemm-probe", action="store_true")
     ap.add_argument("--utts", type=int, default=0,
                     help="profiling aid: only the first N config-4 utterances (0 = all 512)")
     args = ap.parse_args()
@@ -338,7 +384,7 @@ def main():
     # ---- roofline of the dominant kernel class (last timed step, CUDA events on its stream)
     hbm, bf16, src = peaks()
     names = pkg.abi.KERNEL_CLASSES
-    ops, byts, flops, rows = algorithmic_work(t1, plan.n_layers)
+    ops, byts, flops, rows, macs = algorithmic_work(t1, plan.n_layers)
     dom = max(range(len(names)), key=lambda i: prof_ms[i])
     dname = names[dom]
     dms = prof_ms[dom]
@@ -346,8 +392,11 @@ def main():
     tf = os.path.join(ROOT, "profiles", "traffic_per_row.json")
     if os.path.exists(tf):
         tr = json.load(open(tf)).get(dname)
+        # units of the class per step: rows (frontend, lin), rows x layers, or 2 LayerNorms per layer
+        per_layer = 2 * plan.n_layers if dname == "layernorm" else (
+            1 if dname in ("conv1", "conv2", "conv3", "gemm_lin", "gemm_out_argmax") else plan.n_layers)
         if tr and prof_n[dom]:
-            traffic = round(tr * rows / prof_n[dom])
+            traffic = round(tr * rows * per_layer / prof_n[dom])
     if dname in ops:
         ach = ops[dname] / prof_n[dom] / (dms / prof_n[dom] / 1e3) / 1e12
         roof = {"kernel": dname, "bound": "tensor", "achieved": round(ach, 2), "peak": round(2 * bf16, 1),
@@ -360,10 +409,21 @@ def main():
         roof = {"kernel": dname, "bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(ach / hbm, 4), "traffic": traffic, "peak_source": f"{src} hbm_gbs",
                 "launches": int(prof_n[dom]), "avg_launch_us": round(dms / prof_n[dom] * 1e3, 2)}
+    if dname in macs and prof_n[dom]:
+        # CUDA-core roofline: 128 fp32 lanes per SM per clock at the sampled SM clock, 2 per MAC
+        sms = torch.cuda.get_device_properties(local).multi_processor_count
+        mhz = (clocks or {}).get("sm_mhz") or 1965.0
+        peak_mac = sms * 128 * mhz * 1e6 / 2 / 1e12
+        ach_mac = macs[dname] / (dms / 1e3) / 1e12
+        roof["fp32_exact"] = {"achieved": round(ach_mac, 3), "peak": round(peak_mac, 2), "unit": "TMAC/s",
+                              "frac": round(ach_mac / peak_mac, 4),
+                              "basis": f"{sms} SMs x 128 fp32 lanes x {mhz:.0f} MHz / 2 ops per exactly rounded MAC"}
     gemm_ops = sum(ops.values())
     gemm_ms = sum(prof_ms[names.index(k)] for k in ops)
     roof["all_gemms_tops"] = round(gemm_ops / (gemm_ms / 1e3) / 1e12, 2) if gemm_ms else None
     roof["kernel_ms_last_step"] = {names[i]: round(prof_ms[i], 3) for i in range(len(names)) if prof_n[i]}
+
+    gprobe = gemm_probe(pkg, local, stream, 2 * bf16) if (rank == 0 and not args.no_gemm_probe) else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -380,7 +440,8 @@ def main():
                            "rows_rank0": int(sum(t1)), "n_layers": plan.n_layers, "max_rows_per_chunk": args.max_rows,
                            "l2": "flushed (256 MiB write) before every timed step",
                            "parallelism": f"utterance-sharded LPT over {world} GPU(s), no collective"},
-                "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
+                "roofline": roof, "gemm_probe": gprobe, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": int(launches),
                 "clocks": clocks, "device_error": err}
         print(json.dumps(line), flush=True)
     eng.close()
