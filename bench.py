@@ -65,15 +65,56 @@ def peaks():
 
 # ---------------------------------------------------------------- workload
 def make_workload(pkg, shard, lengths):
-    """Synthetic audio of this rank's utterances -> product fbank features."""
-    feats, sils, secs = [], [], 0.0
+    """Synthetic audio of this rank's utterances -> product fbank features.  Also returns the
+    wall time of the host fbank calls alone (the shell's stage, reported as its own line)."""
+    feats, sils, secs, fb_s, pcms = [], [], 0.0, 0.0, []
     for i in shard:
         pcm = pkg.synth.make_audio(100000 + i, lengths[i])
+        t0 = time.perf_counter()
         f, s = pkg.fbank(pcm)
+        fb_s += time.perf_counter() - t0
         feats.append(f)
         sils.append(s)
+        pcms.append(pcm)
         secs += pcm.size / 16000.0
-    return feats, sils, secs
+    return feats, sils, secs, fb_s, pcms
+
+
+def gpu_fbank_line(pkg, pcms, feats, local, stream, reps=5):
+    """The batched GPU fbank (wasr_fbank_device) over this rank's whole PCM, resident in HBM,
+    timed with CUDA events on the launching stream; plus its agreement with the host fbank."""
+    import torch
+    L = pkg.abi.load()
+    dev = f"cuda:{local}"
+    soff = np.concatenate([[0], np.cumsum([p.size for p in pcms])]).astype(np.int64)
+    nfr = [f.shape[0] for f in feats]
+    foff = np.concatenate([[0], np.cumsum(nfr)]).astype(np.int64)
+    frames, n = int(foff[-1]), len(pcms)
+    pcm_d = torch.from_numpy(np.concatenate(pcms).astype(np.int16)).to(dev)
+    soff_d, foff_d = torch.from_numpy(soff).to(dev), torch.from_numpy(foff).to(dev)
+    raw = torch.empty((max(frames, 1), 40), dtype=torch.float64, device=dev)
+    out = torch.empty((max(frames, 1), 40), dtype=torch.float32, device=dev)
+    sil = torch.empty((n, 40), dtype=torch.float32, device=dev)
+    torch.cuda.synchronize()
+
+    def run():
+        return L.wasr_fbank_device(pcm_d.data_ptr(), soff_d.data_ptr(), foff_d.data_ptr(), n, frames, raw.data_ptr(),
+                                   out.data_ptr(), sil.data_ptr(), stream.cuda_stream)
+    for _ in range(2):
+        rc = run()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        rc = run()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    ref = np.concatenate(feats, 0).view(np.int32)
+    got = out[:frames].cpu().numpy().view(np.int32)
+    same = float(np.mean(got == ref)) if frames else 1.0
+    secs = float(sum(p.size for p in pcms)) / 16000.0
+    return {"value": round(secs / (ms / 1e3), 1), "unit": "audio-s/s", "rc": int(rc), "ms": round(ms, 3),
+            "frames": frames, "identical_to_host": same, "impl": "wasr_fbank_device (f64 FFT512 per frame block)"}
 
 
 def algorithmic_work(t1_list, n_layers=40, vocab=10502):
@@ -307,7 +348,7 @@ def main():
         lengths = lengths[:args.utts]
     shards = pkg.synth.lpt_shards(lengths, world)
     shard = shards[rank]
-    feats, sils, my_audio = make_workload(pkg, shard, lengths)
+    feats, sils, my_audio, fbank_s, pcms = make_workload(pkg, shard, lengths)
     total_audio = float(sum(lengths))
     blob, plan = pkg.synth.make_model(seed=1, n_layers=40)
     eng = pkg.Engine(blob, plan, device=local, max_rows=args.max_rows)
@@ -424,6 +465,7 @@ def main():
     roof["kernel_ms_last_step"] = {names[i]: round(prof_ms[i], 3) for i in range(len(names)) if prof_n[i]}
 
     gprobe = gemm_probe(pkg, local, stream, 2 * bf16) if (rank == 0 and not args.no_gemm_probe) else None
+    fbg = gpu_fbank_line(pkg, pcms, feats, local, stream) if (rank == 0 and not args.no_gemm_probe) else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -441,6 +483,10 @@ def main():
                            "l2": "flushed (256 MiB write) before every timed step",
                            "parallelism": f"utterance-sharded LPT over {world} GPU(s), no collective"},
                 "roofline": roof, "gemm_probe": gprobe, "cpu_baseline": cpu, "e2e": e2e,
+                "fbank_host": {"value": round(my_audio / fbank_s, 1) if fbank_s > 0 else None, "unit": "audio-s/s",
+                               "threads": os.cpu_count(), "scope": "rank 0's utterances, one call per utterance",
+                               "impl": "host C++ f64 FFT512 + CMS (src/fbank.rs), OpenMP over frames"},
+                "fbank_gpu": fbg,
                 "gpu_launches": int(launches),
                 "clocks": clocks, "device_error": err}
         print(json.dumps(line), flush=True)

@@ -136,6 +136,20 @@ int wasr_transcribe(WasrModel* m, const float* feats, const int64_t* n_frames, c
  * utterance's silence frame.  Returns the frame count (or, if feats is NULL, the count only). */
 int64_t wasr_fbank(const int16_t* pcm, int64_t n, float* feats, int64_t cap, float* sil);
 
+/* The same fbank on the GPU, batched over n utterances (src/fbank.rs:79-156; no counterpart
+ * in the reference's C ABI, where fbank always runs in the Rust shell).  All pointers are
+ * device pointers on the current device:
+ *   pcm   int16 samples of all utterances, utterance i at [soff[i], soff[i+1]);
+ *   soff  [n+1] sample offsets;  foff [n+1] frame offsets, foff[i+1] - foff[i] =
+ *         (soff[i+1] - soff[i] - 400) / 160 + 1, or 0 below 400 samples;
+ *   raw   scratch, frames x 40 doubles;  feats frames x 40 floats;  sil n x 40 floats (each
+ *         utterance's CMS-normalised silence frame).
+ * Stream-ordered on `stream`; returns 0, -1 for a null pointer, -4 for a launch failure.
+ * The f32 features equal wasr_fbank's except where CUDA's double log and the host libm's differ
+ * in the last place and the result sits on an f32 rounding boundary. */
+int wasr_fbank_device(const int16_t* pcm, const int64_t* soff, const int64_t* foff, int n, int64_t frames,
+                      double* raw, float* feats, float* sil, void* stream);
+
 /* CTC collapse (Model::text without the vocabulary, src/model.rs:622-642): drop repeats
  * and blank id 0.  Returns the collapsed length. */
 int64_t wasr_ctc_collapse(const uint32_t* ids, int64_t n, uint32_t* out);

@@ -16,7 +16,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 OUT = os.path.join(HERE, "libwasr_gpu.so")
-SOURCES = ["gemm.cu", "kern.cu", "ctx.cu", "engine.cu"]
+SOURCES = ["gemm.cu", "kern.cu", "ctx.cu", "engine.cu", "fbank.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

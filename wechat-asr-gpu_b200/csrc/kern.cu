@@ -7,6 +7,7 @@
 // keeps the CPU's order too (8-lane dot, sequential softmax sum, sequential PV sum), and the
 // softmax exp and the GELU tanh are restatements of glibc's algorithms (common.cuh), so they
 // are bit-exact as well.
+#include <algorithm>
 #include <cstdio>
 #include <mutex>
 #include <set>
@@ -139,13 +140,14 @@ __device__ __forceinline__ float tp_fold(const float2* part, int nch, int npos, 
 // outside the segment / the 40 columns), column 40 = 0 -- src/model.rs:420-444.
 // Block = (row r, 32 output channels); stages of 4 input channels.
 __global__ void __launch_bounds__(TP_THREADS, 3) conv2_k(const float* __restrict__ y1, const float* __restrict__ c2,
-                                                      Segs s, float* __restrict__ y2) {
+                                                      Segs s, int row0, float* __restrict__ y2) {
   extern __shared__ __align__(16) float sm[];
   float2* X2 = reinterpret_cast<float2*>(sm);    // [98][40]
   float2* Wt = X2 + CV2_MP * DIM;                 // [98][34]
   float* raw = reinterpret_cast<float*>(Wt + CV2_MP * CV2_WS);  // [7 rows][4 channels][48]
   int* tapoff = reinterpret_cast<int*>(raw + CV2_RAW);          // [196] tap -> raw offset (+ f)
-  const int r = blockIdx.x, og = blockIdx.y, tid = threadIdx.x;
+  // the channel groups of a row are adjacent blocks: they read the same input rows from L2
+  const int r = row0 + blockIdx.y, og = blockIdx.x, tid = threadIdx.x;
   const int sw = s.seg_of_row(r);
   const int fb = s.frame_begin(sw), t = s.frames(sw), ti = r - s.row_begin(sw);
   const int q = tid >> 6, idx = tid & 63;
@@ -225,13 +227,14 @@ __global__ void __launch_bounds__(TP_THREADS, 3) conv2_k(const float* __restrict
 // outside the segment) -- src/model.rs:446-468.  Block = (row r, 64 output channels);
 // stages of 8 input channels.
 __global__ void __launch_bounds__(TP_THREADS, 3) conv3_k(const float* __restrict__ y2, const float* __restrict__ c3,
-                                                      Segs s, float* __restrict__ y3) {
+                                                      Segs s, int row0, float* __restrict__ y3) {
   extern __shared__ __align__(16) float sm[];
   float2* X2 = reinterpret_cast<float2*>(sm);    // [36][20]
   float2* Wt = X2 + CV3_MP * 20;                  // [36][66]
   float* raw = reinterpret_cast<float*>(Wt + CV3_MP * CV3_WS);  // [3 rows][8 channels][44]
   int* tapoff = reinterpret_cast<int*>(raw + CV3_RAW);          // [72] tap -> raw offset (+ 2f)
-  const int r = blockIdx.x, og = blockIdx.y, tid = threadIdx.x;
+  // the channel groups of a row are adjacent blocks: they read the same input rows from L2
+  const int r = row0 + blockIdx.y, og = blockIdx.x, tid = threadIdx.x;
   const int sw = s.seg_of_row(r);
   const int rb = s.row_begin(sw), t1 = s.rows(sw), ti = r - rb;
   const int q = tid >> 6, idx = tid & 63;
@@ -930,13 +933,15 @@ int launch_conv1(const float* x, const float* c1, Segs s, int total_frames, floa
 int launch_conv2(const float* y1, const float* c2, Segs s, int total_rows, float* y2, cudaStream_t st) {
   if (total_rows <= 0) return 0;
   set_smem(reinterpret_cast<const void*>(conv2_k), CV2_SMEM);
-  conv2_k<<<dim3(total_rows, C2 / CV2_CH), TP_THREADS, CV2_SMEM, st>>>(y1, c2, s, y2);
+  for (int r0 = 0; r0 < total_rows; r0 += 65535)  // grid.y limit
+    conv2_k<<<dim3(C2 / CV2_CH, std::min(65535, total_rows - r0)), TP_THREADS, CV2_SMEM, st>>>(y1, c2, s, r0, y2);
   return launched();
 }
 int launch_conv3(const float* y2, const float* c3, Segs s, int total_rows, float* y3, cudaStream_t st) {
   if (total_rows <= 0) return 0;
   set_smem(reinterpret_cast<const void*>(conv3_k), CV3_SMEM);
-  conv3_k<<<dim3(total_rows, C3 / CV3_CH), TP_THREADS, CV3_SMEM, st>>>(y2, c3, s, y3);
+  for (int r0 = 0; r0 < total_rows; r0 += 65535)  // grid.y limit
+    conv3_k<<<dim3(C3 / CV3_CH, std::min(65535, total_rows - r0)), TP_THREADS, CV3_SMEM, st>>>(y2, c3, s, r0, y3);
   return launched();
 }
 int launch_quant_rows(const float* x, int m, int k, int ldx, int8_t* xq, float* xs, cudaStream_t st) {
