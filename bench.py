@@ -484,7 +484,8 @@ def main():
                            "parallelism": f"utterance-sharded LPT over {world} GPU(s), no collective"},
                 "roofline": roof, "gemm_probe": gprobe, "cpu_baseline": cpu, "e2e": e2e,
                 "fbank_host": {"value": round(my_audio / fbank_s, 1) if fbank_s > 0 else None, "unit": "audio-s/s",
-                               "threads": os.cpu_count(), "scope": "rank 0's utterances, one call per utterance",
+                               "threads": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count())),
+                               "scope": "rank 0's utterances, one call per utterance",
                                "impl": "host C++ f64 FFT512 + CMS (src/fbank.rs), OpenMP over frames"},
                 "fbank_gpu": fbg,
                 "gpu_launches": int(launches),
