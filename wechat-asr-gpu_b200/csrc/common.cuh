@@ -264,13 +264,50 @@ __device__ __forceinline__ float expm1f_ref(float x) {
 
 // tanhf, branch-free: tanh(|x|) = 1 - 2/(expm1(2|x|)+2) for |x| >= 1, -t/(t+2) with
 // t = expm1(-2|x|) below 1, 1 - 1e-30 from 22 on; odd symmetry; the tiny / zero / non-finite
-// cases of the reference algorithm as selects.
+// cases of the reference algorithm as selects.  The expm1 is fdlibm's, specialised to the two
+// argument ranges tanh gives it: y in (-2, 0] (k = 0, -1, -2 or -3) and y in [2, 44) (k >= 3).
+// Hence no k = 1 reconstruction; the k <= -2 and 3 <= k < 23 reconstructions share
+// y' = C - (e2 - x) with C = 1 or 1 - 2^-k, and all three non-trivial ones share the final
+// exponent add.  For k > 56 fdlibm's own reconstruction differs, but there t > 2^56 and tanh
+// rounds to 1 either way.  Identical to glibc's tanhf for all 4,278,190,082 non-NaN floats
+// (exhaustive host comparison of the same operation sequence).
 __device__ __forceinline__ float tanhf_ref(float x) {
+  const float ln2_hi = 6.9313812256e-01f, ln2_lo = 9.0580006145e-06f, invln2 = 1.4426950216e+00f;
+  const float Q1 = -3.3333335072e-02f, Q2 = 1.5873016091e-03f, Q3 = -7.9365076090e-05f, Q4 = 4.0082177293e-06f,
+              Q5 = -2.0109921195e-07f;
   const uint32_t jx = __float_as_uint(x), ix = jx & 0x7fffffffu;
   const float ax = fabsf(x);
   const bool ge1 = ix >= 0x3f800000u;
-  const float t = expm1f_ref(__fmul_rn(ge1 ? 2.0f : -2.0f, ax));
-  const float q = __fdiv_rn(ge1 ? 2.0f : -t, __fadd_rn(t, 2.0f));
+  const float y = __fmul_rn(ge1 ? 2.0f : -2.0f, ax);  // exact
+  const uint32_t hy = __float_as_uint(y) & 0x7fffffffu;
+  const int kgen = static_cast<int>(__fadd_rn(__fmul_rn(invln2, y), ge1 ? 0.5f : -0.5f));
+  const int k = ge1 ? kgen : (hy <= 0x3eb17218u ? 0 : (hy < 0x3F851592u ? -1 : kgen));
+  const float tk = static_cast<float>(k);
+  const float hi = __fsub_rn(y, __fmul_rn(tk, ln2_hi)), lo = __fmul_rn(tk, ln2_lo);
+  const float xr = __fsub_rn(hi, lo);
+  const float c = __fsub_rn(__fsub_rn(hi, xr), lo);
+  const float hfx = __fmul_rn(0.5f, xr);
+  const float hxs = __fmul_rn(xr, hfx);
+  float r1 = __fmul_rn(hxs, Q5);
+  r1 = __fmul_rn(hxs, __fadd_rn(Q4, r1));
+  r1 = __fmul_rn(hxs, __fadd_rn(Q3, r1));
+  r1 = __fmul_rn(hxs, __fadd_rn(Q2, r1));
+  r1 = __fadd_rn(1.0f, __fmul_rn(hxs, __fadd_rn(Q1, r1)));
+  const float t = __fsub_rn(3.0f, __fmul_rn(r1, hfx));
+  const float e = __fmul_rn(hxs, __fdiv_rn(__fsub_rn(r1, t), __fsub_rn(6.0f, __fmul_rn(xr, t))));
+  const float res0 = __fsub_rn(xr, __fsub_rn(__fmul_rn(xr, e), hxs));
+  const float e2 = __fsub_rn(__fsub_rn(__fmul_rn(xr, __fsub_rn(e, c)), c), hxs);
+  const float resm1 = __fsub_rn(__fmul_rn(0.5f, __fsub_rn(xr, e2)), 0.5f);
+  const float two_mk = f_from_bits(static_cast<uint32_t>(0x7f - k) << 23);  // 2^-k, k in [-3, 63]
+  const float cab = k < 0 ? 1.0f : __fsub_rn(1.0f, two_mk);
+  const float yab = __fsub_rn(cab, __fsub_rn(e2, xr));
+  const float yc = __fadd_rn(__fsub_rn(xr, __fadd_rn(e2, two_mk)), 1.0f);
+  const float ysel = k < 23 ? yab : yc;
+  float rr = f_from_bits(__float_as_uint(ysel) + (static_cast<uint32_t>(k) << 23));
+  rr = k < 0 ? __fsub_rn(rr, 1.0f) : rr;
+  float em = k == 0 ? res0 : (k == -1 ? resm1 : rr);
+  em = (!ge1 && hy < 0x33000000u) ? y : em;  // |y| < 2^-25: expm1(y) = y
+  const float q = __fdiv_rn(ge1 ? 2.0f : -em, __fadd_rn(em, 2.0f));
   float z = ge1 ? __fsub_rn(1.0f, q) : q;
   z = ix >= 0x41b00000u ? __fsub_rn(1.0f, 1.0e-30f) : z;
   float r = (jx >> 31) ? -z : z;

@@ -91,8 +91,8 @@ constexpr int cmax(int a, int b) { return a > b ? a : b; }
 constexpr int CV2_SMEM = cmax(CV2_MP * (DIM + CV2_WS) * 8 + CV2_RAW * 4 + 2 * CV2_MP * 4, 4 * CV2_CH * DIM * 8);
 
 constexpr int CV3_CH = 64;
-constexpr int CV3_CC = 8;
-constexpr int CV3_MP = CV3_CC * 9 / 2;     // 36
+constexpr int CV3_CC = 16;
+constexpr int CV3_MP = CV3_CC * 9 / 2;     // 72
 constexpr int CV3_WS = CV3_CH + 2;
 constexpr int CV3_RW = 44;                 // raw row: the 41 values of a channel (+ unused pad)
 constexpr int CV3_RAW = 3 * CV3_CC * CV3_RW;
