@@ -205,3 +205,26 @@ def test_config1_layer_with_biases_per_channel(pkg, orc, gpu_lib, dev):
         check_ids(ids, ids_ref, lo_ref)
     finally:
         eng.close()
+
+
+def test_engine_from_reference_model_dir(pkg, gpu_lib, model40, tmp_path):
+    """The engine loaded from the reference's model directory (.xnet + dictionary, written by
+    xnet.write_model_dir, packed by the restated build_plan) gives the same ids and logits as
+    the engine over the blob the files were written from."""
+    blob, plan = model40
+    pkg.xnet.write_model_dir(str(tmp_path), blob, plan)
+    feats, _ = pkg.fbank(pkg.synth.make_audio(41, 6.0))
+    wins = [feats[:400], feats[400:477]]
+    a = pkg.Engine(blob, plan, max_rows=1024)
+    b = pkg.Engine.from_model_dir(str(tmp_path), max_rows=1024)
+    try:
+        ia, la = a.forward(wins, want_logits=True)
+        ib, lb = b.forward(wins, want_logits=True)
+        for x, y in zip(ia, ib):
+            np.testing.assert_array_equal(x, y)
+        for x, y in zip(la, lb):
+            np.testing.assert_array_equal(x, y)
+        assert len(b.tokens) == plan.vocab
+    finally:
+        a.close()
+        b.close()

@@ -7,6 +7,7 @@ that ABI:
 
   * :mod:`.abi`    -- ctypes bindings and the weight-blob plan struct
   * :mod:`.synth`  -- seeded synthetic models, audio and workload configurations
+  * :mod:`.xnet`   -- the reference's model directory (.xnet + dictionary): parse, load, write
   * :mod:`.host`   -- ``Engine`` (batched engine) and ``Gpu`` / ``WindowModel``, a mirror of
                       the reference's Rust FFI wrapper (src/gpu.rs) and per-window GPU
                       forward (src/model.rs:504-619) driven through the reference ABI
@@ -14,7 +15,7 @@ that ABI:
 
 There is no CPU fallback anywhere on this path: if the library is missing, loading fails.
 """
-from . import abi, dist, synth  # noqa: F401
+from . import abi, dist, synth, xnet  # noqa: F401
 from .host import Engine, Gpu, WindowModel, fbank, ctc_collapse  # noqa: F401
 
-__all__ = ["abi", "dist", "synth", "Engine", "Gpu", "WindowModel", "fbank", "ctc_collapse"]
+__all__ = ["abi", "dist", "synth", "xnet", "Engine", "Gpu", "WindowModel", "fbank", "ctc_collapse"]

@@ -58,6 +58,16 @@ class Engine:
             raise RuntimeError("wasr_model_create failed")
         self.device = device
 
+    @classmethod
+    def from_model_dir(cls, path: str, device: int = 0, max_rows: int = 16384) -> "Engine":
+        """Engine over the reference's model directory (.xnet + dict.decoder.utf8.txt), packed
+        the way build_plan packs it (src/model.rs:209-237); the vocabulary is kept as `tokens`."""
+        from . import xnet
+        blob, plan, tokens = xnet.load_plan(path)
+        eng = cls(blob, plan, device=device, max_rows=max_rows)
+        eng.tokens = tokens
+        return eng
+
     def close(self):
         if self.m:
             self.L.wasr_model_destroy(self.m)
