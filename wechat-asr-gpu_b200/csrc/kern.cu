@@ -348,7 +348,7 @@ __global__ void __launch_bounds__(256) quant_rows_k(const float* __restrict__ x,
 // src/model.rs:693-704 (+ the residual add of :493 / csrc/wtl_kern.cu:170-216 when o != 0).
 // Mean and variance are sequential left folds on the CPU, i.e. chains of 512 dependent
 // rounded adds per row, so a block keeps 128 rows folding at once: the rows stream through
-// shared memory in column chunks (coalesced cp.async, double-buffered), and thread i folds row
+// shared memory in column chunks (coalesced cp.async, three chunks in flight), and thread i folds row
 // i over each chunk in column order -- pass 1 the sum, pass 2 the squared deviations.  Then 16
 // warps normalise, write the residual and quantise one row each at a time, coalesced, with
 // gamma / beta in registers.  The residual h + o is recomputed wherever it is needed (the same
@@ -357,12 +357,13 @@ constexpr int LN_ROWS = 128;
 constexpr int LN_THREADS = 512;
 template <bool RES>
 struct LnCfg {
-  static constexpr int CW = RES ? 64 : 128;  // columns per chunk
+  static constexpr int CW = RES ? 32 : 64;   // columns per chunk
   static constexpr int NCH = D / CW;         // chunks per pass
   static constexpr int RS = CW + 4;          // shared row stride in floats (conflict-free float4 rows)
   static constexpr int NSRC = RES ? 2 : 1;   // h (+ o)
+  static constexpr int NBUF = 4;             // chunks in flight: 3 loading while one is folded
   static constexpr int BUF = NSRC * LN_ROWS * RS;
-  static constexpr int SMEM = 2 * BUF * 4 + 2 * LN_ROWS * 4;
+  static constexpr int SMEM = NBUF * BUF * 4 + 2 * LN_ROWS * 4;
 };
 
 __device__ __forceinline__ float4 add4_rn(float4 a, float4 b) {
@@ -375,37 +376,36 @@ __global__ void __launch_bounds__(LN_THREADS) ln_quant_k(float* __restrict__ h, 
                                                          int m, int8_t* __restrict__ xq, float* __restrict__ xs) {
   using C = LnCfg<RES>;
   extern __shared__ __align__(16) float sm[];
-  float* mean = sm + 2 * C::BUF;
+  float* mean = sm + C::NBUF * C::BUF;
   float* rinv = mean + LN_ROWS;
   const int r0 = blockIdx.x * LN_ROWS;
   const int nr = min(LN_ROWS, m - r0);
   const int tid = threadIdx.x;
-  // chunk k (0 .. 2*NCH-1: both passes) -> buffer k & 1
+  constexpr int NK = 2 * C::NCH;  // chunks of both passes
+  // chunk k (0 .. NK-1) -> buffer k % NBUF; one commit group per chunk (empty past the end)
   auto load = [&](int k) {
-    float* dst = sm + (k & 1) * C::BUF;
-    const int col0 = (k % C::NCH) * C::CW;
-    for (int e = tid; e < nr * (C::CW / 4); e += LN_THREADS) {
-      const int rr = e / (C::CW / 4), c4 = e - rr * (C::CW / 4);
-      const int64_t src = static_cast<int64_t>(r0 + rr) * D + col0 + 4 * c4;
-      cp_async16(dst + rr * C::RS + 4 * c4, h + src);
-      if constexpr (RES) cp_async16(dst + LN_ROWS * C::RS + rr * C::RS + 4 * c4, o + src);
+    if (k < NK) {
+      float* dst = sm + (k % C::NBUF) * C::BUF;
+      const int col0 = (k % C::NCH) * C::CW;
+      for (int e = tid; e < nr * (C::CW / 4); e += LN_THREADS) {
+        const int rr = e / (C::CW / 4), c4 = e - rr * (C::CW / 4);
+        const int64_t src = static_cast<int64_t>(r0 + rr) * D + col0 + 4 * c4;
+        cp_async16(dst + rr * C::RS + 4 * c4, h + src);
+        if constexpr (RES) cp_async16(dst + LN_ROWS * C::RS + rr * C::RS + 4 * c4, o + src);
+      }
     }
     cp_async_commit();
   };
-  load(0);
+  for (int k = 0; k < C::NBUF - 1; k++) load(k);
   float sum = 0.0f, s2 = 0.0f, mu = 0.0f;
 #pragma unroll 1
-  for (int k = 0; k < 2 * C::NCH; k++) {
-    if (k + 1 < 2 * C::NCH) {
-      load(k + 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
+  for (int k = 0; k < NK; k++) {
+    cp_async_wait<C::NBUF - 2>();  // chunk k has landed (the next NBUF-2 may still be loading)
+    __syncthreads();               // ... for every thread; chunk k-1's buffer is free again
+    load(k + C::NBUF - 1);
     if (tid < nr) {
-      const float4* hr = reinterpret_cast<const float4*>(sm + (k & 1) * C::BUF + tid * C::RS);
-      const float4* orow = reinterpret_cast<const float4*>(sm + (k & 1) * C::BUF + LN_ROWS * C::RS + tid * C::RS);
+      const float4* hr = reinterpret_cast<const float4*>(sm + (k % C::NBUF) * C::BUF + tid * C::RS);
+      const float4* orow = reinterpret_cast<const float4*>(sm + (k % C::NBUF) * C::BUF + LN_ROWS * C::RS + tid * C::RS);
       if (k < C::NCH) {
 #pragma unroll 8
         for (int c = 0; c < C::CW / 4; c++) {
@@ -431,8 +431,8 @@ __global__ void __launch_bounds__(LN_THREADS) ln_quant_k(float* __restrict__ h, 
         }
       }
     }
-    __syncthreads();  // buffer k & 1 is reloaded by the next iteration
   }
+  cp_async_wait<0>();
   if (tid < nr) {
     const float var = __fdiv_rn(s2, static_cast<float>(D));
     mean[tid] = mu;
@@ -446,17 +446,36 @@ __global__ void __launch_bounds__(LN_THREADS) ln_quant_k(float* __restrict__ h, 
     gg[k] = __ldg(reinterpret_cast<const float4*>(g) + lane + 32 * k);
     bb[k] = __ldg(reinterpret_cast<const float4*>(b) + lane + 32 * k);
   }
+  // rows rr = warp, warp + 16, ...: the next row's values load while this row is computed
+  float4 nh[4], no[4];
+  auto fetch = [&](int rr) {
+    const float4* hr = reinterpret_cast<const float4*>(h + static_cast<int64_t>(r0 + rr) * D);
+#pragma unroll
+    for (int k = 0; k < 4; k++) nh[k] = hr[lane + 32 * k];
+    if constexpr (RES) {
+      const float4* orow = reinterpret_cast<const float4*>(o + static_cast<int64_t>(r0 + rr) * D);
+#pragma unroll
+      for (int k = 0; k < 4; k++) no[k] = orow[lane + 32 * k];
+    }
+  };
+  if (warp < nr) fetch(warp);
   for (int rr = warp; rr < nr; rr += LN_THREADS / 32) {
     const float mu_r = mean[rr], iv = rinv[rr];
     float4* hr = reinterpret_cast<float4*>(h + static_cast<int64_t>(r0 + rr) * D);
-    const float4* orow = RES ? reinterpret_cast<const float4*>(o + static_cast<int64_t>(r0 + rr) * D) : nullptr;
+    float4 ch[4], co[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      ch[k] = nh[k];
+      co[k] = no[k];
+    }
+    if (rr + LN_THREADS / 32 < nr) fetch(rr + LN_THREADS / 32);
     float4 y[4];
     float mx = 0.0f;
 #pragma unroll
     for (int k = 0; k < 4; k++) {
-      float4 v = hr[lane + 32 * k];
+      float4 v = ch[k];
       if constexpr (RES) {
-        v = add4_rn(v, orow[lane + 32 * k]);
+        v = add4_rn(v, co[k]);
         hr[lane + 32 * k] = v;
       }
       y[k].x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.x, mu_r), iv), gg[k].x), bb[k].x);
