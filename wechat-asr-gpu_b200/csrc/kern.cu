@@ -561,7 +561,7 @@ __global__ void __launch_bounds__(256) gelu_quant_k(float* __restrict__ x, int m
 // GELU + per-row quant of a read-only [m][k] input (the FF1 GEMM output): the GELU values are
 // only needed to quantise, so they are staged in shared memory (one warp per row, 8 rows per
 // block) and never written back.  Same results as gelu in place followed by quant.
-constexpr int GQ_ROWS = 8;
+constexpr int GQ_ROWS = 4;
 
 __global__ void __launch_bounds__(256) gelu_quant_ro_k(const float* __restrict__ y, int m, int k,
                                                        int8_t* __restrict__ xq, float* __restrict__ xs) {
