@@ -71,6 +71,7 @@ struct WasrModel {
   bool qkv_fused[WASR_MAX_LAYERS] = {};
   // activations
   float *feats = nullptr, *y1 = nullptr, *y2 = nullptr, *y3 = nullptr;
+  float *c2pre = nullptr, *c3pre = nullptr;  // conv2 / conv3 weights laid out per conv stage
   int8_t* xq = nullptr;
   float* xs = nullptr;
   float *h = nullptr, *qkv = nullptr, *att = nullptr, *f = nullptr;
@@ -207,8 +208,8 @@ int enqueue_chunk(WasrModel* m, const Chunk& c, const int* seg, float* logits, L
   const WasrPlan& P = m->plan;
   // conv frontend -> y3 -> int8 -> linear (src/model.rs:389-478,489)
   TRY(K(WASR_K_CONV1, [&] { return launch_conv1(m->feats, fptr(m, P.c1), s, c.frames, m->y1, st); }));
-  TRY(K(WASR_K_CONV2, [&] { return launch_conv2(m->y1, fptr(m, P.c2), s, M, m->y2, st); }));
-  TRY(K(WASR_K_CONV3, [&] { return launch_conv3(m->y2, fptr(m, P.c3), s, M, m->y3, st); }));
+  TRY(K(WASR_K_CONV2, [&] { return launch_conv2(m->y1, fptr(m, P.c2), m->c2pre, s, M, m->y2, st); }));
+  TRY(K(WASR_K_CONV3, [&] { return launch_conv3(m->y2, fptr(m, P.c3), m->c3pre, s, M, m->y3, st); }));
   TRY(K(WASR_K_QUANT, [&] { return launch_quant_rows(m->y3, M, FLAT, FLAT, m->xq, m->xs, st); }));
   TRY(K(WASR_K_GEMM_LIN, [&] { return gemm_run(gemm_args(m, m->xq, m->xs, M, FLAT, P.lin, D, P.lin_b, EPI_F32, m->h, D), st); }));
   for (int l = 0; l < P.n_layers; l++) {
@@ -526,6 +527,10 @@ WasrModel* wasr_model_create(const void* blob, size_t bytes, const WasrPlan* pla
            cudaMemcpy(m->qkv_bias[l], bs.data(), 3 * D * sizeof(float), cudaMemcpyHostToDevice) == cudaSuccess;
     m->qkv_fused[l] = ok;
   }
+  // conv2 / conv3 weights in the per-stage layout their kernels stage from (once per model)
+  ok = ok && dmalloc(&m->c2pre, conv_pre_floats(2)) && dmalloc(&m->c3pre, conv_pre_floats(3)) &&
+       conv_prepare(fptr(m, plan->c2), fptr(m, plan->c3), m->c2pre, m->c3pre, m->stream) == 0 &&
+       cudaStreamSynchronize(m->stream) == cudaSuccess;
   if (!ok) {
     wasr_model_destroy(m);
     return nullptr;
@@ -540,7 +545,7 @@ void wasr_model_destroy(WasrModel* m) {
   free_graphs(m);
   free_recs(&m->eager_recs);
   void* dptrs[] = {m->w, m->feats, m->y1, m->y2, m->y3, m->xq, m->xs, m->h, m->qkv, m->att, m->f, m->rowmax,
-                   m->keys, m->ids, m->seg};
+                   m->keys, m->ids, m->seg, m->c2pre, m->c3pre};
   for (void* p : dptrs)
     if (p) cudaFree(p);
   for (int l = 0; l < WASR_MAX_LAYERS; l++) {

@@ -140,7 +140,8 @@ __device__ __forceinline__ float tp_fold(const float2* part, int nch, int npos, 
 // outside the segment / the 40 columns), column 40 = 0 -- src/model.rs:420-444.
 // Block = (row r, 32 output channels); stages of 4 input channels.
 __global__ void __launch_bounds__(TP_THREADS, 3) conv2_k(const float* __restrict__ y1, const float* __restrict__ c2,
-                                                      Segs s, int row0, float* __restrict__ y2) {
+                                                      const float2* __restrict__ c2pre, Segs s, int row0,
+                                                      float* __restrict__ y2) {
   extern __shared__ __align__(16) float sm[];
   float2* X2 = reinterpret_cast<float2*>(sm);    // [98][40]
   float2* Wt = X2 + CV2_MP * DIM;                 // [98][34]
@@ -173,15 +174,23 @@ __global__ void __launch_bounds__(TP_THREADS, 3) conv2_k(const float* __restrict
 #pragma unroll 1
   for (int c0 = 0; c0 < C1; c0 += CV2_CC) {
     __syncthreads();  // the previous stage is consumed (and the zeros / offsets are visible)
-    for (int e = tid; e < CV2_MP * CV2_CH; e += TP_THREADS) {
-      const int o = e / CV2_MP, m = e - o * CV2_MP;
-      const float* w = c2 + static_cast<int64_t>(og * CV2_CH + o) * K2 + c0 * 49 + 2 * m;
-      float2* d = Wt + m * CV2_WS + o;
-      if (w8) {
-        cp_async8(d, w);
-      } else {
-        cp_async4(d, w);
-        cp_async4(reinterpret_cast<float*>(d) + 1, w + 1);
+    if (c2pre) {  // the stage's [pair][64 channels] rows, laid out once per model: 16-byte copies
+      const float2* src = c2pre + static_cast<int64_t>(c0 / CV2_CC) * CV2_MP * C2 + og * CV2_CH;
+      for (int e = tid; e < CV2_MP * (CV2_CH / 2); e += TP_THREADS) {
+        const int m = e >> 4, c2x = (e & 15) * 2;
+        cp_async16(Wt + m * CV2_WS + c2x, src + m * C2 + c2x);
+      }
+    } else {
+      for (int e = tid; e < CV2_MP * CV2_CH; e += TP_THREADS) {
+        const int o = e / CV2_MP, m = e - o * CV2_MP;
+        const float* w = c2 + static_cast<int64_t>(og * CV2_CH + o) * K2 + c0 * 49 + 2 * m;
+        float2* d = Wt + m * CV2_WS + o;
+        if (w8) {
+          cp_async8(d, w);
+        } else {
+          cp_async4(d, w);
+          cp_async4(reinterpret_cast<float*>(d) + 1, w + 1);
+        }
       }
     }
     for (int e = tid; e < 7 * CV2_CC * (DIM / 4); e += TP_THREADS) {
@@ -201,9 +210,14 @@ __global__ void __launch_bounds__(TP_THREADS, 3) conv2_k(const float* __restrict
     cp_async_commit();
     cp_async_wait<0>();
     __syncthreads();
-    for (int e = tid; e < CV2_MP * DIM; e += TP_THREADS) {
-      const int m = e / DIM, f = e - m * DIM;
-      X2[e] = make_float2(raw[tapoff[2 * m] + f], raw[tapoff[2 * m + 1] + f]);
+    {  // warp per tap pair, lane per position (the offsets are warp-uniform)
+      const int warp = tid >> 5, lane = tid & 31;
+      for (int m = warp; m < CV2_MP; m += TP_THREADS / 32) {
+        const float* a = raw + tapoff[2 * m];
+        const float* b = raw + tapoff[2 * m + 1];
+        X2[m * DIM + lane] = make_float2(a[lane], b[lane]);
+        if (lane < DIM - 32) X2[m * DIM + 32 + lane] = make_float2(a[32 + lane], b[32 + lane]);
+      }
     }
     __syncthreads();
     tp_accumulate<DIM, CV2_WS, 2>(X2, Wt, CV2_MP, (q - (c0 >> 1)) & 3, f0, o0, acc);
@@ -227,7 +241,8 @@ __global__ void __launch_bounds__(TP_THREADS, 3) conv2_k(const float* __restrict
 // outside the segment) -- src/model.rs:446-468.  Block = (row r, 64 output channels);
 // stages of 8 input channels.
 __global__ void __launch_bounds__(TP_THREADS, 3) conv3_k(const float* __restrict__ y2, const float* __restrict__ c3,
-                                                      Segs s, int row0, float* __restrict__ y3) {
+                                                      const float2* __restrict__ c3pre, Segs s, int row0,
+                                                      float* __restrict__ y3) {
   extern __shared__ __align__(16) float sm[];
   float2* X2 = reinterpret_cast<float2*>(sm);    // [36][20]
   float2* Wt = X2 + CV3_MP * 20;                  // [36][66]
@@ -257,15 +272,23 @@ __global__ void __launch_bounds__(TP_THREADS, 3) conv3_k(const float* __restrict
 #pragma unroll 1
   for (int c0 = 0; c0 < C2; c0 += CV3_CC) {
     __syncthreads();
-    for (int e = tid; e < CV3_MP * CV3_CH; e += TP_THREADS) {
-      const int o = e / CV3_MP, m = e - o * CV3_MP;
-      const float* w = c3 + static_cast<int64_t>(og * CV3_CH + o) * K3 + c0 * 9 + 2 * m;
-      float2* d = Wt + m * CV3_WS + o;
-      if (w8) {
-        cp_async8(d, w);
-      } else {
-        cp_async4(d, w);
-        cp_async4(reinterpret_cast<float*>(d) + 1, w + 1);
+    if (c3pre) {  // the stage's [pair][192 channels] rows, laid out once per model
+      const float2* src = c3pre + static_cast<int64_t>(c0 / CV3_CC) * CV3_MP * C3 + og * CV3_CH;
+      for (int e = tid; e < CV3_MP * (CV3_CH / 2); e += TP_THREADS) {
+        const int m = e >> 5, c2x = (e & 31) * 2;
+        cp_async16(Wt + m * CV3_WS + c2x, src + m * C3 + c2x);
+      }
+    } else {
+      for (int e = tid; e < CV3_MP * CV3_CH; e += TP_THREADS) {
+        const int o = e / CV3_MP, m = e - o * CV3_MP;
+        const float* w = c3 + static_cast<int64_t>(og * CV3_CH + o) * K3 + c0 * 9 + 2 * m;
+        float2* d = Wt + m * CV3_WS + o;
+        if (w8) {
+          cp_async8(d, w);
+        } else {
+          cp_async4(d, w);
+          cp_async4(reinterpret_cast<float*>(d) + 1, w + 1);
+        }
       }
     }
     for (int e = tid; e < 3 * CV3_CC * W2; e += TP_THREADS) {
@@ -277,9 +300,10 @@ __global__ void __launch_bounds__(TP_THREADS, 3) conv3_k(const float* __restrict
     cp_async_commit();
     cp_async_wait<0>();
     __syncthreads();
-    for (int e = tid; e < CV3_MP * 20; e += TP_THREADS) {
-      const int m = e / 20, f = e - m * 20;
-      X2[e] = make_float2(raw[tapoff[2 * m] + 2 * f], raw[tapoff[2 * m + 1] + 2 * f]);
+    {  // warp per tap pair, lane per position
+      const int warp = tid >> 5, lane = tid & 31;
+      for (int m = warp; m < CV3_MP; m += TP_THREADS / 32)
+        if (lane < 20) X2[m * 20 + lane] = make_float2(raw[tapoff[2 * m] + 2 * lane], raw[tapoff[2 * m + 1] + 2 * lane]);
     }
     __syncthreads();
     tp_accumulate<20, CV3_WS, 1>(X2, Wt, CV3_MP, (q - (c0 >> 1)) & 3, f0, o0, acc);
@@ -949,18 +973,43 @@ int launch_conv1(const float* x, const float* c1, Segs s, int total_frames, floa
   conv1_k<<<(n + 127) / 128, 128, 0, st>>>(x, c1, s, total_frames, y1);
   return launched();
 }
-int launch_conv2(const float* y1, const float* c2, Segs s, int total_rows, float* y2, cudaStream_t st) {
+// out[s][m][o] = (c[o][s*taps + 2m], c[o][s*taps + 2m + 1]) for stage s, tap pair m < taps/2,
+// output channel o: the weight pairs of one conv stage, rows of all output channels.
+__global__ void conv_pre_k(const float* __restrict__ c, int nout, int k, int taps, int nstage,
+                           float2* __restrict__ out) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int mp = taps / 2;
+  if (i >= static_cast<int64_t>(nstage) * mp * nout) return;
+  const int o = static_cast<int>(i % nout), m = static_cast<int>((i / nout) % mp), st = static_cast<int>(i / (nout * mp));
+  const float* w = c + static_cast<int64_t>(o) * k + st * taps + 2 * m;
+  out[i] = make_float2(w[0], w[1]);
+}
+
+size_t conv_pre_floats(int which) { return which == 2 ? static_cast<size_t>(C2) * K2 : static_cast<size_t>(C3) * K3; }
+
+int conv_prepare(const float* c2, const float* c3, float* c2pre, float* c3pre, cudaStream_t st) {
+  const int n2 = (C1 / CV2_CC) * CV2_MP * C2, n3 = (C2 / CV3_CC) * CV3_MP * C3;
+  conv_pre_k<<<(n2 + 255) / 256, 256, 0, st>>>(c2, C2, K2, CV2_CC * 49, C1 / CV2_CC, reinterpret_cast<float2*>(c2pre));
+  conv_pre_k<<<(n3 + 255) / 256, 256, 0, st>>>(c3, C3, K3, CV3_CC * 9, C2 / CV3_CC, reinterpret_cast<float2*>(c3pre));
+  return launched();
+}
+
+int launch_conv2(const float* y1, const float* c2, const float* c2pre, Segs s, int total_rows, float* y2,
+                 cudaStream_t st) {
   if (total_rows <= 0) return 0;
   set_smem(reinterpret_cast<const void*>(conv2_k), CV2_SMEM);
   for (int r0 = 0; r0 < total_rows; r0 += 65535)  // grid.y limit
-    conv2_k<<<dim3(C2 / CV2_CH, std::min(65535, total_rows - r0)), TP_THREADS, CV2_SMEM, st>>>(y1, c2, s, r0, y2);
+    conv2_k<<<dim3(C2 / CV2_CH, std::min(65535, total_rows - r0)), TP_THREADS, CV2_SMEM, st>>>(
+        y1, c2, reinterpret_cast<const float2*>(c2pre), s, r0, y2);
   return launched();
 }
-int launch_conv3(const float* y2, const float* c3, Segs s, int total_rows, float* y3, cudaStream_t st) {
+int launch_conv3(const float* y2, const float* c3, const float* c3pre, Segs s, int total_rows, float* y3,
+                 cudaStream_t st) {
   if (total_rows <= 0) return 0;
   set_smem(reinterpret_cast<const void*>(conv3_k), CV3_SMEM);
   for (int r0 = 0; r0 < total_rows; r0 += 65535)  // grid.y limit
-    conv3_k<<<dim3(C3 / CV3_CH, std::min(65535, total_rows - r0)), TP_THREADS, CV3_SMEM, st>>>(y2, c3, s, r0, y3);
+    conv3_k<<<dim3(C3 / CV3_CH, std::min(65535, total_rows - r0)), TP_THREADS, CV3_SMEM, st>>>(
+        y2, c3, reinterpret_cast<const float2*>(c3pre), s, r0, y3);
   return launched();
 }
 int launch_quant_rows(const float* x, int m, int k, int ldx, int8_t* xq, float* xs, cudaStream_t st) {
@@ -1049,8 +1098,8 @@ void wk_front(void* stream, const float* x, const float* c1, const float* c2, co
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const Segs s = one_seg(t, t1);
   launch_conv1(x, c1, s, t, y1, st);
-  launch_conv2(y1, c2, s, t1, y2, st);
-  launch_conv3(y2, c3, s, t1, y3, st);
+  launch_conv2(y1, c2, nullptr, s, t1, y2, st);
+  launch_conv3(y2, c3, nullptr, s, t1, y3, st);
 }
 
 // the 512-wide kernel moves rows as float4 / char4

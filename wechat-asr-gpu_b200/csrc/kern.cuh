@@ -44,8 +44,15 @@ struct Segs {
 
 // host launchers (stream-ordered, no allocation); return 0 or -4 on launch failure
 int launch_conv1(const float* x, const float* c1, Segs s, int total_frames, float* y1, cudaStream_t st);
-int launch_conv2(const float* y1, const float* c2, Segs s, int total_rows, float* y2, cudaStream_t st);
-int launch_conv3(const float* y2, const float* c3, Segs s, int total_rows, float* y3, cudaStream_t st);
+// c2pre / c3pre: optional copies of the weights laid out per conv stage by conv_prepare (one
+// contiguous block of weight pairs per stage); nullptr stages them from the [out][tap] layout.
+int launch_conv2(const float* y1, const float* c2, const float* c2pre, Segs s, int total_rows, float* y2,
+                 cudaStream_t st);
+int launch_conv3(const float* y2, const float* c3, const float* c3pre, Segs s, int total_rows, float* y3,
+                 cudaStream_t st);
+// floats of the stage layout of conv2 (which = 2) or conv3 (which = 3) weights
+size_t conv_pre_floats(int which);
+int conv_prepare(const float* c2, const float* c3, float* c2pre, float* c3pre, cudaStream_t st);
 int launch_quant_rows(const float* x, int m, int k, int ldx, int8_t* xq, float* xs, cudaStream_t st);
 int launch_quant_rows_max(const float* x, int m, int k, const unsigned* rowmax, int8_t* xq, float* xs,
                           cudaStream_t st);
