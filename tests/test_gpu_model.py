@@ -228,3 +228,25 @@ def test_engine_from_reference_model_dir(pkg, gpu_lib, model40, tmp_path):
     finally:
         a.close()
         b.close()
+
+
+@pytest.mark.parametrize("cfg", [2, 3])
+def test_config_utterances_full_model_vs_oracle(pkg, orc, gpu_lib, model40, cfg):
+    """BASELINE configs 2 and 3 end to end at full depth: the 40-layer model, block size 1600,
+    through wasr_transcribe (stream schedule, stacked windows, graphs) against the oracle's
+    transcription of the same features -- per-frame ids and CTC output identical.  Config 2 is
+    the 58.65 s utterance; config 3 takes 8 of its 64 utterances (2-60 s) to bound the oracle's
+    CPU time."""
+    blob, plan = model40
+    lens = pkg.synth.config_lengths(cfg)
+    idx = range(len(lens)) if cfg == 2 else range(0, 64, 8)
+    fs = [pkg.fbank(pkg.synth.make_audio(2000 * cfg + i, lens[i])) for i in idx]
+    eng = pkg.Engine(blob, plan, max_rows=8192)
+    try:
+        got = eng.transcribe([f for f, _ in fs], [s for _, s in fs], blk=1600)
+    finally:
+        eng.close()
+    for (f, s), g in zip(fs, got):
+        ref, _ = orc.transcribe(blob, plan, f, s, blk=1600)
+        np.testing.assert_array_equal(g, ref)
+        np.testing.assert_array_equal(pkg.ctc_collapse(g), orc.ctc(ref))
