@@ -249,16 +249,18 @@ def cpu_baseline(orc, pkg, lengths, budget_s: float):
     blob, plan = pkg.synth.make_model(seed=1, n_layers=40)
     cores = os.cpu_count() or 1
     orc.set_threads(cores)
-    done_s, n, spent = 0.0, 0, 0.0
+    done_s, n, spent, ids = 0.0, 0, 0.0, []
     while spent < budget_s and n < len(lengths):
         pcm = pkg.synth.make_audio(100000 + n, lengths[n])
         f, s = orc.fbank(pcm)
         ts = time.perf_counter()
-        orc.transcribe(blob, plan, f, s, blk=1600)
+        ref, _ = orc.transcribe(blob, plan, f, s, blk=1600)
         spent += time.perf_counter() - ts
+        ids.append(ref)
         done_s += pcm.size / 16000.0
         n += 1
-    return done_s / spent, f"first {n} config-4 utterances ({done_s:.1f} s of audio), {spent:.1f} s CPU wall", cores
+    return (done_s / spent, f"first {n} config-4 utterances ({done_s:.1f} s of audio), {spent:.1f} s CPU wall", cores,
+            ids)
 
 
 def run_reference(args, rank):
@@ -400,7 +402,7 @@ def main():
     value = total_audio / (ms_per_step / 1e3)
 
     # ---- e2e through the public call with host buffers (pinned), copies inside the timing
-    e2e = None
+    e2e, e2e_ids = None, None
     if not args.no_e2e:
         pinned = torch.from_numpy(cat).pin_memory()
         cat_pinned = pinned.numpy()
@@ -418,6 +420,7 @@ def main():
         if dist_on:
             dist.all_reduce(e_t, op=dist.ReduceOp.MAX)
         ids_bytes = 4 * sum(len(o) for o in out)
+        e2e_ids = out if world == 1 else None  # rank 0 of one rank holds every utterance, in order
         e2e = {"value": round(total_audio / float(e_t.item()), 3), "unit": "audio-s/s",
                "h2d_bytes_per_step": int(cat.nbytes), "d2h_bytes_per_step": int(ids_bytes),
                "api": "wasr_transcribe (pinned host features in, host ids out)"}
@@ -470,8 +473,13 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         orc = load_oracle()
-        v, sample, cores = cpu_baseline(orc, pkg, lengths, args.cpu_budget)
+        v, sample, cores, ref_ids = cpu_baseline(orc, pkg, lengths, args.cpu_budget)
         cpu = {"value": round(v, 3), "unit": "audio-s/s", "cores": cores, "kind": "port", "sample": sample}
+        if e2e_ids is not None:
+            # the oracle's per-frame ids of the sample against the GPU's from the e2e run
+            same = [np.array_equal(np.asarray(g, np.uint32), np.asarray(r, np.uint32))
+                    for g, r in zip(e2e_ids, ref_ids)]
+            cpu["parity"] = {"utterances": len(same), "ids_identical": int(sum(same))}
 
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": "audio-s/s", "n_gpus": world,
