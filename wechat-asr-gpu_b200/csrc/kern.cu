@@ -722,6 +722,61 @@ __device__ __forceinline__ void att_copy_rows(float* dst, int ds, const float* _
   cp_async_commit();
 }
 
+// Scores of one 32-key chunk for query rows (2r, 2r+1) of this thread and its keys kt + 8u,
+// u < NU (the groups past the end of a segment are skipped whole): all 8 dotf lanes of a score
+// as 4 float2, folded in lane order, times 0.125, stored as a row pair at out[j].
+template <int NU>
+__device__ __forceinline__ void att_score_chunk(const float* qa, const float* qb, const float* K, int kt, int nj,
+                                                float2* out) {
+  float2 acc[2][NU][4];
+#pragma unroll
+  for (int r = 0; r < 2; r++)
+#pragma unroll
+    for (int u = 0; u < NU; u++)
+#pragma unroll
+      for (int l = 0; l < 4; l++) acc[r][u][l] = make_float2(0.0f, 0.0f);
+#pragma unroll
+  for (int c = 0; c < 8; c++) {
+    const float4 a0 = *reinterpret_cast<const float4*>(qa + 8 * c);
+    const float4 a1 = *reinterpret_cast<const float4*>(qa + 8 * c + 4);
+    const float4 b0 = *reinterpret_cast<const float4*>(qb + 8 * c);
+    const float4 b1 = *reinterpret_cast<const float4*>(qb + 8 * c + 4);
+#pragma unroll
+    for (int u = 0; u < NU; u++) {
+      const float* kr = K + (kt + 8 * u) * ATT_RS + 8 * c;
+      const float4 k0 = *reinterpret_cast<const float4*>(kr);
+      const float4 k1 = *reinterpret_cast<const float4*>(kr + 4);
+      acc[0][u][0] = add2_rn(acc[0][u][0], mulp(lo2(a0), lo2(k0)));
+      acc[0][u][1] = add2_rn(acc[0][u][1], mulp(hi2(a0), hi2(k0)));
+      acc[0][u][2] = add2_rn(acc[0][u][2], mulp(lo2(a1), lo2(k1)));
+      acc[0][u][3] = add2_rn(acc[0][u][3], mulp(hi2(a1), hi2(k1)));
+      acc[1][u][0] = add2_rn(acc[1][u][0], mulp(lo2(b0), lo2(k0)));
+      acc[1][u][1] = add2_rn(acc[1][u][1], mulp(hi2(b0), hi2(k0)));
+      acc[1][u][2] = add2_rn(acc[1][u][2], mulp(lo2(b1), lo2(k1)));
+      acc[1][u][3] = add2_rn(acc[1][u][3], mulp(hi2(b1), hi2(k1)));
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < NU; u++) {
+    const int j = kt + 8 * u;
+    if (j < nj) {
+      float sc[2];
+#pragma unroll
+      for (int r = 0; r < 2; r++) {
+        float x = __fadd_rn(acc[r][u][0].x, acc[r][u][0].y);
+        x = __fadd_rn(x, acc[r][u][1].x);
+        x = __fadd_rn(x, acc[r][u][1].y);
+        x = __fadd_rn(x, acc[r][u][2].x);
+        x = __fadd_rn(x, acc[r][u][2].y);
+        x = __fadd_rn(x, acc[r][u][3].x);
+        x = __fadd_rn(x, acc[r][u][3].y);
+        sc[r] = __fmul_rn(x, 0.125f);
+      }
+      out[j] = make_float2(sc[0], sc[1]);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, const float* __restrict__ k,
                                                  const float* __restrict__ v, int ld, Segs s,
                                                  const int* __restrict__ toff, const int* __restrict__ tord,
@@ -773,52 +828,15 @@ __global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, co
                       min(ATT_KC, t - j0 - ATT_KC), h, tid, a16);
       const float* K = Kb + (ch & 1) * ATT_KC * ATT_RS;
       if (live) {
-        float2 acc[2][4][4];
-#pragma unroll
-        for (int r = 0; r < 2; r++)
-#pragma unroll
-          for (int u = 0; u < 4; u++)
-#pragma unroll
-            for (int l = 0; l < 4; l++) acc[r][u][l] = make_float2(0.0f, 0.0f);
-#pragma unroll
-        for (int c = 0; c < 8; c++) {
-          const float4 a0 = *reinterpret_cast<const float4*>(qa + 8 * c);
-          const float4 a1 = *reinterpret_cast<const float4*>(qa + 8 * c + 4);
-          const float4 b0 = *reinterpret_cast<const float4*>(qb + 8 * c);
-          const float4 b1 = *reinterpret_cast<const float4*>(qb + 8 * c + 4);
-#pragma unroll
-          for (int u = 0; u < 4; u++) {
-            const float* kr = K + (kt + 8 * u) * ATT_RS + 8 * c;
-            const float4 k0 = *reinterpret_cast<const float4*>(kr);
-            const float4 k1 = *reinterpret_cast<const float4*>(kr + 4);
-            acc[0][u][0] = add2_rn(acc[0][u][0], mulp(lo2(a0), lo2(k0)));
-            acc[0][u][1] = add2_rn(acc[0][u][1], mulp(hi2(a0), hi2(k0)));
-            acc[0][u][2] = add2_rn(acc[0][u][2], mulp(lo2(a1), lo2(k1)));
-            acc[0][u][3] = add2_rn(acc[0][u][3], mulp(hi2(a1), hi2(k1)));
-            acc[1][u][0] = add2_rn(acc[1][u][0], mulp(lo2(b0), lo2(k0)));
-            acc[1][u][1] = add2_rn(acc[1][u][1], mulp(hi2(b0), hi2(k0)));
-            acc[1][u][2] = add2_rn(acc[1][u][2], mulp(lo2(b1), lo2(k1)));
-            acc[1][u][3] = add2_rn(acc[1][u][3], mulp(hi2(b1), hi2(k1)));
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-          const int j = kt + 8 * u;
-          if (j < nj) {
-            float sc[2];
-#pragma unroll
-            for (int r = 0; r < 2; r++) {
-              float x = __fadd_rn(acc[r][u][0].x, acc[r][u][0].y);
-              x = __fadd_rn(x, acc[r][u][1].x);
-              x = __fadd_rn(x, acc[r][u][1].y);
-              x = __fadd_rn(x, acc[r][u][2].x);
-              x = __fadd_rn(x, acc[r][u][2].y);
-              x = __fadd_rn(x, acc[r][u][3].x);
-              x = __fadd_rn(x, acc[r][u][3].y);
-              sc[r] = __fmul_rn(x, 0.125f);
-            }
-            S2[rt * sp + j0 + j] = make_float2(sc[0], sc[1]);
-          }
+        // 8-key groups of this warp (keys kt + 8u) that hold keys of the segment: all four but
+        // in a segment's last chunk
+        const int nu = min(4, max(0, (nj - 4 * (warp >> 2) + 7) / 8));
+        switch (nu) {
+          case 4: att_score_chunk<4>(qa, qb, K, kt, nj, S2 + rt * sp + j0); break;
+          case 3: att_score_chunk<3>(qa, qb, K, kt, nj, S2 + rt * sp + j0); break;
+          case 2: att_score_chunk<2>(qa, qb, K, kt, nj, S2 + rt * sp + j0); break;
+          case 1: att_score_chunk<1>(qa, qb, K, kt, nj, S2 + rt * sp + j0); break;
+          default: break;
         }
       }
     }
