@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(TP_THREADS, 3) conv2_k(const float* __restrict
       }
     }
     __syncthreads();
-    tp_accumulate<DIM, CV2_WS, 2>(X2, Wt, CV2_MP, (q - (c0 >> 1)) & 3, f0, o0, acc);
+    tp_accumulate<DIM, CV2_WS, 4>(X2, Wt, CV2_MP, (q - (c0 >> 1)) & 3, f0, o0, acc);
   }
   __syncthreads();
   float2* part = reinterpret_cast<float2*>(sm);  // [4][32][40]
@@ -306,7 +306,7 @@ __global__ void __launch_bounds__(TP_THREADS, 3) conv3_k(const float* __restrict
         if (lane < 20) X2[m * 20 + lane] = make_float2(raw[tapoff[2 * m] + 2 * lane], raw[tapoff[2 * m + 1] + 2 * lane]);
     }
     __syncthreads();
-    tp_accumulate<20, CV3_WS, 1>(X2, Wt, CV3_MP, (q - (c0 >> 1)) & 3, f0, o0, acc);
+    tp_accumulate<20, CV3_WS, 4>(X2, Wt, CV3_MP, (q - (c0 >> 1)) & 3, f0, o0, acc);
   }
   __syncthreads();
   float2* part = reinterpret_cast<float2*>(sm);  // [4][64][20]
