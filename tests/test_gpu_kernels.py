@@ -144,7 +144,7 @@ def _math_inputs():
     return np.concatenate([x, dense, np.array([0x4202422f, 0xc27c65d9], np.uint32).view(np.float32)])
 
 
-@pytest.mark.parametrize("fn,name", [(0, "tanhf"), (1, "expf"), (2, "gelu")])
+@pytest.mark.parametrize("fn,name", [(0, "tanhf"), (1, "expf"), (2, "gelu"), (4, "tanhf"), (5, "gelu")])
 def test_device_libm_restatements_bit_exact(gpu_lib, dev, orc, fn, name):
     """The GELU and softmax kernels evaluate glibc's tanhf / expf algorithms (the functions the
     reference's Rust f32::tanh / f32::exp call): bit-identical to this host's glibc."""

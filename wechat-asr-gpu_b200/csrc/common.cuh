@@ -377,14 +377,94 @@ __device__ __forceinline__ float gelu_ref(float x) {
   float u = __fmul_rn(0.7978846f, __fadd_rn(x, c));
   return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf_ref(u)));
 }
+// ---- the same tanhf / GELU for two independent elements: every multiply is one packed
+// multiply of the pair (mul.rn.f32x2), every add, subtract and divide stays a scalar rounded
+// operation per element (so no multiply can be contracted into an add), and the integer /
+// select logic runs per element.  Identical results to tanhf_ref / gelu_ref element by element.
+__device__ __forceinline__ float2 pmul2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"((static_cast<unsigned long long>(__float_as_uint(a.y)) << 32) |
+                                                 __float_as_uint(a.x)),
+      "l"((static_cast<unsigned long long>(__float_as_uint(b.y)) << 32) | __float_as_uint(b.x)));
+  return make_float2(__uint_as_float(static_cast<uint32_t>(r)), __uint_as_float(static_cast<uint32_t>(r >> 32)));
+}
+__device__ __forceinline__ float2 f2c(float v) { return make_float2(v, v); }
+__device__ __forceinline__ float2 sadd2(float2 a, float2 b) { return make_float2(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y)); }
+__device__ __forceinline__ float2 ssub2(float2 a, float2 b) { return make_float2(__fsub_rn(a.x, b.x), __fsub_rn(a.y, b.y)); }
+__device__ __forceinline__ float2 sdiv2(float2 a, float2 b) { return make_float2(__fdiv_rn(a.x, b.x), __fdiv_rn(a.y, b.y)); }
+
+// per-element part of tanhf_ref after the shared reductions: reconstruction, tanh, specials
+__device__ __forceinline__ float tanh_tail(float x, int k, bool ge1, uint32_t hy, float y, float xr, float e2, float res0,
+                                           float resm1) {
+  const uint32_t jx = __float_as_uint(x), ix = jx & 0x7fffffffu;
+  const float two_mk = f_from_bits(static_cast<uint32_t>(0x7f - k) << 23);
+  const float cab = k < 0 ? 1.0f : __fsub_rn(1.0f, two_mk);
+  const float yab = __fsub_rn(cab, __fsub_rn(e2, xr));
+  const float yc = __fadd_rn(__fsub_rn(xr, __fadd_rn(e2, two_mk)), 1.0f);
+  const float ysel = k < 23 ? yab : yc;
+  float rr = f_from_bits(__float_as_uint(ysel) + (static_cast<uint32_t>(k) << 23));
+  rr = k < 0 ? __fsub_rn(rr, 1.0f) : rr;
+  float em = k == 0 ? res0 : (k == -1 ? resm1 : rr);
+  em = (!ge1 && hy < 0x33000000u) ? y : em;
+  const float q = __fdiv_rn(ge1 ? 2.0f : -em, __fadd_rn(em, 2.0f));
+  float z = ge1 ? __fsub_rn(1.0f, q) : q;
+  z = ix >= 0x41b00000u ? __fsub_rn(1.0f, 1.0e-30f) : z;
+  float r = (jx >> 31) ? -z : z;
+  r = ix < 0x24000000u ? __fmul_rn(x, __fadd_rn(1.0f, x)) : r;
+  r = ix == 0 ? x : r;
+  if (ix >= 0x7f800000u)
+    r = (jx >> 31) ? __fsub_rn(__fdiv_rn(1.0f, x), 1.0f) : __fadd_rn(__fdiv_rn(1.0f, x), 1.0f);
+  return r;
+}
+
+__device__ __forceinline__ float2 tanhf_ref2(float2 x) {
+  const float ln2_hi = 6.9313812256e-01f, ln2_lo = 9.0580006145e-06f, invln2 = 1.4426950216e+00f;
+  const float Q1 = -3.3333335072e-02f, Q2 = 1.5873016091e-03f, Q3 = -7.9365076090e-05f, Q4 = 4.0082177293e-06f,
+              Q5 = -2.0109921195e-07f;
+  const uint32_t ia = __float_as_uint(x.x) & 0x7fffffffu, ib = __float_as_uint(x.y) & 0x7fffffffu;
+  const bool ga = ia >= 0x3f800000u, gb = ib >= 0x3f800000u;
+  const float2 y = pmul2(make_float2(ga ? 2.0f : -2.0f, gb ? 2.0f : -2.0f), make_float2(fabsf(x.x), fabsf(x.y)));
+  const uint32_t hya = __float_as_uint(y.x) & 0x7fffffffu, hyb = __float_as_uint(y.y) & 0x7fffffffu;
+  const float2 iy = pmul2(f2c(invln2), y);
+  const int kga = static_cast<int>(__fadd_rn(iy.x, ga ? 0.5f : -0.5f));
+  const int kgb = static_cast<int>(__fadd_rn(iy.y, gb ? 0.5f : -0.5f));
+  const int ka = ga ? kga : (hya <= 0x3eb17218u ? 0 : (hya < 0x3F851592u ? -1 : kga));
+  const int kb = gb ? kgb : (hyb <= 0x3eb17218u ? 0 : (hyb < 0x3F851592u ? -1 : kgb));
+  const float2 tk = make_float2(static_cast<float>(ka), static_cast<float>(kb));
+  const float2 hi = ssub2(y, pmul2(tk, f2c(ln2_hi))), lo = pmul2(tk, f2c(ln2_lo));
+  const float2 xr = ssub2(hi, lo);
+  const float2 c = ssub2(ssub2(hi, xr), lo);
+  const float2 hfx = pmul2(f2c(0.5f), xr);
+  const float2 hxs = pmul2(xr, hfx);
+  float2 r1 = pmul2(hxs, f2c(Q5));
+  r1 = pmul2(hxs, sadd2(f2c(Q4), r1));
+  r1 = pmul2(hxs, sadd2(f2c(Q3), r1));
+  r1 = pmul2(hxs, sadd2(f2c(Q2), r1));
+  r1 = sadd2(f2c(1.0f), pmul2(hxs, sadd2(f2c(Q1), r1)));
+  const float2 t = ssub2(f2c(3.0f), pmul2(r1, hfx));
+  const float2 e = pmul2(hxs, sdiv2(ssub2(r1, t), ssub2(f2c(6.0f), pmul2(xr, t))));
+  const float2 res0 = ssub2(xr, ssub2(pmul2(xr, e), hxs));
+  const float2 e2 = ssub2(ssub2(pmul2(xr, ssub2(e, c)), c), hxs);
+  const float2 resm1 = ssub2(pmul2(f2c(0.5f), ssub2(xr, e2)), f2c(0.5f));
+  return make_float2(tanh_tail(x.x, ka, ga, hya, y.x, xr.x, e2.x, res0.x, resm1.x),
+                     tanh_tail(x.y, kb, gb, hyb, y.y, xr.y, e2.y, res0.y, resm1.y));
+}
+
+__device__ __forceinline__ float2 gelu_ref2(float2 x) {
+  const float2 c = pmul2(pmul2(pmul2(f2c(0.044715f), x), x), x);
+  const float2 u = pmul2(f2c(0.7978846f), sadd2(x, c));
+  return pmul2(pmul2(f2c(0.5f), x), sadd2(f2c(1.0f), tanhf_ref2(u)));
+}
+
 // Epilogue of src/kernels.rs:53: (acc as f32 * xs[i]) * ws + bias (bias 0.0 when absent).
 __device__ __forceinline__ float dequant(int32_t acc, float xs, float ws, float bias) {
   return __fadd_rn(__fmul_rn(__fmul_rn(static_cast<float>(acc), xs), ws), bias);
 }
 
-// Packed FP32x2 multiply / add with round-to-nearest per component (Blackwell), written as
-// PTX so that no compiler stage can contract a multiply feeding an add into a fused
-// multiply-add: each component is rounded exactly like __fmul_rn / __fadd_rn.
+// Packed FP32x2 multiply / add with round-to-nearest per component (Blackwell).  Each is exact
+// on its own, but a packed multiply feeding a packed add is contracted into a packed fused
+// multiply-add by the code generator (measured: results equal fmaf's), so exact sequences pair
+// a packed multiply with scalar __fadd_rn adds, or scalar __fmul_rn products with a packed add.
 __device__ __forceinline__ unsigned long long f2_bits(float2 a) {
   return (static_cast<unsigned long long>(__float_as_uint(a.y)) << 32) | __float_as_uint(a.x);
 }

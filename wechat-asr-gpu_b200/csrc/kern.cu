@@ -602,7 +602,8 @@ __global__ void __launch_bounds__(256) gelu_quant_ro_k(const float* __restrict__
 #pragma unroll 1
     for (int j = lane * 4; j < k; j += 128) {
       const float4 v = __ldg(reinterpret_cast<const float4*>(r + j));
-      const float4 gv = make_float4(gelu_ref(v.x), gelu_ref(v.y), gelu_ref(v.z), gelu_ref(v.w));
+      const float2 ga = gelu_ref2(make_float2(v.x, v.y)), gb = gelu_ref2(make_float2(v.z, v.w));
+      const float4 gv = make_float4(ga.x, ga.y, gb.x, gb.y);
       *reinterpret_cast<float4*>(g + j) = gv;
       mx = fmaxf(mx, fmaxf(fmaxf(fabsf(gv.x), fabsf(gv.y)), fmaxf(fabsf(gv.z), fabsf(gv.w))));
     }
@@ -957,6 +958,13 @@ __global__ void eval_math_k(int fn, const float* __restrict__ x, float* __restri
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const float v = x[i];
+  if (fn >= 4) {  // the packed-pair forms: element i rides in its pair's x or y slot
+    const int i0 = i & ~1, i1 = i0 + 1 < n ? i0 + 1 : i0;
+    const float2 p = make_float2(x[i0], x[i1]);
+    const float2 r = fn == 4 ? tanhf_ref2(p) : gelu_ref2(p);
+    y[i] = (i & 1) ? r.y : r.x;
+    return;
+  }
   y[i] = fn == 0 ? tanhf_ref(v) : fn == 1 ? expf_ref(v) : fn == 2 ? gelu_ref(v) : expm1f_ref(v);
 }
 
@@ -1226,9 +1234,10 @@ int wk_attention_cublas_part(int part, void* stream, const float* q, const float
 }
 
 // Parity hook: evaluate the device restatements of the libm functions the reference calls
-// (fn 0 tanhf, 1 expf, 2 the GELU of src/model.rs:710-712, 3 expm1f) over n floats.
+// (fn 0 tanhf, 1 expf, 2 the GELU of src/model.rs:710-712, 3 expm1f; 4 tanhf and 5 the GELU
+// in their packed two-element forms) over n floats.
 int wasr_eval_math(int fn, const float* x, float* y, int n, void* stream) {
-  if (!x || !y || fn < 0 || fn > 3) return -1;
+  if (!x || !y || fn < 0 || fn > 5) return -1;
   if (n <= 0) return 0;
   eval_math_k<<<(n + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(fn, x, y, n);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
