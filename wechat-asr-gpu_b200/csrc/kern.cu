@@ -684,22 +684,27 @@ __global__ void keys_to_ids_k(const unsigned long long* __restrict__ keys, int m
 // p_j * v_j[d] from 0 (src/model.rs:714-738).  Every element keeps the reference's exact
 // sequence of rounded multiplies and adds.
 //
-// Register tiles.  Scores: a thread owns query rows (2r, 2r+1) x keys (kt + 8u, u < 4) of a
-// 32-key chunk and keeps all 8 dotf lanes of each score as 4 float2 (lanes 2l, 2l+1 take
-// dims 8c+2l, 8c+2l+1), so a product pair is q[d..d+1] * k[d..d+1].  PV: a thread owns row
+// Register tiles.  Scores: a thread pair (hl = 0, 1) owns 4 query rows x 4 keys (kg + 8u,
+// u < 4) of a 32-key chunk; thread hl keeps dotf lanes 4hl .. 4hl+3 of each score as 2 float2
+// (dims 8c+4hl .. 8c+4hl+3), so each 16-byte load of q or k feeds 4 scores (2 bytes of shared
+// memory per exact MAC).  The lane fold keeps the reference order: hl = 0 folds lanes 0-3,
+// hands the partial sum to its partner by one shuffle, and hl = 1 adds lanes 4-7.  PV: a thread owns row
 // pairs (2p, 2p+1) for p = r, r+16 x head dims d0..d0+3; the accumulators pair (row 2p, dim d)
 // with (row 2p+1, dim d^1).  K and V chunks stream through two shared buffers by cp.async,
-// one barrier per chunk.  Shared layout: exp table | Q [64][68] + K [2][32][68] (scores) /
-// V [2][32][64] (PV) | S2 [32 row pairs][sp] float2 | Z [64].
+// one barrier per chunk.  Shared layout: exp table | Q [64][72] + K [2][32][72] (scores) /
+// V [2][32][64] (PV) | S2 [32 row pairs][sp] float2 | Z [64] | Mx [64].
+// Softmax: the row maxima come out of the score loop (each thread's running maximum, reduced
+// over the 8 thread pairs of a warp that share a row); the exp and divide passes run flat over
+// (row pair, key) with every thread on independent elements; z is one thread per row.
 constexpr int ATT_KC = 32;   // keys per chunk
-constexpr int ATT_RS = 68;   // Q / K row stride in floats (16-byte rows, conflict-free tiles)
+constexpr int ATT_RS = 72;   // Q / K row stride in floats: 16-byte rows, 8 keys of a quarter-warp on distinct banks
 constexpr int ATT_A = (ATT_QT + 2 * ATT_KC) * ATT_RS;  // floats of the Q/K (and V) region
 
 __host__ __device__ inline int att_pair_stride(int max_t1) { return ((max_t1 + 15) / 16) * 16 + 1; }
 
 size_t attention_smem_bytes(int max_t1) {
   const int sp = att_pair_stride(max_t1);
-  return 32 * 8 + static_cast<size_t>(ATT_A) * 4 + static_cast<size_t>(ATT_QT / 2) * sp * 8 + ATT_QT * 4;
+  return 32 * 8 + static_cast<size_t>(ATT_A) * 4 + static_cast<size_t>(ATT_QT / 2) * sp * 8 + 2 * ATT_QT * 4;
 }
 
 __device__ __forceinline__ float2 lo2(float4 a) { return make_float2(a.x, a.y); }
@@ -723,57 +728,51 @@ __device__ __forceinline__ void att_copy_rows(float* dst, int ds, const float* _
   cp_async_commit();
 }
 
-// Scores of one 32-key chunk for query rows (2r, 2r+1) of this thread and its keys kt + 8u,
-// u < NU (the groups past the end of a segment are skipped whole): all 8 dotf lanes of a score
-// as 4 float2, folded in lane order, times 0.125, stored as a row pair at out[j].
+// Scores of one 32-key chunk for the 4 query rows at Qr (row stride ATT_RS, already offset
+// by this thread's lanes 4hl) and keys kg + 8u, u < NU (groups past the end of a segment are
+// skipped whole), K likewise offset.  hl = 1 lanes store score pairs of rows (0, 1) and (2, 3)
+// at out0[j] / out1[j] and keep the running row maxima in mx (order-free).
 template <int NU>
-__device__ __forceinline__ void att_score_chunk(const float* qa, const float* qb, const float* K, int kt, int nj,
-                                                float2* out) {
-  float2 acc[2][NU][4];
+__device__ __forceinline__ void att_score_chunk(const float* Qr, const float* Kr, int kg, int hl, int nj,
+                                                float2* out0, float2* out1, float (&mx)[4]) {
+  float2 acc[4][NU][2];
 #pragma unroll
-  for (int r = 0; r < 2; r++)
+  for (int m = 0; m < 4; m++)
 #pragma unroll
-    for (int u = 0; u < NU; u++)
-#pragma unroll
-      for (int l = 0; l < 4; l++) acc[r][u][l] = make_float2(0.0f, 0.0f);
+    for (int u = 0; u < NU; u++) acc[m][u][0] = acc[m][u][1] = make_float2(0.0f, 0.0f);
 #pragma unroll
   for (int c = 0; c < 8; c++) {
-    const float4 a0 = *reinterpret_cast<const float4*>(qa + 8 * c);
-    const float4 a1 = *reinterpret_cast<const float4*>(qa + 8 * c + 4);
-    const float4 b0 = *reinterpret_cast<const float4*>(qb + 8 * c);
-    const float4 b1 = *reinterpret_cast<const float4*>(qb + 8 * c + 4);
+    float4 qv[4];
+#pragma unroll
+    for (int m = 0; m < 4; m++) qv[m] = *reinterpret_cast<const float4*>(Qr + m * ATT_RS + 8 * c);
 #pragma unroll
     for (int u = 0; u < NU; u++) {
-      const float* kr = K + (kt + 8 * u) * ATT_RS + 8 * c;
-      const float4 k0 = *reinterpret_cast<const float4*>(kr);
-      const float4 k1 = *reinterpret_cast<const float4*>(kr + 4);
-      acc[0][u][0] = add2_rn(acc[0][u][0], mulp(lo2(a0), lo2(k0)));
-      acc[0][u][1] = add2_rn(acc[0][u][1], mulp(hi2(a0), hi2(k0)));
-      acc[0][u][2] = add2_rn(acc[0][u][2], mulp(lo2(a1), lo2(k1)));
-      acc[0][u][3] = add2_rn(acc[0][u][3], mulp(hi2(a1), hi2(k1)));
-      acc[1][u][0] = add2_rn(acc[1][u][0], mulp(lo2(b0), lo2(k0)));
-      acc[1][u][1] = add2_rn(acc[1][u][1], mulp(hi2(b0), hi2(k0)));
-      acc[1][u][2] = add2_rn(acc[1][u][2], mulp(lo2(b1), lo2(k1)));
-      acc[1][u][3] = add2_rn(acc[1][u][3], mulp(hi2(b1), hi2(k1)));
+      const float4 kv = *reinterpret_cast<const float4*>(Kr + 8 * u * ATT_RS + 8 * c);
+#pragma unroll
+      for (int m = 0; m < 4; m++) {
+        acc[m][u][0] = add2_rn(acc[m][u][0], mulp(lo2(qv[m]), lo2(kv)));
+        acc[m][u][1] = add2_rn(acc[m][u][1], mulp(hi2(qv[m]), hi2(kv)));
+      }
     }
   }
 #pragma unroll
   for (int u = 0; u < NU; u++) {
-    const int j = kt + 8 * u;
-    if (j < nj) {
-      float sc[2];
+    float sc[4];
 #pragma unroll
-      for (int r = 0; r < 2; r++) {
-        float x = __fadd_rn(acc[r][u][0].x, acc[r][u][0].y);
-        x = __fadd_rn(x, acc[r][u][1].x);
-        x = __fadd_rn(x, acc[r][u][1].y);
-        x = __fadd_rn(x, acc[r][u][2].x);
-        x = __fadd_rn(x, acc[r][u][2].y);
-        x = __fadd_rn(x, acc[r][u][3].x);
-        x = __fadd_rn(x, acc[r][u][3].y);
-        sc[r] = __fmul_rn(x, 0.125f);
-      }
-      out[j] = make_float2(sc[0], sc[1]);
+    for (int m = 0; m < 4; m++) {
+      // hl = 0: ((l0 + l1) + l2) + l3, passed to hl = 1, which adds l4, l5, l6, l7 in turn
+      const float pl = __fadd_rn(__fadd_rn(__fadd_rn(acc[m][u][0].x, acc[m][u][0].y), acc[m][u][1].x), acc[m][u][1].y);
+      const float lo = __shfl_xor_sync(0xffffffffu, pl, 1);
+      const float x =
+          __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(lo, acc[m][u][0].x), acc[m][u][0].y), acc[m][u][1].x), acc[m][u][1].y);
+      sc[m] = __fmul_rn(x, 0.125f);
+    }
+    const int j = kg + 8 * u;
+    if (hl && j < nj) {
+      out0[j] = make_float2(sc[0], sc[1]);
+      out1[j] = make_float2(sc[2], sc[3]);
+#pragma unroll
+      for (int m = 0; m < 4; m++) mx[m] = fmaxf(mx[m], sc[m]);
     }
   }
 }
@@ -785,11 +784,12 @@ __global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, co
   extern __shared__ __align__(16) float sm[];
   const int sp = att_pair_stride(max_t1);
   unsigned long long* tab = reinterpret_cast<unsigned long long*>(sm);
-  float* Q = sm + 64;                     // [64][68]
-  float* Kb = Q + ATT_QT * ATT_RS;        // [2][32][68]
+  float* Q = sm + 64;                     // [64][72]
+  float* Kb = Q + ATT_QT * ATT_RS;        // [2][32][72]
   float* Vb = Q;                          // [2][32][64] (PV phase)
   float2* S2 = reinterpret_cast<float2*>(Q + ATT_A);  // [32][sp]
   float* Z = reinterpret_cast<float*>(S2 + (ATT_QT / 2) * sp);
+  float* Mx = Z + ATT_QT;                 // [64]: row maxima
   const int tile = tord ? tord[blockIdx.x] : blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
   int sw = 0;
   if (toff) {
@@ -816,10 +816,13 @@ __global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, co
   att_copy_rows(Q, ATT_RS, q, ld, rb + i0, ni, h, tid, a16);
   att_copy_rows(Kb, ATT_RS, k, ld, rb, min(ATT_KC, t), h, tid, a16);
   {
-    const int rt = 8 * (warp & 3) + (lane & 7), kt = 4 * (warp >> 2) + (lane >> 3);
-    const bool live = 16 * (warp & 3) < ni;  // warp-uniform
-    const float* qa = Q + (2 * rt) * ATT_RS;
-    const float* qb = qa + ATT_RS;
+    // warp w: rows 8w .. 8w+7; lane = hl + 2 kg + 16 rg: rows 8w + 4rg + m (m < 4), keys kg + 8u
+    const int hl = lane & 1, kg = (lane >> 1) & 7, rg = lane >> 4, row0 = 8 * warp + 4 * rg;
+    const bool live = 8 * warp < ni;  // warp-uniform
+    const float* Qr = Q + row0 * ATT_RS + 4 * hl;
+    float2* out0 = S2 + (row0 >> 1) * sp;
+    float2* out1 = out0 + sp;
+    float mx[4] = {-3.40282347e+38f, -3.40282347e+38f, -3.40282347e+38f, -3.40282347e+38f};
     for (int ch = 0; ch < nchunks; ch++) {
       const int j0 = ch * ATT_KC, nj = min(ATT_KC, t - j0);
       cp_async_wait<0>();
@@ -827,48 +830,56 @@ __global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, co
       if (ch + 1 < nchunks)
         att_copy_rows(Kb + ((ch + 1) & 1) * ATT_KC * ATT_RS, ATT_RS, k, ld, rb + j0 + ATT_KC,
                       min(ATT_KC, t - j0 - ATT_KC), h, tid, a16);
-      const float* K = Kb + (ch & 1) * ATT_KC * ATT_RS;
+      const float* Kr = Kb + (ch & 1) * ATT_KC * ATT_RS + kg * ATT_RS + 4 * hl;
       if (live) {
-        // 8-key groups of this warp (keys kt + 8u) that hold keys of the segment: all four but
-        // in a segment's last chunk
-        const int nu = min(4, max(0, (nj - 4 * (warp >> 2) + 7) / 8));
-        switch (nu) {
-          case 4: att_score_chunk<4>(qa, qb, K, kt, nj, S2 + rt * sp + j0); break;
-          case 3: att_score_chunk<3>(qa, qb, K, kt, nj, S2 + rt * sp + j0); break;
-          case 2: att_score_chunk<2>(qa, qb, K, kt, nj, S2 + rt * sp + j0); break;
-          case 1: att_score_chunk<1>(qa, qb, K, kt, nj, S2 + rt * sp + j0); break;
-          default: break;
+        // 8-key groups holding keys of the segment: all four but in a segment's last chunk
+        switch (min(4, (nj + 7) >> 3)) {
+          case 4: att_score_chunk<4>(Qr, Kr, kg, hl, nj, out0 + j0, out1 + j0, mx); break;
+          case 3: att_score_chunk<3>(Qr, Kr, kg, hl, nj, out0 + j0, out1 + j0, mx); break;
+          case 2: att_score_chunk<2>(Qr, Kr, kg, hl, nj, out0 + j0, out1 + j0, mx); break;
+          default: att_score_chunk<1>(Qr, Kr, kg, hl, nj, out0 + j0, out1 + j0, mx); break;
+        }
+      }
+    }
+    // the 8 hl = 1 lanes of a row group hold the same rows (lane bits 1-3 differ)
+#pragma unroll
+    for (int m = 0; m < 4; m++) {
+      mx[m] = fmaxf(mx[m], __shfl_xor_sync(0xffffffffu, mx[m], 2));
+      mx[m] = fmaxf(mx[m], __shfl_xor_sync(0xffffffffu, mx[m], 4));
+      mx[m] = fmaxf(mx[m], __shfl_xor_sync(0xffffffffu, mx[m], 8));
+    }
+    if (live && (lane & 15) == 1)
+#pragma unroll
+      for (int m = 0; m < 4; m++) Mx[row0 + m] = mx[m];
+  }
+  __syncthreads();  // scores and row maxima complete; the Q/K region is free
+  // the first V chunk streams in while the softmax runs
+  att_copy_rows(Vb, HD, v, ld, rb, min(ATT_KC, t), h, tid, a16);
+  // ---- softmax.  e = exp(s - max) over (row pair p, key j): threads tid & 63 take keys
+  // j = tid & 63 + 64u, tid >> 6 the row pairs p = 4w + tid >> 6 (4 keys x 2 rows in flight)
+  const int npair = (ni + 1) >> 1, jl = tid & 63;
+  for (int p = tid >> 6; p < npair; p += 4) {
+    const bool two = 2 * p + 1 < ni;  // the second row of the last pair may be past the tile
+    const float ma = Mx[2 * p], mb = Mx[2 * p + 1];
+    float2* row = S2 + p * sp;
+    for (int jb = 0; jb < t; jb += 256) {
+      float2 a[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++)
+        if (jb + jl + 64 * u < t) a[u] = row[jb + jl + 64 * u];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int j = jb + jl + 64 * u;
+        if (j < t) {
+          a[u].x = expf_ref_smem(__fsub_rn(a[u].x, ma), tab);
+          if (two) a[u].y = expf_ref_smem(__fsub_rn(a[u].y, mb), tab);
+          row[j] = a[u];
         }
       }
     }
   }
-  __syncthreads();  // scores complete; the Q/K region is free
-  // the first V chunk streams in while the softmax runs
-  att_copy_rows(Vb, HD, v, ld, rb, min(ATT_KC, t), h, tid, a16);
-  // ---- softmax: row max (order-free, warp per row), exp (element-wise), sequential row sum
-  float* Sf = reinterpret_cast<float*>(S2);
-  // (element loops run 4 independent elements per lane: the exp is a long dependent chain)
-  for (int i = warp; i < ni; i += 8) {
-    float* row = Sf + (i >> 1) * sp * 2 + (i & 1);
-    float m4[4] = {-3.40282347e+38f, -3.40282347e+38f, -3.40282347e+38f, -3.40282347e+38f};
-    int j = lane;
-    for (; j + 96 < t; j += 128) {
-#pragma unroll
-      for (int u = 0; u < 4; u++) m4[u] = fmaxf(m4[u], row[2 * (j + 32 * u)]);
-    }
-    for (; j < t; j += 32) m4[0] = fmaxf(m4[0], row[2 * j]);
-    const float m = warp_max(fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
-    j = lane;
-    for (; j + 96 < t; j += 128) {
-      float a[4];
-#pragma unroll
-      for (int u = 0; u < 4; u++) a[u] = row[2 * (j + 32 * u)];
-#pragma unroll
-      for (int u = 0; u < 4; u++) row[2 * (j + 32 * u)] = expf_ref_smem(__fsub_rn(a[u], m), tab);
-    }
-    for (; j < t; j += 32) row[2 * j] = expf_ref_smem(__fsub_rn(row[2 * j], m), tab);
-  }
   __syncthreads();
+  float* Sf = reinterpret_cast<float*>(S2);
   if (tid < ni) {  // z: a left fold over j, loads issued 8 at a time ahead of the adds
     const float* row = Sf + (tid >> 1) * sp * 2 + (tid & 1);
     float z = 0.0f;
@@ -884,18 +895,25 @@ __global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, co
     Z[tid] = z;
   }
   __syncthreads();
-  for (int i = warp; i < ni; i += 8) {  // p_j = e_j / z, warp per row
-    float* row = Sf + (i >> 1) * sp * 2 + (i & 1);
-    const float z = Z[i];
-    int j = lane;
-    for (; j + 96 < t; j += 128) {
-      float a[4];
+  for (int p = tid >> 6; p < npair; p += 4) {  // p = e / z, same mapping as the exp pass
+    const bool two = 2 * p + 1 < ni;
+    const float za = Z[2 * p], zb = two ? Z[2 * p + 1] : 1.0f;
+    float2* row = S2 + p * sp;
+    for (int jb = 0; jb < t; jb += 256) {
+      float2 a[4];
 #pragma unroll
-      for (int u = 0; u < 4; u++) a[u] = row[2 * (j + 32 * u)];
+      for (int u = 0; u < 4; u++)
+        if (jb + jl + 64 * u < t) a[u] = row[jb + jl + 64 * u];
 #pragma unroll
-      for (int u = 0; u < 4; u++) row[2 * (j + 32 * u)] = __fdiv_rn(a[u], z);
+      for (int u = 0; u < 4; u++) {
+        const int j = jb + jl + 64 * u;
+        if (j < t) {
+          a[u].x = __fdiv_rn(a[u].x, za);
+          if (two) a[u].y = __fdiv_rn(a[u].y, zb);
+          row[j] = a[u];
+        }
+      }
     }
-    for (; j < t; j += 32) row[2 * j] = __fdiv_rn(row[2 * j], z);
   }
   // ---- PV
   const int pr = 8 * (warp & 1) + (lane & 7), dt = 4 * (warp >> 1) + (lane >> 3);
