@@ -156,8 +156,9 @@ int64_t wasr_ctc_collapse(const uint32_t* ids, int64_t n, uint32_t* out);
 
 /* Parity hook: evaluates the kernels' restatements of the libm functions the reference CPU
  * path calls (fn 0: tanhf, 1: expf, 2: GELU of src/model.rs:710-712, 3: expm1f; 4: tanhf and
- * 5: GELU in the packed two-element form the GELU kernel runs) on n device floats, so tests
- * can compare them bit for bit with the host's glibc. */
+ * 5: GELU in the packed two-element form the GELU kernel runs; 6: the attention softmax's
+ * division, y[2i] = x[2i] / x[2i+1] for numerators in [0, 1] and row sums in [1, 2^24)) on n
+ * device floats, so tests can compare them bit for bit with the host's glibc / IEEE division. */
 int wasr_eval_math(int fn, const float* x, float* y, int n, void* stream);
 
 const char* wasr_version(void);

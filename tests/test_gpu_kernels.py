@@ -158,3 +158,25 @@ def test_device_libm_restatements_bit_exact(gpu_lib, dev, orc, fn, name):
     ref = {"tanhf": orc.libm_tanhf, "expf": orc.libm_expf, "gelu": orc.gelu}[name](x)
     bad = np.flatnonzero(got.view(np.uint32) != ref.view(np.uint32))
     assert bad.size == 0, (bad.size, x[bad[:5]], got[bad[:5]], ref[bad[:5]])
+
+
+def test_softmax_division_exact(gpu_lib, dev):
+    """The attention softmax divides each exp by its row sum through a reciprocal and Markstein's
+    correction (numerators in [0, 1], row sums in [1, 2^24)); the quotient must be the correctly
+    rounded IEEE quotient, which is what the reference's f32 division gives."""
+    L = gpu_lib
+    rng = np.random.default_rng(11)
+    a = np.arange(0, 0x3F800001, 97, dtype=np.uint32).view(np.float32)          # every 97th float in [0, 1]
+    a = np.concatenate([a, np.float32([0.0, 1.0, 2.0 ** -80, 2.0 ** -81, 1e-30, 1e-45, 0.5])])
+    specials = np.float32([1.0, np.nextafter(np.float32(1), np.float32(2)), np.nextafter(np.float32(2), np.float32(1)),
+                           2.0, 3.0, 7.0, 255.0, 256.0, 8191.5, 3.0 * 2 ** 20, 16777215.0])
+    b = np.where(rng.random(a.size) < 0.5, rng.uniform(1.0, 8192.0, a.size).astype(np.float32),
+                 specials[rng.integers(0, specials.size, a.size)]).astype(np.float32)
+    x = np.empty(2 * a.size, np.float32)
+    x[0::2], x[1::2] = a, b
+    px, py = dev.put(x), dev.empty(x.nbytes)
+    assert L.wasr_eval_math(6, px, py, x.size, None) == 0
+    got = dev.get(py, x.shape, np.float32)[0::2]
+    ref = (a / b).astype(np.float32)
+    bad = np.flatnonzero(got.view(np.uint32) != ref.view(np.uint32))
+    assert bad.size == 0, (bad.size, a[bad[:5]], b[bad[:5]], got[bad[:5]], ref[bad[:5]])

@@ -331,18 +331,11 @@ __constant__ static const unsigned long long kExp2Tab[32] = {
 // tab[i] above = bits(2^(i/32)) - (i << 47): adding k << 47 to tab[k % 32] yields 2^(k/32).
 // `lookup(i)` returns tab[i]: from constant memory (expf_ref) or from a shared-memory copy
 // (expf_ref_smem; indexed constant loads serialise when the lanes of a warp differ).
+// Branch-free: the main path runs for every input and the special ranges are selected after
+// it, so several calls in a row can overlap (the double-precision chain is ~230 cycles long).
 template <typename Lookup>
 __device__ __forceinline__ float expf_body(float x, Lookup lookup) {
   const uint32_t ux = __float_as_uint(x);
-  if (ux == 0x4202422fu) return f_from_bits(0x56fc9f1cu);  // the two inputs where glibc's result
-  if (ux == 0xc27c65d9u) return f_from_bits(0x11fa2993u);  // is the other float neighbour
-  const uint32_t abstop = (ux >> 20) & 0x7ffu;
-  if (abstop >= (0x42b00000u >> 20)) {  // |x| >= 88 or non-finite
-    if (ux == 0xff800000u) return 0.0f;
-    if (abstop >= (0x7f800000u >> 20)) return __fadd_rn(x, x);
-    if (x > 88.72283172607421875f) return __int_as_float(0x7f800000);
-    if (x < -103.97207641601562f) return 0.0f;
-  }
   const double inv_ln2_n = 0x1.71547652b82fep+0 * 32.0;
   const double shift = 0x1.8p+52;
   const double c0 = 0x1.c6af84b912394p-5 / 32768.0;  // cubic coefficients of 2^(r/32), r in [-1/2, 1/2]
@@ -360,7 +353,18 @@ __device__ __forceinline__ float expf_body(float x, Lookup lookup) {
   double y = __dadd_rn(__dmul_rn(c2, r), 1.0);
   y = __dadd_rn(__dmul_rn(zz, r2), y);
   y = __dmul_rn(y, s);
-  return __double2float_rn(y);
+  float res = __double2float_rn(y);
+  const uint32_t abstop = (ux >> 20) & 0x7ffu;
+  if (abstop >= (0x42b00000u >> 20)) {  // |x| >= 88 or non-finite (the main path result is
+    // kept for x in [88, 88.72] and [-103.97, -88], as in the reference algorithm)
+    res = x < -103.97207641601562f ? 0.0f : res;
+    res = x > 88.72283172607421875f ? __int_as_float(0x7f800000) : res;
+    res = abstop >= (0x7f800000u >> 20) ? __fadd_rn(x, x) : res;
+    res = ux == 0xff800000u ? 0.0f : res;
+  }
+  res = ux == 0x4202422fu ? f_from_bits(0x56fc9f1cu) : res;  // the two inputs where glibc's result
+  res = ux == 0xc27c65d9u ? f_from_bits(0x11fa2993u) : res;  // is the other float neighbour
+  return res;
 }
 __device__ __forceinline__ float expf_ref(float x) {
   return expf_body(x, [](int i) { return kExp2Tab[i]; });
@@ -454,6 +458,23 @@ __device__ __forceinline__ float2 gelu_ref2(float2 x) {
   const float2 c = pmul2(pmul2(pmul2(f2c(0.044715f), x), x), x);
   const float2 u = pmul2(f2c(0.7978846f), sadd2(x, c));
   return pmul2(pmul2(f2c(0.5f), x), sadd2(f2c(1.0f), tanhf_ref2(u)));
+}
+
+// a / b rounded to nearest for a in [0, 1] and b in [1, 2^24) (a softmax numerator and row
+// sum), given yb = __frcp_rn(b): Markstein's correction (P. Markstein, IBM J. Res. Dev. 34(1),
+// 1990, "Computation of elementary functions on the IBM RISC System/6000 processor"): with yb
+// the correctly rounded reciprocal and q within an ulp of a/b, r = a - b*q is exact (one fma)
+// and RN(q + r*yb) is the correctly rounded quotient.  Numerators below 2^-80 (where q or r
+// could underflow) need the full division: div_unit_fast leaves them to the caller
+// (div_unit_tiny), which tests for them once per warp so the common case has no division.
+__device__ __forceinline__ float div_unit_fast(float a, float b, float yb) {
+  const float q = __fmul_rn(a, yb);
+  const float r = __fmaf_rn(-q, b, a);
+  return __fmaf_rn(r, yb, q);
+}
+__device__ __forceinline__ bool div_unit_tiny(float a) { return a < 0x1p-80f; }
+__device__ __forceinline__ float div_unit_rn(float a, float b, float yb) {
+  return div_unit_tiny(a) ? __fdiv_rn(a, b) : div_unit_fast(a, b, yb);
 }
 
 // Epilogue of src/kernels.rs:53: (acc as f32 * xs[i]) * ws + bias (bias 0.0 when absent).

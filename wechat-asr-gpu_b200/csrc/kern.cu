@@ -692,7 +692,7 @@ __global__ void keys_to_ids_k(const unsigned long long* __restrict__ keys, int m
 // pairs (2p, 2p+1) for p = r, r+16 x head dims d0..d0+3; the accumulators pair (row 2p, dim d)
 // with (row 2p+1, dim d^1).  K and V chunks stream through two shared buffers by cp.async,
 // one barrier per chunk.  Shared layout: exp table | Q [64][72] + K [2][32][72] (scores) /
-// V [2][32][64] (PV) | S2 [32 row pairs][sp] float2 | Z [64] | Mx [64].
+// V [2][32][64] (PV) | S2 [32 row pairs][sp] float2 | ZY [32][4] | Mx [64].
 // Softmax: the row maxima come out of the score loop (each thread's running maximum, reduced
 // over the 8 thread pairs of a warp that share a row); the exp and divide passes run flat over
 // (row pair, key) with every thread on independent elements; z is one thread per row.
@@ -704,7 +704,7 @@ __host__ __device__ inline int att_pair_stride(int max_t1) { return ((max_t1 + 1
 
 size_t attention_smem_bytes(int max_t1) {
   const int sp = att_pair_stride(max_t1);
-  return 32 * 8 + static_cast<size_t>(ATT_A) * 4 + static_cast<size_t>(ATT_QT / 2) * sp * 8 + 2 * ATT_QT * 4;
+  return 32 * 8 + static_cast<size_t>(ATT_A) * 4 + static_cast<size_t>(ATT_QT / 2) * sp * 8 + 3 * ATT_QT * 4;
 }
 
 __device__ __forceinline__ float2 lo2(float4 a) { return make_float2(a.x, a.y); }
@@ -777,6 +777,80 @@ __device__ __forceinline__ void att_score_chunk(const float* Qr, const float* Kr
   }
 }
 
+// Softmax passes over the flat element list e = p * t + j of a tile's row pairs p (float2
+// per key j): element e of batch slot k is e0 + 256k.  Loads are clamped to the last element
+// and every exp / quotient is computed unconditionally, so the NB pairs of a batch overlap;
+// only the stores are guarded.  (e + 0.5) / t in float recovers p exactly for p < 32 and
+// t < 2^16: its error is below 32 * 2^-23 = 2^-18 while its distance to an integer is at least
+// 1 / (2t) > 2^-17.
+__device__ __forceinline__ int att_pair(int e, float inv_t) {
+  return static_cast<int>(__fmul_rn(__fadd_rn(static_cast<float>(e), 0.5f), inv_t));
+}
+template <int NB>
+__device__ __forceinline__ void att_exp_batch(float2* S2, const float2* M2, const unsigned long long* tab, int sp, int t,
+                                              float inv_t, int E, int e0) {
+  float2 a[NB], m[NB];
+  int off[NB];
+#pragma unroll
+  for (int k = 0; k < NB; k++) {
+    const int e = min(e0 + 256 * k, E - 1), p = att_pair(e, inv_t);
+    off[k] = p * sp + (e - p * t);
+    m[k] = M2[p];
+    a[k] = S2[off[k]];
+  }
+#pragma unroll
+  for (int k = 0; k < NB; k++)
+    a[k] = make_float2(expf_ref_smem(__fsub_rn(a[k].x, m[k].x), tab), expf_ref_smem(__fsub_rn(a[k].y, m[k].y), tab));
+#pragma unroll
+  for (int k = 0; k < NB; k++)
+    if (e0 + 256 * k < E) S2[off[k]] = a[k];
+}
+// p = e / z with zy[p] = (z_2p, z_2p+1, rcp z_2p, rcp z_2p+1)
+template <int NB>
+__device__ __forceinline__ void att_div_batch(float2* S2, const float4* ZY, int sp, int t, float inv_t, int E, int e0) {
+  float2 a[NB], q[NB];
+  float4 zy[NB];
+  int off[NB];
+  bool tiny = false;
+#pragma unroll
+  for (int k = 0; k < NB; k++) {
+    const int e = min(e0 + 256 * k, E - 1), p = att_pair(e, inv_t);
+    off[k] = p * sp + (e - p * t);
+    zy[k] = ZY[p];
+    a[k] = S2[off[k]];
+  }
+#pragma unroll
+  for (int k = 0; k < NB; k++) {
+    q[k] = make_float2(div_unit_fast(a[k].x, zy[k].x, zy[k].z), div_unit_fast(a[k].y, zy[k].y, zy[k].w));
+    tiny |= div_unit_tiny(a[k].x) | div_unit_tiny(a[k].y);
+  }
+  if (__any_sync(0xffffffffu, tiny))  // numerators below 2^-80: the full division
+#pragma unroll
+    for (int k = 0; k < NB; k++) {
+      if (div_unit_tiny(a[k].x)) q[k].x = __fdiv_rn(a[k].x, zy[k].x);
+      if (div_unit_tiny(a[k].y)) q[k].y = __fdiv_rn(a[k].y, zy[k].y);
+    }
+#pragma unroll
+  for (int k = 0; k < NB; k++)
+    if (e0 + 256 * k < E) S2[off[k]] = q[k];
+}
+// runs batches of 8 slots, then the remainder (Kw slots in all for this warp)
+#define ATT_BATCHES(FN, ...)                                   \
+  {                                                            \
+    int k0 = 0;                                                \
+    for (; k0 + 8 <= Kw; k0 += 8) FN<8>(__VA_ARGS__, tid + 256 * k0); \
+    switch (Kw - k0) {                                         \
+      case 7: FN<7>(__VA_ARGS__, tid + 256 * k0); break;       \
+      case 6: FN<6>(__VA_ARGS__, tid + 256 * k0); break;       \
+      case 5: FN<5>(__VA_ARGS__, tid + 256 * k0); break;       \
+      case 4: FN<4>(__VA_ARGS__, tid + 256 * k0); break;       \
+      case 3: FN<3>(__VA_ARGS__, tid + 256 * k0); break;       \
+      case 2: FN<2>(__VA_ARGS__, tid + 256 * k0); break;       \
+      case 1: FN<1>(__VA_ARGS__, tid + 256 * k0); break;       \
+      default: break;                                          \
+    }                                                          \
+  }
+
 __global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, const float* __restrict__ k,
                                                  const float* __restrict__ v, int ld, Segs s,
                                                  const int* __restrict__ toff, const int* __restrict__ tord,
@@ -788,8 +862,8 @@ __global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, co
   float* Kb = Q + ATT_QT * ATT_RS;        // [2][32][72]
   float* Vb = Q;                          // [2][32][64] (PV phase)
   float2* S2 = reinterpret_cast<float2*>(Q + ATT_A);  // [32][sp]
-  float* Z = reinterpret_cast<float*>(S2 + (ATT_QT / 2) * sp);
-  float* Mx = Z + ATT_QT;                 // [64]: row maxima
+  float* ZY = reinterpret_cast<float*>(S2 + (ATT_QT / 2) * sp);  // [32][4]: z and 1/z of each row pair
+  float* Mx = ZY + 2 * ATT_QT;            // [64]: row maxima
   const int tile = tord ? tord[blockIdx.x] : blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
   int sw = 0;
   if (toff) {
@@ -855,66 +929,41 @@ __global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, co
   __syncthreads();  // scores and row maxima complete; the Q/K region is free
   // the first V chunk streams in while the softmax runs
   att_copy_rows(Vb, HD, v, ld, rb, min(ATT_KC, t), h, tid, a16);
-  // ---- softmax.  e = exp(s - max) over (row pair p, key j): threads tid & 63 take keys
-  // j = tid & 63 + 64u, tid >> 6 the row pairs p = 4w + tid >> 6 (4 keys x 2 rows in flight)
-  const int npair = (ni + 1) >> 1, jl = tid & 63;
-  for (int p = tid >> 6; p < npair; p += 4) {
-    const bool two = 2 * p + 1 < ni;  // the second row of the last pair may be past the tile
-    const float ma = Mx[2 * p], mb = Mx[2 * p + 1];
-    float2* row = S2 + p * sp;
-    for (int jb = 0; jb < t; jb += 256) {
-      float2 a[4];
-#pragma unroll
-      for (int u = 0; u < 4; u++)
-        if (jb + jl + 64 * u < t) a[u] = row[jb + jl + 64 * u];
-#pragma unroll
-      for (int u = 0; u < 4; u++) {
-        const int j = jb + jl + 64 * u;
-        if (j < t) {
-          a[u].x = expf_ref_smem(__fsub_rn(a[u].x, ma), tab);
-          if (two) a[u].y = expf_ref_smem(__fsub_rn(a[u].y, mb), tab);
-          row[j] = a[u];
-        }
-      }
-    }
-  }
+  // ---- softmax: e = exp(s - max) flat over the npair * t row-pair elements; z per row (a
+  // left fold, one thread per row) with its reciprocal; p = e / z flat again.  Kw: the slots of
+  // this warp's first lane (later lanes clamp the one element they may lack)
+  const int npair = (ni + 1) >> 1, E = npair * t, Kw = max(0, (E - warp * 32 + 255) >> 8);
+  const float inv_t = 1.0f / static_cast<float>(t);
+  ATT_BATCHES(att_exp_batch, S2, reinterpret_cast<const float2*>(Mx), tab, sp, t, inv_t, E)
   __syncthreads();
   float* Sf = reinterpret_cast<float*>(S2);
-  if (tid < ni) {  // z: a left fold over j, loads issued 8 at a time ahead of the adds
+  if (tid < ni) {  // z: a left fold over j; the next 8 loads are issued before the current adds
     const float* row = Sf + (tid >> 1) * sp * 2 + (tid & 1);
     float z = 0.0f;
+    float x[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) x[u] = row[2 * min(u, t - 1)];
     int j = 0;
     for (; j + 8 <= t; j += 8) {
-      float x[8];
+      float nx[8];
 #pragma unroll
-      for (int u = 0; u < 8; u++) x[u] = row[2 * (j + u)];
+      for (int u = 0; u < 8; u++) nx[u] = row[2 * min(j + 8 + u, t - 1)];
 #pragma unroll
       for (int u = 0; u < 8; u++) z = __fadd_rn(z, x[u]);
+#pragma unroll
+      for (int u = 0; u < 8; u++) x[u] = nx[u];
     }
-    for (; j < t; j++) z = __fadd_rn(z, row[2 * j]);
-    Z[tid] = z;
+#pragma unroll
+    for (int u = 0; u < 7; u++)
+      if (j + u < t) z = __fadd_rn(z, x[u]);
+    ZY[4 * (tid >> 1) + (tid & 1)] = z;
+    ZY[4 * (tid >> 1) + 2 + (tid & 1)] = __frcp_rn(z);
+  } else if (tid == ni && (ni & 1)) {  // the unused second row of an odd tile's last pair
+    ZY[4 * (tid >> 1) + 1] = 1.0f;
+    ZY[4 * (tid >> 1) + 3] = 1.0f;
   }
   __syncthreads();
-  for (int p = tid >> 6; p < npair; p += 4) {  // p = e / z, same mapping as the exp pass
-    const bool two = 2 * p + 1 < ni;
-    const float za = Z[2 * p], zb = two ? Z[2 * p + 1] : 1.0f;
-    float2* row = S2 + p * sp;
-    for (int jb = 0; jb < t; jb += 256) {
-      float2 a[4];
-#pragma unroll
-      for (int u = 0; u < 4; u++)
-        if (jb + jl + 64 * u < t) a[u] = row[jb + jl + 64 * u];
-#pragma unroll
-      for (int u = 0; u < 4; u++) {
-        const int j = jb + jl + 64 * u;
-        if (j < t) {
-          a[u].x = __fdiv_rn(a[u].x, za);
-          if (two) a[u].y = __fdiv_rn(a[u].y, zb);
-          row[j] = a[u];
-        }
-      }
-    }
-  }
+  ATT_BATCHES(att_div_batch, S2, reinterpret_cast<const float4*>(ZY), sp, t, inv_t, E)
   // ---- PV
   const int pr = 8 * (warp & 1) + (lane & 7), dt = 4 * (warp >> 1) + (lane >> 3);
   const bool live0 = 16 * (warp & 1) < ni, live1 = 32 + 16 * (warp & 1) < ni;  // warp-uniform
@@ -976,6 +1025,13 @@ __global__ void eval_math_k(int fn, const float* __restrict__ x, float* __restri
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const float v = x[i];
+  if (fn == 6) {  // softmax division: y[2i] = x[2i] / x[2i+1] by div_unit_rn, y[2i+1] = x[2i+1]
+    const int i0 = i & ~1;
+    if (i0 + 1 >= n) { y[i] = v; return; }
+    const float b = x[i0 + 1];
+    y[i] = (i & 1) ? b : div_unit_rn(x[i0], b, __frcp_rn(b));
+    return;
+  }
   if (fn >= 4) {  // the packed-pair forms: element i rides in its pair's x or y slot
     const int i0 = i & ~1, i1 = i0 + 1 < n ? i0 + 1 : i0;
     const float2 p = make_float2(x[i0], x[i1]);
@@ -1253,9 +1309,9 @@ int wk_attention_cublas_part(int part, void* stream, const float* q, const float
 
 // Parity hook: evaluate the device restatements of the libm functions the reference calls
 // (fn 0 tanhf, 1 expf, 2 the GELU of src/model.rs:710-712, 3 expm1f; 4 tanhf and 5 the GELU
-// in their packed two-element forms) over n floats.
+// in their packed two-element forms; 6 the softmax division of (x[2i], x[2i+1])) over n floats.
 int wasr_eval_math(int fn, const float* x, float* y, int n, void* stream) {
-  if (!x || !y || fn < 0 || fn > 5) return -1;
+  if (!x || !y || fn < 0 || fn > 6) return -1;
   if (n <= 0) return 0;
   eval_math_k<<<(n + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(fn, x, y, n);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
