@@ -598,10 +598,13 @@ __global__ void __launch_bounds__(256) gelu_quant_ro_k(const float* __restrict__
   int8_t* q = xq + static_cast<int64_t>(row) * k;
   float mx = 0.0f;
   if ((k & 127) == 0 && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
-    // four independent GELUs per lane per step: the long exact tanh chains overlap
+    // four independent GELUs per lane per step: the long exact tanh chains overlap; the next
+    // step's row values are loaded before this step's GELUs
+    float4 nv = __ldg(reinterpret_cast<const float4*>(r + lane * 4));
 #pragma unroll 1
     for (int j = lane * 4; j < k; j += 128) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(r + j));
+      const float4 v = nv;
+      if (j + 128 < k) nv = __ldg(reinterpret_cast<const float4*>(r + j + 128));
       const float2 ga = gelu_ref2(make_float2(v.x, v.y)), gb = gelu_ref2(make_float2(v.z, v.w));
       const float4 gv = make_float4(ga.x, ga.y, gb.x, gb.y);
       *reinterpret_cast<float4*>(g + j) = gv;
