@@ -692,7 +692,7 @@ __global__ void keys_to_ids_k(const unsigned long long* __restrict__ keys, int m
 // (dims 8c+4hl .. 8c+4hl+3), so each 16-byte load of q or k feeds 4 scores (2 bytes of shared
 // memory per exact MAC).  The lane fold keeps the reference order: hl = 0 folds lanes 0-3,
 // hands the partial sum to its partner by one shuffle, and hl = 1 adds lanes 4-7.  PV: a thread owns row
-// pairs (2p, 2p+1) for p = r, r+16 x head dims d0..d0+3; the accumulators pair (row 2p, dim d)
+// pairs (2p, 2p+1) for p = pa, pa+1 x head dims d0..d0+3; the accumulators pair (row 2p, dim d)
 // with (row 2p+1, dim d^1).  K and V chunks stream through two shared buffers by cp.async,
 // one barrier per chunk.  Shared layout: exp table | Q [64][72] + K [2][32][72] (scores) /
 // V [2][32][64] (PV) | S2 [32 row pairs][sp] float2 | ZY [32][4] | Mx [64].
@@ -837,14 +837,12 @@ __device__ __forceinline__ void att_div_batch(float2* S2, const float4* ZY, int 
   for (int k = 0; k < NB; k++)
     if (e0 + 256 * k < E) S2[off[k]] = q[k];
 }
-// runs batches of 8 slots, then the remainder (Kw slots in all for this warp)
+// runs batches of 6 slots, then the remainder (Kw slots in all for this warp)
 #define ATT_BATCHES(FN, ...)                                   \
   {                                                            \
     int k0 = 0;                                                \
-    for (; k0 + 8 <= Kw; k0 += 8) FN<8>(__VA_ARGS__, tid + 256 * k0); \
+    for (; k0 + 6 <= Kw; k0 += 6) FN<6>(__VA_ARGS__, tid + 256 * k0); \
     switch (Kw - k0) {                                         \
-      case 7: FN<7>(__VA_ARGS__, tid + 256 * k0); break;       \
-      case 6: FN<6>(__VA_ARGS__, tid + 256 * k0); break;       \
       case 5: FN<5>(__VA_ARGS__, tid + 256 * k0); break;       \
       case 4: FN<4>(__VA_ARGS__, tid + 256 * k0); break;       \
       case 3: FN<3>(__VA_ARGS__, tid + 256 * k0); break;       \
@@ -967,9 +965,10 @@ __global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, co
   }
   __syncthreads();
   ATT_BATCHES(att_div_batch, S2, reinterpret_cast<const float4*>(ZY), sp, t, inv_t, E)
-  // ---- PV
-  const int pr = 8 * (warp & 1) + (lane & 7), dt = 4 * (warp >> 1) + (lane >> 3);
-  const bool live0 = 16 * (warp & 1) < ni, live1 = 32 + 16 * (warp & 1) < ni;  // warp-uniform
+  // ---- PV: warp w owns rows 8w .. 8w+7 (row pairs pa = 4w + 2rg and pa + 1 for lane half
+  // rg) x dims 4dg .. 4dg+3 (dg = lane & 15): 4 rows x 4 dims per lane
+  const int rg = lane >> 4, dg = lane & 15, pa = 4 * warp + 2 * rg;
+  const bool live = 8 * warp < ni;  // warp-uniform
   float2 o[2][4];
 #pragma unroll
   for (int a = 0; a < 2; a++)
@@ -982,44 +981,34 @@ __global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, co
     if (ch + 1 < nchunks)
       att_copy_rows(Vb + ((ch + 1) & 1) * ATT_KC * HD, HD, v, ld, rb + j0 + ATT_KC, min(ATT_KC, t - j0 - ATT_KC), h,
                     tid, a16);
-    const float2* p0 = S2 + pr * sp + j0;
-    const float2* p1 = S2 + (pr + 16) * sp + j0;
-    const float* vr = Vb + (ch & 1) * ATT_KC * HD + 4 * dt;
-    if (live1) {
+    const float2* p0 = S2 + pa * sp + j0;
+    const float2* p1 = p0 + sp;
+    const float* vr = Vb + (ch & 1) * ATT_KC * HD + 4 * dg;
+    if (live) {
 #pragma unroll 4
       for (int jj = 0; jj < nj; jj++) {
-        const float2 pa = p0[jj], pb = p1[jj];
+        const float2 pa2 = p0[jj], pb2 = p1[jj];
         const float4 x = *reinterpret_cast<const float4*>(vr + jj * HD);
-        o[0][0] = add2_rn(o[0][0], mulp(pa, lo2(x)));
-        o[0][1] = add2_rn(o[0][1], mulp(pa, make_float2(x.y, x.x)));
-        o[0][2] = add2_rn(o[0][2], mulp(pa, hi2(x)));
-        o[0][3] = add2_rn(o[0][3], mulp(pa, make_float2(x.w, x.z)));
-        o[1][0] = add2_rn(o[1][0], mulp(pb, lo2(x)));
-        o[1][1] = add2_rn(o[1][1], mulp(pb, make_float2(x.y, x.x)));
-        o[1][2] = add2_rn(o[1][2], mulp(pb, hi2(x)));
-        o[1][3] = add2_rn(o[1][3], mulp(pb, make_float2(x.w, x.z)));
-      }
-    } else if (live0) {
-#pragma unroll 4
-      for (int jj = 0; jj < nj; jj++) {
-        const float2 pa = p0[jj];
-        const float4 x = *reinterpret_cast<const float4*>(vr + jj * HD);
-        o[0][0] = add2_rn(o[0][0], mulp(pa, lo2(x)));
-        o[0][1] = add2_rn(o[0][1], mulp(pa, make_float2(x.y, x.x)));
-        o[0][2] = add2_rn(o[0][2], mulp(pa, hi2(x)));
-        o[0][3] = add2_rn(o[0][3], mulp(pa, make_float2(x.w, x.z)));
+        o[0][0] = add2_rn(o[0][0], mulp(pa2, lo2(x)));
+        o[0][1] = add2_rn(o[0][1], mulp(pa2, make_float2(x.y, x.x)));
+        o[0][2] = add2_rn(o[0][2], mulp(pa2, hi2(x)));
+        o[0][3] = add2_rn(o[0][3], mulp(pa2, make_float2(x.w, x.z)));
+        o[1][0] = add2_rn(o[1][0], mulp(pb2, lo2(x)));
+        o[1][1] = add2_rn(o[1][1], mulp(pb2, make_float2(x.y, x.x)));
+        o[1][2] = add2_rn(o[1][2], mulp(pb2, hi2(x)));
+        o[1][3] = add2_rn(o[1][3], mulp(pb2, make_float2(x.w, x.z)));
       }
     }
   }
   // o[a][0] = (row 2p d0, row 2p+1 d0+1), o[a][1] = (2p d0+1, 2p+1 d0), [2],[3] likewise at d0+2
 #pragma unroll
   for (int a = 0; a < 2; a++) {
-    const int r0 = 2 * (pr + 16 * a);
+    const int r0 = 2 * (pa + a);
     if (r0 < ni)
-      *reinterpret_cast<float4*>(out + static_cast<int64_t>(rb + i0 + r0) * ldo + h * HD + 4 * dt) =
+      *reinterpret_cast<float4*>(out + static_cast<int64_t>(rb + i0 + r0) * ldo + h * HD + 4 * dg) =
           make_float4(o[a][0].x, o[a][1].x, o[a][2].x, o[a][3].x);
     if (r0 + 1 < ni)
-      *reinterpret_cast<float4*>(out + static_cast<int64_t>(rb + i0 + r0 + 1) * ldo + h * HD + 4 * dt) =
+      *reinterpret_cast<float4*>(out + static_cast<int64_t>(rb + i0 + r0 + 1) * ldo + h * HD + 4 * dg) =
           make_float4(o[a][1].y, o[a][0].y, o[a][3].y, o[a][2].y);
   }
 }
