@@ -521,6 +521,110 @@ __global__ void __launch_bounds__(LN_THREADS) ln_quant_k(float* __restrict__ h, 
   }
 }
 
+// LayerNorm + quant without a residual (the engine's case: the GEMM epilogue already added
+// it), with the block's rows resident in shared memory: 56 rows of 512 floats, loaded once by
+// cp.async in 8 column chunks (one commit group each).  Thread r < 56 folds row r's sum while
+// the chunks land, then its squared deviations from shared memory (the same left folds as
+// ln_quant_k); 8 warps then normalise and quantise the rows from shared memory.  Float4 slot
+// c4 of row r sits at slot c4 ^ (r & 7), so the 8 rows a quarter-warp folds at one column hit
+// distinct banks and a warp's 32 consecutive slots of one row stay conflict-free.  Two blocks
+// (2 x 115 KB) fit an SM, so 16384 rows are one wave of 293 blocks.
+constexpr int LR_ROWS = 56;
+constexpr int LR_THREADS = 256;
+constexpr size_t LR_SMEM = static_cast<size_t>(LR_ROWS) * D * 4 + 2 * LR_ROWS * 4;
+__device__ __forceinline__ int lr_slot(int r, int c4) { return r * (D / 4) + (c4 ^ (r & 7)); }
+__device__ __forceinline__ void cp_async_wait_n(int n) {  // n in 0..7, a run-time count
+  switch (n) {
+    case 7: cp_async_wait<7>(); break;
+    case 6: cp_async_wait<6>(); break;
+    case 5: cp_async_wait<5>(); break;
+    case 4: cp_async_wait<4>(); break;
+    case 3: cp_async_wait<3>(); break;
+    case 2: cp_async_wait<2>(); break;
+    case 1: cp_async_wait<1>(); break;
+    default: cp_async_wait<0>(); break;
+  }
+}
+
+__global__ void __launch_bounds__(LR_THREADS, 2) ln_rows_k(const float* __restrict__ h, const float* __restrict__ g,
+                                                           const float* __restrict__ b, int m,
+                                                           int8_t* __restrict__ xq, float* __restrict__ xs) {
+  extern __shared__ __align__(16) float sm[];
+  float4* S = reinterpret_cast<float4*>(sm);
+  float* mean = sm + LR_ROWS * D;
+  float* rinv = mean + LR_ROWS;
+  const int r0 = blockIdx.x * LR_ROWS, nr = min(LR_ROWS, m - r0), tid = threadIdx.x;
+  for (int c = 0; c < 8; c++) {  // chunk c: columns 64c .. 64c+63 of every row
+    for (int e = tid; e < nr * 16; e += LR_THREADS) {
+      const int rr = e >> 4, c4 = 16 * c + (e & 15);
+      cp_async16(S + lr_slot(rr, c4), h + static_cast<int64_t>(r0 + rr) * D + 4 * c4);
+    }
+    cp_async_commit();
+  }
+  float sum = 0.0f;
+  for (int c = 0; c < 8; c++) {
+    cp_async_wait_n(7 - c);  // this thread's copies of chunk c have landed ...
+    __syncthreads();         // ... and every thread's
+    if (tid < nr) {
+#pragma unroll 8
+      for (int c4 = 16 * c; c4 < 16 * c + 16; c4++) {
+        const float4 v = S[lr_slot(tid, c4)];
+        sum = __fadd_rn(sum, v.x);
+        sum = __fadd_rn(sum, v.y);
+        sum = __fadd_rn(sum, v.z);
+        sum = __fadd_rn(sum, v.w);
+      }
+    }
+  }
+  if (tid < nr) {
+    const float mu = __fdiv_rn(sum, static_cast<float>(D));
+    float s2 = 0.0f;
+#pragma unroll 8
+    for (int c4 = 0; c4 < D / 4; c4++) {
+      const float4 v = S[lr_slot(tid, c4)];
+      const float dx = __fsub_rn(v.x, mu), dy = __fsub_rn(v.y, mu), dz = __fsub_rn(v.z, mu), dw = __fsub_rn(v.w, mu);
+      s2 = __fadd_rn(s2, __fmul_rn(dx, dx));
+      s2 = __fadd_rn(s2, __fmul_rn(dy, dy));
+      s2 = __fadd_rn(s2, __fmul_rn(dz, dz));
+      s2 = __fadd_rn(s2, __fmul_rn(dw, dw));
+    }
+    mean[tid] = mu;
+    rinv[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s2, static_cast<float>(D)), 1e-6f)));
+  }
+  __syncthreads();
+  const int warp = tid >> 5, lane = tid & 31;
+  float4 gg[4], bb[4];
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    gg[k] = __ldg(reinterpret_cast<const float4*>(g) + lane + 32 * k);
+    bb[k] = __ldg(reinterpret_cast<const float4*>(b) + lane + 32 * k);
+  }
+  for (int rr = warp; rr < nr; rr += LR_THREADS / 32) {
+    const float mu_r = mean[rr], iv = rinv[rr];
+    float4 y[4];
+    float mx = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const float4 v = S[lr_slot(rr, lane + 32 * k)];
+      y[k].x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.x, mu_r), iv), gg[k].x), bb[k].x);
+      y[k].y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.y, mu_r), iv), gg[k].y), bb[k].y);
+      y[k].z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.z, mu_r), iv), gg[k].z), bb[k].z);
+      y[k].w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.w, mu_r), iv), gg[k].w), bb[k].w);
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(y[k].x), fabsf(y[k].y)), fmaxf(fabsf(y[k].z), fabsf(y[k].w))));
+    }
+    mx = warp_max(mx);
+    const float sc = quant_scale(mx), inv = quant_inv(sc);
+    char4* q = reinterpret_cast<char4*>(xq + static_cast<int64_t>(r0 + rr) * D);
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      char4 cq;
+      cq.x = quant_one(y[k].x, inv); cq.y = quant_one(y[k].y, inv); cq.z = quant_one(y[k].z, inv); cq.w = quant_one(y[k].w, inv);
+      q[lane + 32 * k] = cq;
+    }
+    if (lane == 0) xs[r0 + rr] = sc;
+  }
+}
+
 // LayerNorm for any d (the reference ABI takes d as an argument): one block per row,
 // thread 0 folds like the CPU.  Used only when d != 512.
 __global__ void __launch_bounds__(256) ln_quant_any_k(float* __restrict__ h, const float* __restrict__ o,
@@ -1045,7 +1149,11 @@ static void set_smem(const void* kern, int bytes) {
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lk(mu);
   if (done.count({kern, dev})) return;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess)
+  // the largest shared-memory carveout, so that as many blocks as fit by shared memory can be
+  // resident (the default may size the carveout for one block)
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess &&
+      cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared) ==
+          cudaSuccess)
     done.insert({kern, dev});
 }
 
@@ -1054,7 +1162,7 @@ bool kern_prepare() {
   set_smem(reinterpret_cast<const void*>(conv3_k), CV3_SMEM);
   set_smem(reinterpret_cast<const void*>(attn_k), 227 * 1024);
   set_smem(reinterpret_cast<const void*>(gelu_quant_ro_k), 227 * 1024);
-  set_smem(reinterpret_cast<const void*>(ln_quant_k<false>), LnCfg<false>::SMEM);
+  set_smem(reinterpret_cast<const void*>(ln_rows_k), LR_SMEM);
   set_smem(reinterpret_cast<const void*>(ln_quant_k<true>), LnCfg<true>::SMEM);
   return cudaGetLastError() == cudaSuccess;
 }
@@ -1123,8 +1231,8 @@ int launch_ln_quant(float* h, const float* o, const float* g, const float* b, in
     set_smem(reinterpret_cast<const void*>(ln_quant_k<true>), LnCfg<true>::SMEM);
     ln_quant_k<true><<<blocks, LN_THREADS, LnCfg<true>::SMEM, st>>>(h, o, g, b, m, xq, xs);
   } else {
-    set_smem(reinterpret_cast<const void*>(ln_quant_k<false>), LnCfg<false>::SMEM);
-    ln_quant_k<false><<<blocks, LN_THREADS, LnCfg<false>::SMEM, st>>>(h, o, g, b, m, xq, xs);
+    set_smem(reinterpret_cast<const void*>(ln_rows_k), LR_SMEM);
+    ln_rows_k<<<(m + LR_ROWS - 1) / LR_ROWS, LR_THREADS, LR_SMEM, st>>>(h, g, b, m, xq, xs);
   }
   return launched();
 }
