@@ -561,32 +561,47 @@ __global__ void __launch_bounds__(LR_THREADS, 2) ln_rows_k(const float* __restri
     }
     cp_async_commit();
   }
+  // the folds are chains of dependent adds: each chunk's loads are all issued before its adds
   float sum = 0.0f;
   for (int c = 0; c < 8; c++) {
     cp_async_wait_n(7 - c);  // this thread's copies of chunk c have landed ...
     __syncthreads();         // ... and every thread's
     if (tid < nr) {
-#pragma unroll 8
-      for (int c4 = 16 * c; c4 < 16 * c + 16; c4++) {
-        const float4 v = S[lr_slot(tid, c4)];
-        sum = __fadd_rn(sum, v.x);
-        sum = __fadd_rn(sum, v.y);
-        sum = __fadd_rn(sum, v.z);
-        sum = __fadd_rn(sum, v.w);
+      float4 v[16];
+#pragma unroll
+      for (int k = 0; k < 16; k++) v[k] = S[lr_slot(tid, 16 * c + k)];
+#pragma unroll
+      for (int k = 0; k < 16; k++) {
+        sum = __fadd_rn(sum, v[k].x);
+        sum = __fadd_rn(sum, v[k].y);
+        sum = __fadd_rn(sum, v[k].z);
+        sum = __fadd_rn(sum, v[k].w);
       }
     }
   }
   if (tid < nr) {
     const float mu = __fdiv_rn(sum, static_cast<float>(D));
     float s2 = 0.0f;
-#pragma unroll 8
-    for (int c4 = 0; c4 < D / 4; c4++) {
-      const float4 v = S[lr_slot(tid, c4)];
-      const float dx = __fsub_rn(v.x, mu), dy = __fsub_rn(v.y, mu), dz = __fsub_rn(v.z, mu), dw = __fsub_rn(v.w, mu);
-      s2 = __fadd_rn(s2, __fmul_rn(dx, dx));
-      s2 = __fadd_rn(s2, __fmul_rn(dy, dy));
-      s2 = __fadd_rn(s2, __fmul_rn(dz, dz));
-      s2 = __fadd_rn(s2, __fmul_rn(dw, dw));
+    float4 cur[8], nxt[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) cur[k] = S[lr_slot(tid, k)];
+#pragma unroll 1
+    for (int c4 = 0; c4 < D / 4; c4 += 8) {
+      if (c4 + 8 < D / 4) {
+#pragma unroll
+        for (int k = 0; k < 8; k++) nxt[k] = S[lr_slot(tid, c4 + 8 + k)];
+      }
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const float4 v = cur[k];
+        const float dx = __fsub_rn(v.x, mu), dy = __fsub_rn(v.y, mu), dz = __fsub_rn(v.z, mu), dw = __fsub_rn(v.w, mu);
+        s2 = __fadd_rn(s2, __fmul_rn(dx, dx));
+        s2 = __fadd_rn(s2, __fmul_rn(dy, dy));
+        s2 = __fadd_rn(s2, __fmul_rn(dz, dz));
+        s2 = __fadd_rn(s2, __fmul_rn(dw, dw));
+      }
+#pragma unroll
+      for (int k = 0; k < 8; k++) cur[k] = nxt[k];
     }
     mean[tid] = mu;
     rinv[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s2, static_cast<float>(D)), 1e-6f)));
@@ -599,29 +614,44 @@ __global__ void __launch_bounds__(LR_THREADS, 2) ln_rows_k(const float* __restri
     gg[k] = __ldg(reinterpret_cast<const float4*>(g) + lane + 32 * k);
     bb[k] = __ldg(reinterpret_cast<const float4*>(b) + lane + 32 * k);
   }
-  for (int rr = warp; rr < nr; rr += LR_THREADS / 32) {
-    const float mu_r = mean[rr], iv = rinv[rr];
-    float4 y[4];
-    float mx = 0.0f;
+  // two rows per step (rr and rr + 8; the second is a repeat of the first past the end), so
+  // the two reductions and quantisations overlap
+  for (int rr = warp; rr < nr; rr += 2 * (LR_THREADS / 32)) {
+    const int r2 = rr + LR_THREADS / 32 < nr ? rr + LR_THREADS / 32 : rr;
+    const int row[2] = {rr, r2};
+    float4 y[2][4];
+    float mx[2] = {0.0f, 0.0f};
 #pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const float4 v = S[lr_slot(rr, lane + 32 * k)];
-      y[k].x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.x, mu_r), iv), gg[k].x), bb[k].x);
-      y[k].y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.y, mu_r), iv), gg[k].y), bb[k].y);
-      y[k].z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.z, mu_r), iv), gg[k].z), bb[k].z);
-      y[k].w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.w, mu_r), iv), gg[k].w), bb[k].w);
-      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(y[k].x), fabsf(y[k].y)), fmaxf(fabsf(y[k].z), fabsf(y[k].w))));
-    }
-    mx = warp_max(mx);
-    const float sc = quant_scale(mx), inv = quant_inv(sc);
-    char4* q = reinterpret_cast<char4*>(xq + static_cast<int64_t>(r0 + rr) * D);
+    for (int a = 0; a < 2; a++) {
+      const float mu_r = mean[row[a]], iv = rinv[row[a]];
 #pragma unroll
-    for (int k = 0; k < 4; k++) {
-      char4 cq;
-      cq.x = quant_one(y[k].x, inv); cq.y = quant_one(y[k].y, inv); cq.z = quant_one(y[k].z, inv); cq.w = quant_one(y[k].w, inv);
-      q[lane + 32 * k] = cq;
+      for (int k = 0; k < 4; k++) {
+        const float4 v = S[lr_slot(row[a], lane + 32 * k)];
+        y[a][k].x = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.x, mu_r), iv), gg[k].x), bb[k].x);
+        y[a][k].y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.y, mu_r), iv), gg[k].y), bb[k].y);
+        y[a][k].z = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.z, mu_r), iv), gg[k].z), bb[k].z);
+        y[a][k].w = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v.w, mu_r), iv), gg[k].w), bb[k].w);
+        mx[a] = fmaxf(mx[a], fmaxf(fmaxf(fabsf(y[a][k].x), fabsf(y[a][k].y)), fmaxf(fabsf(y[a][k].z), fabsf(y[a][k].w))));
+      }
     }
-    if (lane == 0) xs[r0 + rr] = sc;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      mx[0] = fmaxf(mx[0], __shfl_xor_sync(0xffffffffu, mx[0], o));
+      mx[1] = fmaxf(mx[1], __shfl_xor_sync(0xffffffffu, mx[1], o));
+    }
+#pragma unroll
+    for (int a = 0; a < 2; a++) {
+      const float sc = quant_scale(mx[a]), inv = quant_inv(sc);
+      char4* q = reinterpret_cast<char4*>(xq + static_cast<int64_t>(r0 + row[a]) * D);
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        char4 cq;
+        cq.x = quant_one(y[a][k].x, inv); cq.y = quant_one(y[a][k].y, inv);
+        cq.z = quant_one(y[a][k].z, inv); cq.w = quant_one(y[a][k].w, inv);
+        q[lane + 32 * k] = cq;
+      }
+      if (lane == 0) xs[r0 + row[a]] = sc;
+    }
   }
 }
 
