@@ -88,15 +88,18 @@ constexpr int CV2_WS = CV2_CH + 2;         // W2 row stride in float2 (16-byte r
 constexpr int CV2_RW = 48;                 // raw row: 4 zeros | 40 values | 4 zeros (16-byte aligned data)
 constexpr int CV2_RAW = 7 * CV2_CC * CV2_RW;
 constexpr int cmax(int a, int b) { return a > b ? a : b; }
-constexpr int CV2_SMEM = cmax(CV2_MP * (DIM + CV2_WS) * 8 + CV2_RAW * 4 + 2 * CV2_MP * 4, 4 * CV2_CH * DIM * 8);
+constexpr int CV2_PS = DIM + 2;            // partial-lane row stride in float2 (conflict-free stores)
+constexpr int CV2_SMEM = cmax(CV2_MP * (DIM + CV2_WS) * 8 + CV2_RAW * 4 + 2 * CV2_MP * 4, 4 * CV2_CH * CV2_PS * 8);
 
 constexpr int CV3_CH = 64;
 constexpr int CV3_CC = 16;
 constexpr int CV3_MP = CV3_CC * 9 / 2;     // 72
 constexpr int CV3_WS = CV3_CH + 2;
-constexpr int CV3_RW = 44;                 // raw row: the 41 values of a channel (+ unused pad)
+constexpr int CV3_RW = W2;                 // raw row: the 41 values of a channel, so the 16 channels
+                                           // of an input row are one contiguous 16-byte-aligned span
 constexpr int CV3_RAW = 3 * CV3_CC * CV3_RW;
-constexpr int CV3_SMEM = cmax(CV3_MP * (20 + CV3_WS) * 8 + CV3_RAW * 4 + 2 * CV3_MP * 4, 4 * CV3_CH * 20 * 8);
+constexpr int CV3_PS = 21;                 // partial-lane row stride in float2 (conflict-free stores)
+constexpr int CV3_SMEM = cmax(CV3_MP * (20 + CV3_WS) * 8 + CV3_RAW * 4 + 2 * CV3_MP * 4, 4 * CV3_CH * CV3_PS * 8);
 
 __device__ __forceinline__ float2 mulp(float2 a, float2 b) {
   return make_float2(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y));
@@ -223,16 +226,16 @@ __global__ void __launch_bounds__(TP_THREADS, 3) conv2_k(const float* __restrict
     tp_accumulate<DIM, CV2_WS, 4>(X2, Wt, CV2_MP, (q - (c0 >> 1)) & 3, f0, o0, acc);
   }
   __syncthreads();
-  float2* part = reinterpret_cast<float2*>(sm);  // [4][32][40]
+  float2* part = reinterpret_cast<float2*>(sm);  // [4][32][42]
 #pragma unroll
   for (int p = 0; p < TP_P; p++)
 #pragma unroll
-    for (int c = 0; c < TP_C; c++) part[(q * CV2_CH + o0 + c) * DIM + f0 + p] = acc[p][c];
+    for (int c = 0; c < TP_C; c++) part[(q * CV2_CH + o0 + c) * CV2_PS + f0 + p] = acc[p][c];
   __syncthreads();
   float* out = y2 + static_cast<int64_t>(r) * (C2 * W2) + og * CV2_CH * W2;
   for (int e = tid; e < CV2_CH * DIM; e += TP_THREADS) {
     const int o = e / DIM, f = e - o * DIM;
-    out[o * W2 + f] = fmaxf(tp_fold(part, CV2_CH, DIM, o, f), 0.0f);
+    out[o * W2 + f] = fmaxf(tp_fold(part, CV2_CH, CV2_PS, o, f), 0.0f);
   }
   if (tid < CV2_CH) out[tid * W2 + DIM] = 0.0f;
 }
@@ -246,7 +249,7 @@ __global__ void __launch_bounds__(TP_THREADS, 3) conv3_k(const float* __restrict
   extern __shared__ __align__(16) float sm[];
   float2* X2 = reinterpret_cast<float2*>(sm);    // [36][20]
   float2* Wt = X2 + CV3_MP * 20;                  // [36][66]
-  float* raw = reinterpret_cast<float*>(Wt + CV3_MP * CV3_WS);  // [3 rows][8 channels][44]
+  float* raw = reinterpret_cast<float*>(Wt + CV3_MP * CV3_WS);  // [3 rows][16 channels][41]
   int* tapoff = reinterpret_cast<int*>(raw + CV3_RAW);          // [72] tap -> raw offset (+ 2f)
   // the channel groups of a row are adjacent blocks: they read the same input rows from L2
   const int r = row0 + blockIdx.y, og = blockIdx.x, tid = threadIdx.x;
@@ -264,6 +267,7 @@ __global__ void __launch_bounds__(TP_THREADS, 3) conv3_k(const float* __restrict
     if (tt < 0 || tt >= t1) raw[e] = 0.0f;
   }
   const bool w8 = (reinterpret_cast<uintptr_t>(c3) & 7) == 0;
+  const bool y16 = (reinterpret_cast<uintptr_t>(y2) & 15) == 0;
   float2 acc[TP_P][TP_C];
 #pragma unroll
   for (int p = 0; p < TP_P; p++)
@@ -291,11 +295,16 @@ __global__ void __launch_bounds__(TP_THREADS, 3) conv3_k(const float* __restrict
         }
       }
     }
-    for (int e = tid; e < 3 * CV3_CC * W2; e += TP_THREADS) {
-      const int row = e / W2, col = e - row * W2, i = row / CV3_CC, cl = row - i * CV3_CC;
+    for (int i = 0; i < 3; i++) {  // input row i: channels c0 .. c0+15 are 656 contiguous floats
       const int tt = ti + i - 1;
-      if (tt >= 0 && tt < t1)
-        cp_async4(raw + row * CV3_RW + col, y2 + static_cast<int64_t>(rb + tt) * (C2 * W2) + (c0 + cl) * W2 + col);
+      if (tt < 0 || tt >= t1) continue;  // block-uniform; the row stays zero
+      const float* src = y2 + static_cast<int64_t>(rb + tt) * (C2 * W2) + c0 * W2;
+      float* dst = raw + i * CV3_CC * CV3_RW;
+      if (y16) {
+        for (int e = tid; e < CV3_CC * W2 / 4; e += TP_THREADS) cp_async16(dst + 4 * e, src + 4 * e);
+      } else {
+        for (int e = tid; e < CV3_CC * W2; e += TP_THREADS) cp_async4(dst + e, src + e);
+      }
     }
     cp_async_commit();
     cp_async_wait<0>();
@@ -309,16 +318,16 @@ __global__ void __launch_bounds__(TP_THREADS, 3) conv3_k(const float* __restrict
     tp_accumulate<20, CV3_WS, 4>(X2, Wt, CV3_MP, (q - (c0 >> 1)) & 3, f0, o0, acc);
   }
   __syncthreads();
-  float2* part = reinterpret_cast<float2*>(sm);  // [4][64][20]
+  float2* part = reinterpret_cast<float2*>(sm);  // [4][64][21]
 #pragma unroll
   for (int p = 0; p < TP_P; p++)
 #pragma unroll
-    for (int c = 0; c < TP_C; c++) part[(q * CV3_CH + o0 + c) * 20 + f0 + p] = acc[p][c];
+    for (int c = 0; c < TP_C; c++) part[(q * CV3_CH + o0 + c) * CV3_PS + f0 + p] = acc[p][c];
   __syncthreads();
   float* out = y3 + static_cast<int64_t>(r) * FLAT + og * CV3_CH * 20;
   for (int e = tid; e < CV3_CH * 20; e += TP_THREADS) {
     const int o = e / 20, f = e - o * 20;
-    out[o * 20 + f] = fmaxf(tp_fold(part, CV3_CH, 20, o, f), 0.0f);
+    out[o * 20 + f] = fmaxf(tp_fold(part, CV3_CH, CV3_PS, o, f), 0.0f);
   }
 }
 
