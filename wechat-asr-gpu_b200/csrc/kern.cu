@@ -740,18 +740,25 @@ __global__ void __launch_bounds__(256) gelu_quant_ro_k(const float* __restrict__
   const float* r = y + static_cast<int64_t>(row) * k;
   int8_t* q = xq + static_cast<int64_t>(row) * k;
   float mx = 0.0f;
-  if ((k & 127) == 0 && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
-    // four independent GELUs per lane per step: the long exact tanh chains overlap; the next
-    // step's row values are loaded before this step's GELUs
-    float4 nv = __ldg(reinterpret_cast<const float4*>(r + lane * 4));
+  if ((k & 255) == 0 && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
+    // eight independent GELUs per lane per step (columns j .. j+3 and j+128 .. j+131): the long
+    // exact tanh chains overlap; the next step's row values are loaded before this step's GELUs
+    float4 nv0 = __ldg(reinterpret_cast<const float4*>(r + lane * 4));
+    float4 nv1 = __ldg(reinterpret_cast<const float4*>(r + lane * 4 + 128));
 #pragma unroll 1
-    for (int j = lane * 4; j < k; j += 128) {
-      const float4 v = nv;
-      if (j + 128 < k) nv = __ldg(reinterpret_cast<const float4*>(r + j + 128));
-      const float2 ga = gelu_ref2(make_float2(v.x, v.y)), gb = gelu_ref2(make_float2(v.z, v.w));
-      const float4 gv = make_float4(ga.x, ga.y, gb.x, gb.y);
-      *reinterpret_cast<float4*>(g + j) = gv;
-      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(gv.x), fabsf(gv.y)), fmaxf(fabsf(gv.z), fabsf(gv.w))));
+    for (int j = lane * 4; j < k; j += 256) {
+      const float4 v0 = nv0, v1 = nv1;
+      if (j + 256 < k) {
+        nv0 = __ldg(reinterpret_cast<const float4*>(r + j + 256));
+        nv1 = __ldg(reinterpret_cast<const float4*>(r + j + 384));
+      }
+      const float2 ga = gelu_ref2(make_float2(v0.x, v0.y)), gb = gelu_ref2(make_float2(v0.z, v0.w));
+      const float2 gc = gelu_ref2(make_float2(v1.x, v1.y)), gd = gelu_ref2(make_float2(v1.z, v1.w));
+      const float4 g0 = make_float4(ga.x, ga.y, gb.x, gb.y), g1 = make_float4(gc.x, gc.y, gd.x, gd.y);
+      *reinterpret_cast<float4*>(g + j) = g0;
+      *reinterpret_cast<float4*>(g + j + 128) = g1;
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(g0.x), fabsf(g0.y)), fmaxf(fabsf(g0.z), fabsf(g0.w))));
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(g1.x), fabsf(g1.y)), fmaxf(fabsf(g1.z), fabsf(g1.w))));
     }
     mx = warp_max(mx);
     const float sc = quant_scale(mx), inv = quant_inv(sc);
