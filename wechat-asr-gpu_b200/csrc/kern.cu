@@ -347,6 +347,25 @@ __global__ void __launch_bounds__(256) quant_rows_k(const float* __restrict__ x,
   if (row >= m) return;
   const float* r = x + static_cast<int64_t>(row) * ldx;
   const bool vec = ((k & 3) == 0) && ((reinterpret_cast<uintptr_t>(r) & 15) == 0);
+  if (k == D && vec && !rowmax) {  // the engine's rows: held in registers, one pass, loads all in flight
+    float4 v[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) v[i] = *reinterpret_cast<const float4*>(r + lane * 4 + 128 * i);
+    float m4 = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; i++) m4 = fmaxf(m4, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+    m4 = warp_max(m4);
+    const float sc4 = quant_scale(m4), inv4 = quant_inv(sc4);
+    int8_t* q4 = xq + static_cast<int64_t>(row) * k;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      char4 c;
+      c.x = quant_one(v[i].x, inv4); c.y = quant_one(v[i].y, inv4); c.z = quant_one(v[i].z, inv4); c.w = quant_one(v[i].w, inv4);
+      *reinterpret_cast<char4*>(q4 + lane * 4 + 128 * i) = c;
+    }
+    if (lane == 0) xs[row] = sc4;
+    return;
+  }
   float mx;
   if (rowmax) {
     mx = __uint_as_float(rowmax[row]);
