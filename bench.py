@@ -311,6 +311,60 @@ def run_reference(args, rank):
 
 
 # ---------------------------------------------------------------- our arm
+def stream_line(pkg, eng, utts=3, seconds=20.0, chunk_s=0.1, partial_every=5):
+    """The streaming path (src/stream.rs) on the GPU engine: each utterance is fed in chunk_s
+    pieces as audio would arrive, partial() every partial_every pushes (a UI refresh), finish()
+    at the end; one window per decode through the 40-layer model, graphs off as Stream::new sets
+    them below 20000 frames.  Host wall-clock per call (fbank, copy in, forward, copy out, text):
+    the latency a user sees.  Also the host text output (Model::text + tidy) of the e2e ids."""
+    st = pkg.stream
+    vocab = ["<blank>"] + [f"t{i}" for i in range(1, 10502)]
+    chunk = int(round(chunk_s * 16000))
+    part, commit, fin = [], [], []
+    windows, busy, audio = 0, 0.0, 0.0
+    for u in range(utts + 1):  # the first utterance warms up and is not counted
+        pcm = pkg.synth.make_audio(1000 + u, seconds)
+        s = st.Stream(eng, vocab)
+        t_u = time.perf_counter()
+        for k, a in enumerate(range(0, pcm.size, chunk)):
+            s0 = s.s
+            t0 = time.perf_counter()
+            s.push(pcm[a:a + chunk])
+            if s.s != s0 and u:
+                commit.append(time.perf_counter() - t0)
+            if k % partial_every == partial_every - 1:
+                t0 = time.perf_counter()
+                s.partial()
+                if u:
+                    part.append(time.perf_counter() - t0)
+        t0 = time.perf_counter()
+        s.finish()
+        if u:
+            fin.append(time.perf_counter() - t0)
+            busy += time.perf_counter() - t_u
+            audio += pcm.size / 16000.0
+            windows += s.n_windows
+        s.fb.close()
+    eng.set_graphs(True)
+    ms = lambda v, q: round(float(np.quantile(np.asarray(v), q)) * 1e3, 3) if v else None  # noqa: E731
+    return {"partial_ms_p50": ms(part, 0.5), "partial_ms_p99": ms(part, 0.99), "commit_ms_p50": ms(commit, 0.5),
+            "finish_ms_p50": ms(fin, 0.5), "windows": windows, "partials": len(part),
+            "rtf": round(busy / audio, 5) if audio else None, "utterances": utts, "seconds_each": seconds,
+            "chunk_s": chunk_s, "partial_every_s": round(chunk_s * partial_every, 3),
+            "cfg": "prev 200 / blk 400 / post 100 frames + 50 silence, 40 layers, one stream"}
+
+
+def text_line(pkg, ids_list):
+    """Host text output (Model::text + tidy) of every utterance's ids, placeholder vocabulary."""
+    st = pkg.stream
+    vocab = ["<blank>"] + [f"t{i}" for i in range(1, 10502)]
+    t0 = time.perf_counter()
+    n_chars = sum(len(st.tidy(st.text(ids, vocab))) for ids in ids_list)
+    dt = time.perf_counter() - t0
+    return {"utterances": len(ids_list), "ms": round(dt * 1e3, 3), "chars": n_chars,
+            "impl": "Python restatement of Model::text + tidy (src/model.rs:620-642, src/stream.rs:203-210)"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -322,6 +376,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-gemm-probe", action="store_true")
+    ap.add_argument("--no-stream", action="store_true")
     ap.add_argument("--utts", type=int, default=0,
                     help="profiling aid: only the first N config-4 utterances (0 = all 512)")
     args = ap.parse_args()
@@ -478,6 +533,9 @@ def main():
     gprobe = gemm_probe(pkg, local, stream, 2 * bf16) if (rank == 0 and not args.no_gemm_probe) else None
     fbg = gpu_fbank_line(pkg, pcms, feats, local, stream) if (rank == 0 and not args.no_gemm_probe) else None
 
+    strm = stream_line(pkg, eng) if (rank == 0 and not args.no_stream) else None
+    txt = text_line(pkg, e2e_ids) if (rank == 0 and e2e_ids is not None and not args.no_stream) else None
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         orc = load_oracle()
@@ -504,6 +562,7 @@ def main():
                                "scope": "rank 0's utterances, one call per utterance",
                                "impl": "host C++ f64 FFT512 + CMS (src/fbank.rs), OpenMP over frames"},
                 "fbank_gpu": fbg,
+                "stream": strm, "text_host": txt,
                 "gpu_launches": int(launches),
                 "clocks": clocks, "device_error": err}
         print(json.dumps(line), flush=True)

@@ -150,6 +150,21 @@ int64_t wasr_fbank(const int16_t* pcm, int64_t n, float* feats, int64_t cap, flo
 int wasr_fbank_device(const int16_t* pcm, const int64_t* soff, const int64_t* foff, int n, int64_t frames,
                       double* raw, float* feats, float* sil, void* stream);
 
+/* Streaming fbank (src/fbank.rs:122-161, the reference's Fbank): PCM arrives in pieces.
+ *   wasr_fbank_stream_pending: frames a push of n more samples would emit.
+ *   wasr_fbank_stream_push: appends n samples and writes the frames they complete to feats
+ *     ([frames][40] host fp32, cap frames); returns the frame count, or -1 (nothing consumed)
+ *     when cap is short.  Each frame is normalised by the 50-frame rolling mean as it stands
+ *     after that frame, so the frames of any split equal wasr_fbank's frames of the whole.
+ *   wasr_fbank_stream_silence: the silence frame under the rolling mean as it stands now
+ *     (Fbank::silence, which the stream schedule pads its windows with). */
+typedef struct WasrFbank WasrFbank;
+WasrFbank* wasr_fbank_stream_create(void);
+void wasr_fbank_stream_destroy(WasrFbank* st);
+int64_t wasr_fbank_stream_pending(const WasrFbank* st, int64_t n);
+int64_t wasr_fbank_stream_push(WasrFbank* st, const int16_t* pcm, int64_t n, float* feats, int64_t cap);
+int wasr_fbank_stream_silence(const WasrFbank* st, float* sil);
+
 /* CTC collapse (Model::text without the vocabulary, src/model.rs:622-642): drop repeats
  * and blank id 0.  Returns the collapsed length. */
 int64_t wasr_ctc_collapse(const uint32_t* ids, int64_t n, uint32_t* out);

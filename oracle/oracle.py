@@ -51,6 +51,10 @@ def lib():
             "wo_fbank_frame": (None, [P, P]),
             "wo_fbank": (I64, [P, I64, P, I64, P]),
             "wo_transcribe": (I64, [P, P, P, I64, P, I, I, I, P, I64, P]),
+            "wo_stream_commit": (I, [P, P, P, I64, P, I, I, I, P, P, P, I64, P]),
+            "wo_stream_tail": (I64, [P, P, P, I64, P, I, I64, P, I64, I, P, I64, P]),
+            "wo_text": (I64, [P, I64, P, I64, P, I64]),
+            "wo_tidy": (I64, [C.c_char_p, I]),
         }
         for k, (r, a) in sig.items():
             f = getattr(L, k)
@@ -206,3 +210,80 @@ def ctc(ids):
     out = np.zeros(max(ids.size, 1), np.uint32)
     m = lib().wo_ctc(_p(ids), ids.size, _p(out))
     return out[:m]
+
+
+# ---- text output (Model::text src/model.rs:620-642, tidy src/stream.rs:203-210)
+def text(ids, vocab) -> str:
+    """ids -> text by the C restatement of Model::text."""
+    ids = np.ascontiguousarray(ids, np.uint32)
+    toks = [t.encode("utf-8") for t in vocab]
+    arr = (C.c_char_p * len(toks))(*toks)
+    cap = 16 + sum(len(toks[i]) + 1 for i in ids.tolist() if i < len(toks))
+    out = C.create_string_buffer(cap)
+    n = lib().wo_text(_p(ids), ids.size, C.cast(arr, C.c_void_p), len(toks), C.cast(out, C.c_void_p), cap)
+    if n < 0:
+        raise ValueError("id outside the vocabulary")
+    return out.raw[:n].decode("utf-8")
+
+
+def tidy(s: str, trim_end: bool = False) -> str:
+    """tidy() of the C restatement; trim_end also strips trailing punctuation (partial())."""
+    buf = C.create_string_buffer(s.encode("utf-8"))
+    n = lib().wo_tidy(buf, 1 if trim_end else 0)
+    return buf.raw[:n].decode("utf-8")
+
+
+# ---- streaming schedule (src/stream.rs:58-168)
+class Stream:
+    """The reference's Stream restated on the oracle: the features of the audio so far come from
+    the whole-prefix fbank (the rolling mean is causal, so the prefix's frames are the stream's
+    frames) together with the silence frame under the prefix's final rolling mean; the commit
+    loop, partial and finish ids come from the C restatement, every window through wo_forward.
+    vocab None: partial() / finish() return ids; else text as Stream::partial / finish do."""
+
+    def __init__(self, blob, plan, vocab=None, prev=200, blk=400, post=100):
+        self.blob, self.plan, self.vocab = blob, plan, vocab
+        self.prev, self.blk, self.post = prev, blk, post
+        self.pcm = np.zeros(0, np.int16)
+        self.s = C.c_int64(0)
+        self.ids = np.zeros(64, np.uint32)
+        self.n_ids = C.c_int64(0)
+        self.n_fwd = 0
+        self.feats = np.zeros((0, 40), np.float32)
+        self.sil = np.zeros(40, np.float32)
+
+    def push(self, pcm):
+        self.pcm = np.concatenate([self.pcm, np.asarray(pcm, np.int16)])
+        self.feats, self.sil = fbank(self.pcm)
+        n = self.feats.shape[0]
+        cap = n // 5 + 64
+        if self.ids.size < cap:
+            grown = np.zeros(cap, np.uint32)
+            grown[:self.n_ids.value] = self.ids[:self.n_ids.value]
+            self.ids = grown
+        nf = C.c_int(0)
+        rc = lib().wo_stream_commit(_p(self.blob), C.byref(self.plan), _p(self.feats), n, _p(self.sil), self.prev,
+                                    self.blk, self.post, C.byref(self.s), _p(self.ids), C.byref(self.n_ids),
+                                    self.ids.size, C.byref(nf))
+        assert rc == 0
+        self.n_fwd += nf.value
+
+    def _tail(self, finish: bool):
+        n = self.feats.shape[0]
+        cap = n // 5 + 64 + self.n_ids.value
+        out = np.zeros(cap, np.uint32)
+        nf = C.c_int(0)
+        m = lib().wo_stream_tail(_p(self.blob), C.byref(self.plan), _p(self.feats), n, _p(self.sil), self.prev,
+                                 self.s.value, _p(self.ids), self.n_ids.value, 1 if finish else 0, _p(out), cap,
+                                 C.byref(nf))
+        assert m >= 0
+        self.n_fwd += nf.value
+        return out[:m]
+
+    def partial(self):
+        ids = self._tail(False)
+        return ids if self.vocab is None else tidy(text(ids, self.vocab), trim_end=True)
+
+    def finish(self):
+        ids = self._tail(True)
+        return ids if self.vocab is None else tidy(text(ids, self.vocab))

@@ -623,3 +623,147 @@ int64_t wo_transcribe(const uint8_t* blob, const WasrPlan* plan, const float* fe
   free(buf);
   return len;
 }
+
+/* ---- streaming schedule (src/stream.rs:128-168) over features that arrive in pieces.  The
+ * caller keeps every frame so far (feats, n), the silence frame as the stream's fbank gives it
+ * now (sil), and the stream state: the commit position *s and the committed ids (ids, *n_ids). */
+
+/* push's loop (src/stream.rs:67-69): commit() while n >= s + blk + post (136-147) */
+int wo_stream_commit(const uint8_t* blob, const WasrPlan* plan, const float* feats, int64_t n,
+                     const float* sil, int prev, int blk, int post, int64_t* s, uint32_t* ids,
+                     int64_t* n_ids, int64_t cap, int* n_fwd) {
+  uint32_t* buf = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)(n / 5 + 64));
+  while (n >= *s + blk + post) {
+    int64_t m = decode(blob, plan, feats, sil, *s, prev, *s + blk + post, WASR_PAD, buf, n_fwd);
+    if (m > blk / 5) m = blk / 5;
+    for (int64_t c = m - 1; c >= m / 2 && c >= 1; c--)
+      if (buf[c] == 0 && buf[c - 1] == 0) {
+        m = c;
+        break;
+      }
+    if (*n_ids + m > cap) { free(buf); return -1; }
+    memcpy(ids + *n_ids, buf, sizeof(uint32_t) * (size_t)m);
+    *n_ids += m;
+    *s += m * 5;
+  }
+  free(buf);
+  return 0;
+}
+
+/* partial() ids (src/stream.rs:150-157): the committed ids, then the open tail decoded with
+ * half the left context; finish() ids (159-168): the whole utterance at once when it is at most
+ * WHOLE_MAX frames, else the committed ids and the tail with the full left context.  Returns the
+ * id count written to out, or -1. */
+int64_t wo_stream_tail(const uint8_t* blob, const WasrPlan* plan, const float* feats, int64_t n,
+                       const float* sil, int prev, int64_t s, const uint32_t* ids, int64_t n_ids,
+                       int finish, uint32_t* out, int64_t cap, int* n_fwd) {
+  if (finish && n <= WASR_WHOLE_MAX) {
+    const int64_t t1 = n >= 5 ? (n - 5) / 5 + 1 : 0;
+    if (t1 > cap) return -1;
+    if (t1 > 0) {
+      wo_forward(blob, plan, feats, (int)n, out, NULL);
+      if (n_fwd) (*n_fwd)++;
+    }
+    return t1;
+  }
+  if (n_ids > cap) return -1;
+  memcpy(out, ids, sizeof(uint32_t) * (size_t)n_ids);
+  int64_t len = n_ids;
+  if (n > s) {
+    uint32_t* buf = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)(n / 5 + 64));
+    const int64_t m = decode(blob, plan, feats, sil, s, finish ? prev : prev / 2, n, WASR_PAD, buf, n_fwd);
+    if (len + m > cap) { free(buf); return -1; }
+    memcpy(out + len, buf, sizeof(uint32_t) * (size_t)m);
+    len += m;
+    free(buf);
+  }
+  return len;
+}
+
+/* ---- text output: Model::text (src/model.rs:620-642) and tidy (src/stream.rs:203-210) */
+
+/* UTF-8 helpers: length of the sequence starting at p, and its code point */
+static int u8len(const unsigned char* p) {
+  return p[0] < 0x80 ? 1 : (p[0] >> 5) == 6 ? 2 : (p[0] >> 4) == 14 ? 3 : 4;
+}
+static uint32_t u8cp(const unsigned char* p) {
+  const int l = u8len(p);
+  if (l == 1) return p[0];
+  if (l == 2) return ((uint32_t)(p[0] & 31) << 6) | (p[1] & 63);
+  if (l == 3) return ((uint32_t)(p[0] & 15) << 12) | ((uint32_t)(p[1] & 63) << 6) | (p[2] & 63);
+  return ((uint32_t)(p[0] & 7) << 18) | ((uint32_t)(p[1] & 63) << 12) | ((uint32_t)(p[2] & 63) << 6) | (p[3] & 63);
+}
+/* PUNCT of src/stream.rs:173: ，。？！、,.?! */
+static int is_punct(uint32_t c) {
+  return c == 0xFF0C || c == 0x3002 || c == 0xFF1F || c == 0xFF01 || c == 0x3001 || c == ',' || c == '.' ||
+         c == '?' || c == '!';
+}
+
+/* ids -> UTF-8 text: repeats and blank 0 dropped, "<UNK>" skipped, "<SPACE>" a space, "|w"
+ * starts an English word (a space first when the text ends in an ASCII letter or digit).
+ * vocab: n_vocab NUL-terminated UTF-8 tokens.  Returns the byte length (out is NUL-terminated),
+ * or -1 if cap is short or an id is outside the vocabulary. */
+int64_t wo_text(const uint32_t* ids, int64_t n, const char* const* vocab, int64_t n_vocab, char* out, int64_t cap) {
+  int64_t len = 0;
+  uint32_t prevt = 0xFFFFFFFFu;
+  if (cap < 1) return -1;
+  for (int64_t k = 0; k < n; k++) {
+    const uint32_t i = ids[k];
+    if (i != prevt && i != 0) {
+      if ((int64_t)i >= n_vocab) return -1;
+      const char* t = vocab[i];
+      const size_t tl = strlen(t);
+      if (strcmp(t, "<UNK>") == 0) {
+      } else if (strcmp(t, "<SPACE>") == 0) {
+        if (len + 2 > cap) return -1;
+        out[len++] = ' ';
+      } else if (tl > 1 && t[0] == '|') {
+        const char last = len > 0 ? out[len - 1] : 0;
+        const int alnum = (last >= '0' && last <= '9') || (last >= 'a' && last <= 'z') || (last >= 'A' && last <= 'Z');
+        if (len + (alnum ? 1 : 0) + (int64_t)tl > cap) return -1;
+        if (alnum) out[len++] = ' ';
+        memcpy(out + len, t + 1, tl - 1);
+        len += (int64_t)tl - 1;
+      } else {
+        if (len + (int64_t)tl + 1 > cap) return -1;
+        memcpy(out + len, t, tl);
+        len += (int64_t)tl;
+      }
+    }
+    prevt = i;
+  }
+  out[len] = 0;
+  return len;
+}
+
+/* tidy: leading punctuation removed; of a run of punctuation marks only the last kept.
+ * trim_end: also remove trailing punctuation (partial()).  In place; returns the new length. */
+int64_t wo_tidy(char* s, int trim_end) {
+  const unsigned char* p = (const unsigned char*)s;
+  int64_t n = (int64_t)strlen(s), i = 0, o = 0;
+  while (i < n && is_punct(u8cp(p + i))) i += u8len(p + i);
+  char* w = s;
+  while (i < n) {
+    const int l = u8len(p + i);
+    const int pc = is_punct(u8cp(p + i));
+    const int next_pc = i + l < n && is_punct(u8cp(p + i + l));
+    if (!(pc && next_pc)) {
+      memmove(w + o, s + i, (size_t)l);
+      o += l;
+    }
+    i += l;
+  }
+  w[o] = 0;
+  if (trim_end) {
+    /* strip trailing punctuation: find the last non-punctuation character */
+    int64_t j = 0, keep = 0;
+    while (j < o) {
+      const int l = u8len((const unsigned char*)w + j);
+      if (!is_punct(u8cp((const unsigned char*)w + j))) keep = j + l;
+      j += l;
+    }
+    o = keep;
+    w[o] = 0;
+  }
+  return o;
+}

@@ -74,6 +74,17 @@ int64_t wo_fbank(const int16_t* pcm, int64_t n, float* feats, int64_t cap, float
 int64_t wo_transcribe(const uint8_t* blob, const WasrPlan* plan, const float* feats, int64_t n,
                       const float* sil, int prev, int blk, int post, uint32_t* ids, int64_t ids_cap,
                       int* n_fwd);
+/* src/stream.rs:128-168 for features arriving in pieces: push's commit loop, and the ids of
+ * partial() (finish = 0) or finish() (finish = 1). */
+int wo_stream_commit(const uint8_t* blob, const WasrPlan* plan, const float* feats, int64_t n,
+                     const float* sil, int prev, int blk, int post, int64_t* s, uint32_t* ids,
+                     int64_t* n_ids, int64_t cap, int* n_fwd);
+int64_t wo_stream_tail(const uint8_t* blob, const WasrPlan* plan, const float* feats, int64_t n,
+                       const float* sil, int prev, int64_t s, const uint32_t* ids, int64_t n_ids,
+                       int finish, uint32_t* out, int64_t cap, int* n_fwd);
+/* Model::text (src/model.rs:620-642) and tidy (src/stream.rs:203-210), UTF-8 */
+int64_t wo_text(const uint32_t* ids, int64_t n, const char* const* vocab, int64_t n_vocab, char* out, int64_t cap);
+int64_t wo_tidy(char* s, int trim_end);
 
 #ifdef __cplusplus
 }

@@ -8,6 +8,8 @@ that ABI:
   * :mod:`.abi`    -- ctypes bindings and the weight-blob plan struct
   * :mod:`.synth`  -- seeded synthetic models, audio and workload configurations
   * :mod:`.xnet`   -- the reference's model directory (.xnet + dictionary): parse, load, write
+  * :mod:`.stream` -- the reference's streaming front end (Stream::push / partial / finish,
+                      src/stream.rs) and text output (Model::text, tidy) over the engine
   * :mod:`.host`   -- ``Engine`` (batched engine) and ``Gpu`` / ``WindowModel``, a mirror of
                       the reference's Rust FFI wrapper (src/gpu.rs) and per-window GPU
                       forward (src/model.rs:504-619) driven through the reference ABI
@@ -15,7 +17,7 @@ that ABI:
 
 There is no CPU fallback anywhere on this path: if the library is missing, loading fails.
 """
-from . import abi, dist, synth, xnet  # noqa: F401
+from . import abi, dist, stream, synth, xnet  # noqa: F401
 from .host import Engine, Gpu, WindowModel, fbank, ctc_collapse  # noqa: F401
 
-__all__ = ["abi", "dist", "synth", "xnet", "Engine", "Gpu", "WindowModel", "fbank", "ctc_collapse"]
+__all__ = ["abi", "dist", "stream", "synth", "xnet", "Engine", "Gpu", "WindowModel", "fbank", "ctc_collapse"]

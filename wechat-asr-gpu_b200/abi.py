@@ -104,6 +104,11 @@ SIGNATURES = {
     "wasr_transcribe": (I, [P, P, P, P, I, I, I, I, P, P, I64]),
     "wasr_fbank": (I64, [P, I64, P, I64, P]),
     "wasr_fbank_device": (I, [P, P, P, I, I64, P, P, P, P]),
+    "wasr_fbank_stream_create": (P, []),
+    "wasr_fbank_stream_destroy": (None, [P]),
+    "wasr_fbank_stream_pending": (I64, [P, I64]),
+    "wasr_fbank_stream_push": (I64, [P, P, I64, P, I64]),
+    "wasr_fbank_stream_silence": (I, [P, P]),
     "wasr_ctc_collapse": (I64, [P, I64, P]),
     "wasr_eval_math": (I, [I, P, P, I, P]),
     "wasr_version": (C.c_char_p, []),

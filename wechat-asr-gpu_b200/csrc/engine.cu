@@ -21,6 +21,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <deque>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -672,6 +673,66 @@ int64_t wasr_fbank(const int16_t* pcm, int64_t n, float* feats, int64_t cap, flo
     for (int i = 0; i < DIM; i++) sil[i] = static_cast<float>(s[i] - sum[i] / nn);
   }
   return nfr;
+}
+
+// Streaming fbank (src/fbank.rs:122-161 Fbank): PCM arrives in pieces; a push emits the frames
+// its samples complete, each normalised by the rolling mean as it stands after that frame, and
+// the silence frame uses the rolling mean as it stands now.  The same frame() and CMS order as
+// wasr_fbank, so the frames of any split of a signal equal wasr_fbank's frames of the whole.
+struct WasrFbank {
+  std::vector<int16_t> buf;                  // samples not yet consumed by a frame hop
+  std::deque<std::vector<double>> hist;      // raw frames in the rolling window (<= CMS_WIN)
+  double sum[fb::FDIM] = {0};
+};
+
+WasrFbank* wasr_fbank_stream_create() { return new (std::nothrow) WasrFbank(); }
+void wasr_fbank_stream_destroy(WasrFbank* st) { delete st; }
+
+int64_t wasr_fbank_stream_pending(const WasrFbank* st, int64_t n) {
+  if (!st || n < 0) return -1;
+  const int64_t have = static_cast<int64_t>(st->buf.size()) + n;
+  return have >= fb::WIN ? (have - fb::WIN) / fb::HOP + 1 : 0;
+}
+
+int64_t wasr_fbank_stream_push(WasrFbank* st, const int16_t* pcm, int64_t n, float* feats, int64_t cap) {
+  using namespace fb;
+  if (!st || n < 0 || (!pcm && n > 0)) return -1;
+  const int64_t nfr = wasr_fbank_stream_pending(st, n);
+  if (nfr > 0 && (!feats || nfr > cap)) return -1;  // nothing is consumed
+  st->buf.insert(st->buf.end(), pcm, pcm + n);
+  if (nfr == 0) return 0;
+  std::vector<double> raw(static_cast<size_t>(nfr) * FDIM);
+  (void)tables();
+  if (nfr >= 16) {  // frames are independent: parallel like the reference's rayon path
+#pragma omp parallel for schedule(static)
+    for (int64_t k = 0; k < nfr; k++) frame(st->buf.data() + k * HOP, raw.data() + k * FDIM);
+  } else {
+    for (int64_t k = 0; k < nfr; k++) frame(st->buf.data() + k * HOP, raw.data() + k * FDIM);
+  }
+  for (int64_t k = 0; k < nfr; k++) {  // the rolling mean, in frame order
+    const double* f = raw.data() + k * FDIM;
+    if (static_cast<int>(st->hist.size()) == CMS_WIN) {
+      const std::vector<double>& o = st->hist.front();
+      for (int i = 0; i < FDIM; i++) st->sum[i] -= o[i];
+      st->hist.pop_front();
+    }
+    st->hist.emplace_back(f, f + FDIM);
+    for (int i = 0; i < FDIM; i++) st->sum[i] += f[i];
+    const double nn = static_cast<double>(st->hist.size());
+    for (int i = 0; i < FDIM; i++) feats[k * FDIM + i] = static_cast<float>(f[i] - st->sum[i] / nn);
+  }
+  st->buf.erase(st->buf.begin(), st->buf.begin() + nfr * HOP);
+  return nfr;
+}
+
+int wasr_fbank_stream_silence(const WasrFbank* st, float* sil) {
+  using namespace fb;
+  if (!st || !sil) return -1;
+  double s[FDIM] = {0};
+  s[NCH] = std::log(1e-10);
+  const double nn = static_cast<double>(st->hist.empty() ? 1 : st->hist.size());
+  for (int i = 0; i < FDIM; i++) sil[i] = static_cast<float>(s[i] - st->sum[i] / nn);
+  return 0;
 }
 
 int64_t wasr_ctc_collapse(const uint32_t* ids, int64_t n, uint32_t* out) {

@@ -176,6 +176,30 @@ def tensors_from_blob(blob: np.ndarray, plan: WasrPlan) -> list[tuple[str, int, 
     return out
 
 
+def rust_lines(s: str) -> list[str]:
+    """Rust's str::lines: split at '\\n', one trailing '\\r' removed per line, and no empty last
+    line for a final line ending (other Unicode line separators stay inside the line)."""
+    if not s:
+        return []
+    parts = s.split("\n")
+    if s.endswith("\n"):
+        parts.pop()
+    return [p[:-1] if p.endswith("\r") else p for p in parts]
+
+
+def read_vocab(path: str) -> list[str]:
+    """dict.decoder.utf8.txt as Model::load reads it (src/model.rs:267-271): UTF-8 (invalid
+    bytes are an error), lines as str::lines gives them, the token the second space-separated
+    field ("" when there is none)."""
+    with open(path, "rb") as f:
+        data = f.read().decode("utf-8")
+    out = []
+    for ln in rust_lines(data):
+        fields = ln.split(" ")
+        out.append(fields[1] if len(fields) > 1 else "")
+    return out
+
+
 def write_model_dir(path: str, blob: np.ndarray, plan: WasrPlan, tokens: list[str] | None = None) -> None:
     """Write `model.xnet` and `dict.decoder.utf8.txt` for a 40-layer blob/plan into `path`."""
     os.makedirs(path, exist_ok=True)
@@ -241,8 +265,7 @@ def load_plan(path: str):
         return x
 
     vocab = rec("output_conv.bias").dims[0] if rec("output_conv.bias").dims else 0
-    with open(os.path.join(path, "dict.decoder.utf8.txt"), encoding="utf-8") as f:
-        tokens = [(ln.split(" ")[1] if len(ln.split(" ")) > 1 else "") for ln in f.read().splitlines()]
+    tokens = read_vocab(os.path.join(path, "dict.decoder.utf8.txt"))
     if len(tokens) != vocab:
         raise ValueError(f"vocabulary size {len(tokens)} != model output {vocab}")
     out_n = (vocab + 3) // 4 * 4
