@@ -533,8 +533,9 @@ def main():
     gprobe = gemm_probe(pkg, local, stream, 2 * bf16) if (rank == 0 and not args.no_gemm_probe) else None
     fbg = gpu_fbank_line(pkg, pcms, feats, local, stream) if (rank == 0 and not args.no_gemm_probe) else None
 
-    strm = stream_line(pkg, eng) if (rank == 0 and not args.no_stream) else None
-    txt = text_line(pkg, e2e_ids) if (rank == 0 and e2e_ids is not None and not args.no_stream) else None
+    # single-stream latency does not depend on N: measured at N = 1 only
+    strm = stream_line(pkg, eng) if (world == 1 and not args.no_stream) else None
+    txt = text_line(pkg, e2e_ids) if (world == 1 and e2e_ids is not None and not args.no_stream) else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
