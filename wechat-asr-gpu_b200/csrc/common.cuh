@@ -81,6 +81,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, uin
       : "memory");
 }
 
+// Prefetch of one 2-D box into L2 (no shared memory, no completion: a hint).  x must satisfy
+// the same 16-byte rule as a load.
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* m, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(m)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
 // 2-D tiled store of one box from shared memory (bulk-group completion).  The box is clipped
 // to the tensor's bounds, so rows / columns past the end are never written.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, const void* src, int x, int y) {

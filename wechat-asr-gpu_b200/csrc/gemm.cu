@@ -95,14 +95,14 @@ int num_sms() {
 
 // Opt the kernel into its dynamic shared memory once per device (outside any capture: the
 // host entry points call gemm_prepare() at context / model creation).
-template <int BN, int EPI>
+template <int BN, int EPI, int EW = 8>
 bool ensure_attr() {
   static unsigned done = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (done & (1u << (dev & 31))) return true;
-  if (cudaFuncSetAttribute(gemm_i8_tc<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<BN, EPI>::SMEM) !=
-      cudaSuccess)
+  if (cudaFuncSetAttribute(gemm_i8_tc<BN, EPI, EW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           TcCfg<BN, EPI, EW>::SMEM) != cudaSuccess)
     return false;
   done |= 1u << (dev & 31);
   return true;
@@ -110,10 +110,11 @@ bool ensure_attr() {
 
 template <int EPI>
 bool prepare_epi() {
-  return ensure_attr<256, EPI>() && ensure_attr<128, EPI>() && ensure_attr<64, EPI>();
+  return ensure_attr<256, EPI>() && ensure_attr<128, EPI>() && ensure_attr<64, EPI>() &&
+         (EPI != EPI_F32_ADD || ensure_attr<128, EPI, 4>());
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, int EW = 8>
 int launch_tc(const GemmArgs& g0, cudaStream_t s) {
   CUtensorMap ta, tb, to;
   if (!tensor_map(g0.a, g0.M, g0.K, g0.K, 128, 0, &ta) || !tensor_map(g0.b, g0.N, g0.K, g0.K, BN, 0, &tb)) return -4;
@@ -123,10 +124,10 @@ int launch_tc(const GemmArgs& g0, cudaStream_t s) {
   g.tma_out = EPI != EPI_ARGMAX && obase && (reinterpret_cast<uintptr_t>(obase) % 16 == 0) && (g.ldo % 4 == 0) &&
               tensor_map(obase, g.M, g.n_store, g.ldo, 32, 1, &to);
   if (!g.tma_out) memset(&to, 0, sizeof(to));
-  constexpr int smem = TcCfg<BN, EPI>::SMEM;
-  if (!ensure_attr<BN, EPI>()) return -4;
+  constexpr int smem = TcCfg<BN, EPI, EW>::SMEM;
+  if (!ensure_attr<BN, EPI, EW>()) return -4;
   const int tiles = ((g.n_store + BN - 1) / BN) * ((g.M + 127) / 128);
-  gemm_i8_tc<BN, EPI><<<std::min(tiles, num_sms()), TcCfg<BN, EPI>::THREADS, smem, s>>>(ta, tb, to, g);
+  gemm_i8_tc<BN, EPI, EW><<<std::min(tiles, num_sms()), TcCfg<BN, EPI, EW>::THREADS, smem, s>>>(ta, tb, to, g);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 
@@ -144,6 +145,9 @@ int launch_epi(const GemmArgs& g, cudaStream_t s) {
   auto ctas = [&](int bn) { return tm * ((g.n_store + bn - 1) / bn); };
   // (the residual epilogue keeps 3 staging blocks per warp: at BN=256 only 2 ring stages fit)
   if (EPI != EPI_F32_ADD && ctas(256) >= sms) return launch_tc<256, EPI>(g, s);
+  // a long K keeps the tensor pipe busy longer than the residual epilogue: 4 epilogue warps
+  // leave shared memory for 5 ring stages instead of 3
+  if (EPI == EPI_F32_ADD && g.K >= 1024 && ctas(128) >= sms) return launch_tc<128, EPI, 4>(g, s);
   if (ctas(128) >= sms) return launch_tc<128, EPI>(g, s);
   return launch_tc<64, EPI>(g, s);
 }

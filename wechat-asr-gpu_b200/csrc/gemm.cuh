@@ -114,7 +114,9 @@ __device__ __forceinline__ void epi_finish_row(const GemmArgs& g, int row, float
   }
 }
 
-template <int BN, int EPI>
+// EW: epilogue warps, 8 (two per TMEM lane quarter, half the columns each) or 4 (one per
+// quarter, all columns) -- the latter frees shared memory for deeper K pipelines.
+template <int BN, int EPI, int EW = 8>
 struct TcCfg {
   static_assert(BN == 64 || BN == 128 || BN == 256, "tile width");
   static constexpr int BM = 128;
@@ -124,8 +126,10 @@ struct TcCfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   // staging buffers per epilogue warp: 2 for stores, 3 when h blocks are loaded ahead as well
   static constexpr int NBUF = EPI == EPI_F32_ADD ? 3 : 2;
-  static constexpr int STAGES = BN >= 256 ? (EPI == EPI_F32_ADD ? 2 : 3) : (EPI == EPI_F32_ADD && BN == 128 ? 3 : 4);
-  static constexpr int EPI_WARPS = 8;                 // two per TMEM lane quarter, half the columns each
+  static constexpr int STAGES = EW == 4 ? 5 : BN >= 256 ? (EPI == EPI_F32_ADD ? 2 : 3) : (EPI == EPI_F32_ADD && BN == 128 ? 3 : 4);
+  static_assert(EW == 8 || EW == 4, "epilogue warps");
+  static constexpr int EPI_WARPS = EW;
+  static constexpr int HALVES = EW / 4;               // column halves of a tile per lane quarter
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int TMEM_COLS = 2 * BN;            // two accumulator buffers
   static constexpr int STG_FLOATS = 32 * 32;          // one 32 x 32 block (4 KB, 1024-byte aligned)
@@ -301,11 +305,11 @@ __device__ __forceinline__ void epi_block_tma(const GemmArgs& g, float* buf, con
 // walks its sequence of 32 x 32 output blocks (BN/64 per tile); on the TMA path block cc is
 // staged in buffer cc % NBUF and stored with one bulk tensor store, and for the residual
 // epilogue lane 0 loads the h block of cc+2 as soon as its buffer's last store has read it.
-template <int BN, int EPI>
-__global__ void __launch_bounds__(TcCfg<BN, EPI>::THREADS, 1)
+template <int BN, int EPI, int EW = 8>
+__global__ void __launch_bounds__(TcCfg<BN, EPI, EW>::THREADS, 1)
     gemm_i8_tc(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                const __grid_constant__ CUtensorMap tma_o, GemmArgs g) {
-  using Cfg = TcCfg<BN, EPI>;
+  using Cfg = TcCfg<BN, EPI, EW>;
   constexpr int ST = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -405,10 +409,11 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI>::THREADS, 1)
     }
   } else {
     const int e = warp - 2, q = warp & 3, half = e >> 2;  // TMEM lane quarter = warp % 4
+    constexpr int HW = BN / Cfg::HALVES;                    // columns of a tile per warp
     float* wb = stg_all + e * Cfg::NBUF * Cfg::STG_FLOATS;
     float* colc = colc_all + e * Cfg::COLC;
     uint64_t* hb = hbar + e * Cfg::NBUF;
-    constexpr int CPT = BN / 64;  // 32-column blocks per tile for this warp
+    constexpr int CPT = HW / 32;  // 32-column blocks per tile for this warp
     // block cc of this warp's sequence -> (first row, first column); false past the last tile
     // or past n_store
     auto block_at = [&](int cc, int& row, int& col) {
@@ -416,7 +421,7 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI>::THREADS, 1)
       const int tile = blockIdx.x + k * gridDim.x;
       if (tile >= tiles) return false;
       row = (tile / n_tiles) * Cfg::BM + q * 32;
-      col = (tile % n_tiles) * BN + half * (BN / 2) + 32 * (cc - k * CPT);
+      col = (tile % n_tiles) * BN + half * HW + 32 * (cc - k * CPT);
       return col < g.n_store;
     };
     uint32_t hpar = 0, pend = 0;  // per-buffer phase parity (all lanes); loads in flight (lane 0)
@@ -428,10 +433,17 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI>::THREADS, 1)
       tma_load_2d(wb + bi * Cfg::STG_FLOATS, &tma_o, hb + bi, col, row);
       pend |= 1u << bi;
     };
+    // with the long-K configuration (4 epilogue warps), h blocks one tile ahead of their load
+    // are prefetched into L2 (measured: a gain there, a loss with 8 warps and K = 512)
+    auto prefetch_h = [&](int cc) {  // lane 0 only
+      int row, col;
+      if (EW == 4 && block_at(cc, row, col)) tma_prefetch_2d(&tma_o, col, row);
+    };
     if constexpr (EPI == EPI_F32_ADD) {
       if (tma_out && lane == 0) {
         load_h(0);
         load_h(1);
+        for (int j = 2; j < 2 + CPT; j++) prefetch_h(j);
       }
     }
     // column constants (per-channel scale, bias) of the next block, one per lane, fetched a
@@ -466,7 +478,7 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI>::THREADS, 1)
       uint32_t bidx = 0xFFFFFFFFu;
 #pragma unroll 1
       for (int c = 0; c < CPT; c++, cc++) {
-        const int c0 = half * (BN / 2) + 32 * c;
+        const int c0 = half * HW + 32 * c;
         const int col = n0 + c0;
         uint32_t r[32];
         tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * BN + c0), r);
@@ -506,6 +518,7 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI>::THREADS, 1)
           if (tma_out && lane == 0) {
             bulk_wait_read<1>();  // buffer (cc+2) % 3 was last read by the store of block cc-1
             load_h(cc + 2);
+            prefetch_h(cc + 2 + CPT);
           }
         }
       }
