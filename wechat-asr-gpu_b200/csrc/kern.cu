@@ -642,16 +642,19 @@ __global__ void __launch_bounds__(LR_THREADS, 2) ln_rows_k(const float* __restri
     gg[k] = __ldg(reinterpret_cast<const float4*>(g) + lane + 32 * k);
     bb[k] = __ldg(reinterpret_cast<const float4*>(b) + lane + 32 * k);
   }
-  // two rows per step (rr and rr + 8; the second is a repeat of the first past the end), so
-  // the two reductions and quantisations overlap
-  for (int rr = warp; rr < nr; rr += 2 * (LR_THREADS / 32)) {
-    const int r2 = rr + LR_THREADS / 32 < nr ? rr + LR_THREADS / 32 : rr;
-    const int row[2] = {rr, r2};
-    float4 y[2][4];
-    float mx[2] = {0.0f, 0.0f};
+  // four rows per step (rr + 8a; rows past the end repeat rr, writing the same values), so
+  // the four reductions and quantisations overlap
+  constexpr int NB = 4, NW = LR_THREADS / 32;
+  for (int rr = warp; rr < nr; rr += NB * NW) {
+    int row[NB];
 #pragma unroll
-    for (int a = 0; a < 2; a++) {
+    for (int a = 0; a < NB; a++) row[a] = rr + a * NW < nr ? rr + a * NW : rr;
+    float4 y[NB][4];
+    float mx[NB];
+#pragma unroll
+    for (int a = 0; a < NB; a++) {
       const float mu_r = mean[row[a]], iv = rinv[row[a]];
+      mx[a] = 0.0f;
 #pragma unroll
       for (int k = 0; k < 4; k++) {
         const float4 v = S[lr_slot(row[a], lane + 32 * k)];
@@ -663,12 +666,11 @@ __global__ void __launch_bounds__(LR_THREADS, 2) ln_rows_k(const float* __restri
       }
     }
 #pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      mx[0] = fmaxf(mx[0], __shfl_xor_sync(0xffffffffu, mx[0], o));
-      mx[1] = fmaxf(mx[1], __shfl_xor_sync(0xffffffffu, mx[1], o));
-    }
+    for (int o = 16; o; o >>= 1)
 #pragma unroll
-    for (int a = 0; a < 2; a++) {
+      for (int a = 0; a < NB; a++) mx[a] = fmaxf(mx[a], __shfl_xor_sync(0xffffffffu, mx[a], o));
+#pragma unroll
+    for (int a = 0; a < NB; a++) {
       const float sc = quant_scale(mx[a]), inv = quant_inv(sc);
       char4* q = reinterpret_cast<char4*>(xq + static_cast<int64_t>(r0 + row[a]) * D);
 #pragma unroll
