@@ -371,7 +371,8 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--max-rows", type=int, default=16384)
+    ap.add_argument("--max-rows", type=int, default=0,
+                    help="rows per engine chunk (0 = this rank's whole shard in one chunk)")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -408,12 +409,15 @@ def main():
     feats, sils, my_audio, fbank_s, pcms = make_workload(pkg, shard, lengths)
     total_audio = float(sum(lengths))
     blob, plan = pkg.synth.make_model(seed=1, n_layers=40)
+    t = np.array([f.shape[0] for f in feats], np.int32)
+    t1 = [(x - 5) // 5 + 1 if x >= 5 else 0 for x in t]
+    # one chunk holds the whole shard by default (the activations of 72K rows take ~5 GB): every
+    # launch then has its full width and no short last chunk
+    args.max_rows = args.max_rows if args.max_rows > 0 else max(int(sum(t1)), 1024)
     eng = pkg.Engine(blob, plan, device=local, max_rows=args.max_rows)
     stream = torch.cuda.Stream(device=local)
     eng.set_stream(stream.cuda_stream)
 
-    t = np.array([f.shape[0] for f in feats], np.int32)
-    t1 = [(x - 5) // 5 + 1 if x >= 5 else 0 for x in t]
     cat = np.ascontiguousarray(np.concatenate(feats, 0), np.float32)
     feats_dev = torch.from_numpy(cat).to(f"cuda:{local}")
     ids_dev = torch.empty(max(sum(t1), 1), dtype=torch.int32, device=f"cuda:{local}")
