@@ -50,7 +50,7 @@ void wo_quant(const float* x, int64_t t, int k, int8_t* q, float* s) {
       float v = roundf(r[j] * inv);
       if (v > 127.0f) v = 127.0f;
       if (v < -127.0f) v = -127.0f;
-      qr[j] = (int8_t)v;
+      qr[j] = v != v ? 0 : (int8_t)v;  /* Rust: NaN.clamp(..) is NaN, and NaN as i8 is 0 */
     }
     s[i] = sc;
   }

@@ -9,6 +9,25 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
+def test_wk_quant_nan_inf_like_rust(gpu_lib, dev, orc):
+    """NaN -> 0 and +-inf -> +-127 as Rust's clamp + `as i8` give them (src/kernels.rs:20), on the
+    vectorised 512-wide path and the general path."""
+    L = gpu_lib
+    for k in (512, 1000):
+        x = np.random.default_rng(k).standard_normal((3, k)).astype(np.float32)
+        x[0, 0], x[0, 7] = np.nan, np.nan                     # NaN in a finite row
+        x[1, 3], x[1, 5], x[1, 9] = np.inf, -np.inf, np.nan   # an infinite row max: inv = 0
+        x[2, 1] = np.nan
+        px, pq, ps = dev.put(x), dev.empty(3 * k), dev.empty(12)
+        L.wk_quant(None, px, 3, k, pq, ps)
+        assert L.wk_last_error() == 0
+        q, s = orc.quant(x)
+        got = dev.get(pq, (3, k), np.int8)
+        np.testing.assert_array_equal(got, q)
+        assert got[0, 0] == 0 and got[0, 7] == 0 and not got[1].any()
+        np.testing.assert_array_equal(dev.get(ps, (3,), np.float32), s)
+
+
 @pytest.mark.parametrize("t,k", [(1, 512), (390, 512), (77, 2048), (129, 3840), (5, 10), (3, 1000)])
 def test_wk_quant(gpu_lib, dev, orc, t, k):
     L = gpu_lib

@@ -79,6 +79,19 @@ def test_quant_ties_round_half_away(orc):
     assert list(q[0]) == [127, 1, -1, 2, -2, 3, -3, 0]
 
 
+def test_quant_nan_and_inf_like_rust(orc):
+    """Rust's `(v * inv).round().clamp(-127.0, 127.0) as i8` (src/kernels.rs:20): NaN stays NaN
+    through clamp and `as i8` makes it 0; +-inf clamps to +-127.  The row max ignores NaN
+    (f32::max), and an infinite max makes inv = 0, so every value of that row becomes
+    NaN or 0 -> 0."""
+    x = np.array([[np.nan, 1.0, -2.0, 0.5], [np.inf, 3.0, -np.inf, np.nan], [np.nan, np.nan, 0.0, 0.0]],
+                 np.float32)
+    q, s = orc.quant(x)
+    assert q[0].tolist() == [0, 64, -127, 32] and s[0] == np.float32(2.0) / np.float32(127.0)
+    assert q[1].tolist() == [0, 0, 0, 0] and np.isinf(s[1])
+    assert q[2].tolist() == [0, 0, 0, 0] and s[2] == 1.0
+
+
 @pytest.mark.parametrize("shape", [(400, 512, 2048), (37, 2048, 512), (64, 3840, 512), (3, 512, 10502)])
 def test_qgemm_int32_exact_and_epilogue(orc, shape):
     """Config-0 style GEMM: AVX2 dot2x4 path == scalar dot1 == int64 numpy; epilogue equals

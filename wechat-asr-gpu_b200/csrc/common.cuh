@@ -199,10 +199,12 @@ __host__ __device__ constexpr uint32_t idesc_i8(int n) {
 // inv = 1/s, q = round_half_away(v * inv) clamped to [-127, 127].
 __device__ __forceinline__ float quant_scale(float m) { return m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f; }
 __device__ __forceinline__ float quant_inv(float s) { return __fdiv_rn(1.0f, s); }
+// The clamp and cast follow Rust's `.clamp(-127.0, 127.0) as i8`: NaN gives 0 and +-inf +-127.
+// The float -> int conversion (cvt.rzi: saturating, NaN to 0) comes first and the clamp is
+// then an integer one; for the integral values round() gives it equals the float clamp.
 __device__ __forceinline__ int8_t quant_one(float v, float inv) {
-  float q = roundf(__fmul_rn(v, inv));
-  q = fminf(127.0f, fmaxf(-127.0f, q));
-  return static_cast<int8_t>(q);
+  const int q = __float2int_rz(roundf(__fmul_rn(v, inv)));
+  return static_cast<int8_t>(min(127, max(-127, q)));
 }
 // ---------------------------------------------------------------- libm restatements
 // The reference CPU path calls the platform libm: Rust's f32::tanh / f32::exp are glibc's
