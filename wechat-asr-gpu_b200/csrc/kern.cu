@@ -858,11 +858,11 @@ __global__ void keys_to_ids_k(const unsigned long long* __restrict__ keys, int m
 // p_j * v_j[d] from 0 (src/model.rs:714-738).  Every element keeps the reference's exact
 // sequence of rounded multiplies and adds.
 //
-// Register tiles.  Scores: a thread pair (hl = 0, 1) owns 4 query rows x 4 keys (kg + 8u,
-// u < 4) of a 32-key chunk; thread hl keeps dotf lanes 4hl .. 4hl+3 of each score as 2 float2
-// (dims 8c+4hl .. 8c+4hl+3), so each 16-byte load of q or k feeds 4 scores (2 bytes of shared
-// memory per exact MAC).  The lane fold keeps the reference order: hl = 0 folds lanes 0-3,
-// hands the partial sum to its partner by one shuffle, and hl = 1 adds lanes 4-7.  PV: a thread owns row
+// Register tiles.  Scores: a thread owns one row pair x 4 keys (kg + 8u, u < 4) of a 32-key
+// chunk with all 8 dotf lanes of each score as 4 float2 (lane l holds dims 8c + l), so the lane
+// fold is 7 adds in one thread, in the reference order.  A lane's first step starts from the
+// product itself rather than 0 + product: the two differ at most in the sign of a zero, which
+// no later step can see (a zero score enters the softmax only through s - max and exp).  PV: a thread owns row
 // pairs (2p, 2p+1) for p = pa, pa+1 x head dims d0..d0+3; the accumulators pair (row 2p, dim d)
 // with (row 2p+1, dim d^1).  K and V chunks stream through two shared buffers by cp.async,
 // one barrier per chunk.  Shared layout: exp table | Q [64][72] + K [2][32][72] (scores) /
@@ -871,7 +871,7 @@ __global__ void keys_to_ids_k(const unsigned long long* __restrict__ keys, int m
 // over the 8 thread pairs of a warp that share a row); the exp and divide passes run flat over
 // (row pair, key) with every thread on independent elements; z is one thread per row.
 constexpr int ATT_KC = 32;   // keys per chunk
-constexpr int ATT_RS = 72;   // Q / K row stride in floats: 16-byte rows, 8 keys of a quarter-warp on distinct banks
+constexpr int ATT_RS = 68;   // Q / K row stride in floats: the 8 keys (or 4 row pairs) of a 16-byte load on distinct banks
 constexpr int ATT_A = (ATT_QT + 2 * ATT_KC) * ATT_RS;  // floats of the Q/K (and V) region
 
 __host__ __device__ inline int att_pair_stride(int max_t1) { return ((max_t1 + 15) / 16) * 16 + 1; }
@@ -902,51 +902,55 @@ __device__ __forceinline__ void att_copy_rows(float* dst, int ds, const float* _
   cp_async_commit();
 }
 
-// Scores of one 32-key chunk for the 4 query rows at Qr (row stride ATT_RS, already offset
-// by this thread's lanes 4hl) and keys kg + 8u, u < NU (groups past the end of a segment are
-// skipped whole), K likewise offset.  hl = 1 lanes store score pairs of rows (0, 1) and (2, 3)
-// at out0[j] / out1[j] and keep the running row maxima in mx (order-free).
+// Scores of one 32-key chunk for the query rows Qr and Qr + ATT_RS (row stride ATT_RS) and keys
+// kg + 8u, u < NU (groups past the end of a segment are skipped whole) at Kr + 8u ATT_RS.  The
+// score pairs of the two rows go to out[j]; mx keeps the running row maxima (order-free).
 template <int NU>
-__device__ __forceinline__ void att_score_chunk(const float* Qr, const float* Kr, int kg, int hl, int nj,
-                                                float2* out0, float2* out1, float (&mx)[4]) {
-  float2 acc[4][NU][2];
-#pragma unroll
-  for (int m = 0; m < 4; m++)
-#pragma unroll
-    for (int u = 0; u < NU; u++) acc[m][u][0] = acc[m][u][1] = make_float2(0.0f, 0.0f);
+__device__ __forceinline__ void att_score_chunk(const float* Qr, const float* Kr, int kg, int nj, float2* out,
+                                                float (&mx)[2]) {
+  float2 acc[2][NU][4];
 #pragma unroll
   for (int c = 0; c < 8; c++) {
-    float4 qv[4];
+    float4 qv[2][2];
 #pragma unroll
-    for (int m = 0; m < 4; m++) qv[m] = *reinterpret_cast<const float4*>(Qr + m * ATT_RS + 8 * c);
+    for (int r = 0; r < 2; r++) {
+      qv[r][0] = *reinterpret_cast<const float4*>(Qr + r * ATT_RS + 8 * c);
+      qv[r][1] = *reinterpret_cast<const float4*>(Qr + r * ATT_RS + 8 * c + 4);
+    }
 #pragma unroll
     for (int u = 0; u < NU; u++) {
-      const float4 kv = *reinterpret_cast<const float4*>(Kr + 8 * u * ATT_RS + 8 * c);
+      const float4 k0 = *reinterpret_cast<const float4*>(Kr + 8 * u * ATT_RS + 8 * c);
+      const float4 k1 = *reinterpret_cast<const float4*>(Kr + 8 * u * ATT_RS + 8 * c + 4);
 #pragma unroll
-      for (int m = 0; m < 4; m++) {
-        acc[m][u][0] = add2_rn(acc[m][u][0], mulp(lo2(qv[m]), lo2(kv)));
-        acc[m][u][1] = add2_rn(acc[m][u][1], mulp(hi2(qv[m]), hi2(kv)));
+      for (int r = 0; r < 2; r++) {
+        const float2 p0 = mulp(lo2(qv[r][0]), lo2(k0)), p1 = mulp(hi2(qv[r][0]), hi2(k0));
+        const float2 p2 = mulp(lo2(qv[r][1]), lo2(k1)), p3 = mulp(hi2(qv[r][1]), hi2(k1));
+        if (c == 0) {
+          acc[r][u][0] = p0, acc[r][u][1] = p1, acc[r][u][2] = p2, acc[r][u][3] = p3;
+        } else {
+          acc[r][u][0] = add2_rn(acc[r][u][0], p0);
+          acc[r][u][1] = add2_rn(acc[r][u][1], p1);
+          acc[r][u][2] = add2_rn(acc[r][u][2], p2);
+          acc[r][u][3] = add2_rn(acc[r][u][3], p3);
+        }
       }
     }
   }
 #pragma unroll
   for (int u = 0; u < NU; u++) {
-    float sc[4];
+    float sc[2];
 #pragma unroll
-    for (int m = 0; m < 4; m++) {
-      // hl = 0: ((l0 + l1) + l2) + l3, passed to hl = 1, which adds l4, l5, l6, l7 in turn
-      const float pl = __fadd_rn(__fadd_rn(__fadd_rn(acc[m][u][0].x, acc[m][u][0].y), acc[m][u][1].x), acc[m][u][1].y);
-      const float lo = __shfl_xor_sync(0xffffffffu, pl, 1);
-      const float x =
-          __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(lo, acc[m][u][0].x), acc[m][u][0].y), acc[m][u][1].x), acc[m][u][1].y);
-      sc[m] = __fmul_rn(x, 0.125f);
+    for (int r = 0; r < 2; r++) {
+      float x = __fadd_rn(acc[r][u][0].x, acc[r][u][0].y);
+#pragma unroll
+      for (int l = 1; l < 4; l++) x = __fadd_rn(__fadd_rn(x, acc[r][u][l].x), acc[r][u][l].y);
+      sc[r] = __fmul_rn(x, 0.125f);
     }
     const int j = kg + 8 * u;
-    if (hl && j < nj) {
-      out0[j] = make_float2(sc[0], sc[1]);
-      out1[j] = make_float2(sc[2], sc[3]);
-#pragma unroll
-      for (int m = 0; m < 4; m++) mx[m] = fmaxf(mx[m], sc[m]);
+    if (j < nj) {
+      out[j] = make_float2(sc[0], sc[1]);
+      mx[0] = fmaxf(mx[0], sc[0]);
+      mx[1] = fmaxf(mx[1], sc[1]);
     }
   }
 }
@@ -1030,8 +1034,8 @@ __global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, co
   extern __shared__ __align__(16) float sm[];
   const int sp = att_pair_stride(max_t1);
   unsigned long long* tab = reinterpret_cast<unsigned long long*>(sm);
-  float* Q = sm + 64;                     // [64][72]
-  float* Kb = Q + ATT_QT * ATT_RS;        // [2][32][72]
+  float* Q = sm + 64;                     // [64][68]
+  float* Kb = Q + ATT_QT * ATT_RS;        // [2][32][68]
   float* Vb = Q;                          // [2][32][64] (PV phase)
   float2* S2 = reinterpret_cast<float2*>(Q + ATT_A);  // [32][sp]
   float* ZY = reinterpret_cast<float*>(S2 + (ATT_QT / 2) * sp);  // [32][4]: z and 1/z of each row pair
@@ -1062,13 +1066,12 @@ __global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, co
   att_copy_rows(Q, ATT_RS, q, ld, rb + i0, ni, h, tid, a16);
   att_copy_rows(Kb, ATT_RS, k, ld, rb, min(ATT_KC, t), h, tid, a16);
   {
-    // warp w: rows 8w .. 8w+7; lane = hl + 2 kg + 16 rg: rows 8w + 4rg + m (m < 4), keys kg + 8u
-    const int hl = lane & 1, kg = (lane >> 1) & 7, rg = lane >> 4, row0 = 8 * warp + 4 * rg;
+    // warp w: rows 8w .. 8w+7; lane = kg + 8 rg: rows 8w + 2rg and 8w + 2rg + 1, keys kg + 8u
+    const int kg = lane & 7, rg = lane >> 3, row0 = 8 * warp + 2 * rg;
     const bool live = 8 * warp < ni;  // warp-uniform
-    const float* Qr = Q + row0 * ATT_RS + 4 * hl;
-    float2* out0 = S2 + (row0 >> 1) * sp;
-    float2* out1 = out0 + sp;
-    float mx[4] = {-3.40282347e+38f, -3.40282347e+38f, -3.40282347e+38f, -3.40282347e+38f};
+    const float* Qr = Q + row0 * ATT_RS;
+    float2* outp = S2 + (row0 >> 1) * sp;
+    float mx[2] = {-3.40282347e+38f, -3.40282347e+38f};
     for (int ch = 0; ch < nchunks; ch++) {
       const int j0 = ch * ATT_KC, nj = min(ATT_KC, t - j0);
       cp_async_wait<0>();
@@ -1076,27 +1079,25 @@ __global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, co
       if (ch + 1 < nchunks)
         att_copy_rows(Kb + ((ch + 1) & 1) * ATT_KC * ATT_RS, ATT_RS, k, ld, rb + j0 + ATT_KC,
                       min(ATT_KC, t - j0 - ATT_KC), h, tid, a16);
-      const float* Kr = Kb + (ch & 1) * ATT_KC * ATT_RS + kg * ATT_RS + 4 * hl;
+      const float* Kr = Kb + (ch & 1) * ATT_KC * ATT_RS + kg * ATT_RS;
       if (live) {
         // 8-key groups holding keys of the segment: all four but in a segment's last chunk
         switch (min(4, (nj + 7) >> 3)) {
-          case 4: att_score_chunk<4>(Qr, Kr, kg, hl, nj, out0 + j0, out1 + j0, mx); break;
-          case 3: att_score_chunk<3>(Qr, Kr, kg, hl, nj, out0 + j0, out1 + j0, mx); break;
-          case 2: att_score_chunk<2>(Qr, Kr, kg, hl, nj, out0 + j0, out1 + j0, mx); break;
-          default: att_score_chunk<1>(Qr, Kr, kg, hl, nj, out0 + j0, out1 + j0, mx); break;
+          case 4: att_score_chunk<4>(Qr, Kr, kg, nj, outp + j0, mx); break;
+          case 3: att_score_chunk<3>(Qr, Kr, kg, nj, outp + j0, mx); break;
+          case 2: att_score_chunk<2>(Qr, Kr, kg, nj, outp + j0, mx); break;
+          default: att_score_chunk<1>(Qr, Kr, kg, nj, outp + j0, mx); break;
         }
       }
     }
-    // the 8 hl = 1 lanes of a row group hold the same rows (lane bits 1-3 differ)
+    // the 8 lanes of a row pair (lane bits 0-2) hold the same rows
 #pragma unroll
-    for (int m = 0; m < 4; m++) {
+    for (int m = 0; m < 2; m++) {
+      mx[m] = fmaxf(mx[m], __shfl_xor_sync(0xffffffffu, mx[m], 1));
       mx[m] = fmaxf(mx[m], __shfl_xor_sync(0xffffffffu, mx[m], 2));
       mx[m] = fmaxf(mx[m], __shfl_xor_sync(0xffffffffu, mx[m], 4));
-      mx[m] = fmaxf(mx[m], __shfl_xor_sync(0xffffffffu, mx[m], 8));
     }
-    if (live && (lane & 15) == 1)
-#pragma unroll
-      for (int m = 0; m < 4; m++) Mx[row0 + m] = mx[m];
+    if (live && kg == 0) Mx[row0] = mx[0], Mx[row0 + 1] = mx[1];
   }
   __syncthreads();  // scores and row maxima complete; the Q/K region is free
   // the first V chunk streams in while the softmax runs
