@@ -134,7 +134,9 @@ def test_wk_front_bit_exact(gpu_lib, dev, orc, pkg, t):
     np.testing.assert_array_equal(got, orc.frontend(x, c1, c2, c3))
 
 
-@pytest.mark.parametrize("t", [1, 5, 31, 32, 33, 150, 390, 512])
+# t covers every key-tail width of a 32-key chunk (1, 2, 3 and 4 groups of 8: t mod 32 = 1, 13,
+# 22, 31) and 1-, 2-, 3-, 7- and 8-tile segments (65 and 100: tiles of 33 and 50 rows)
+@pytest.mark.parametrize("t", [1, 5, 13, 31, 32, 33, 45, 65, 100, 150, 390, 512])
 def test_wk_attention(gpu_lib, dev, orc, t):
     L = gpu_lib
     rng = np.random.default_rng(t + 100)
