@@ -406,8 +406,9 @@ __device__ __forceinline__ float gelu_ref(float x) {
   return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf_ref(u)));
 }
 // ---- the same tanhf / GELU for two independent elements: every multiply is one packed
-// multiply of the pair (mul.rn.f32x2), every add, subtract and divide stays a scalar rounded
-// operation per element (so no multiply can be contracted into an add), and the integer /
+// multiply of the pair (mul.rn.f32x2); every add and divide, and every subtract with a product
+// as an operand, stays a scalar rounded operation per element (so no multiply can be contracted
+// into an add); a subtract of two scalar results is one packed sub.rn.f32x2; the integer /
 // select logic runs per element.  Identical results to tanhf_ref / gelu_ref element by element.
 __device__ __forceinline__ float2 pmul2(float2 a, float2 b) {
   unsigned long long r;
@@ -420,6 +421,14 @@ __device__ __forceinline__ float2 f2c(float v) { return make_float2(v, v); }
 __device__ __forceinline__ float2 sadd2(float2 a, float2 b) { return make_float2(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y)); }
 __device__ __forceinline__ float2 ssub2(float2 a, float2 b) { return make_float2(__fsub_rn(a.x, b.x), __fsub_rn(a.y, b.y)); }
 __device__ __forceinline__ float2 sdiv2(float2 a, float2 b) { return make_float2(div_nr(a.x, b.x), div_nr(a.y, b.y)); }
+// packed subtract, used only where neither operand comes straight from a packed multiply
+__device__ __forceinline__ float2 psub2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"((static_cast<unsigned long long>(__float_as_uint(a.y)) << 32) |
+                                                 __float_as_uint(a.x)),
+      "l"((static_cast<unsigned long long>(__float_as_uint(b.y)) << 32) | __float_as_uint(b.x)));
+  return make_float2(__uint_as_float(static_cast<uint32_t>(r)), __uint_as_float(static_cast<uint32_t>(r >> 32)));
+}
 
 // per-element part of tanhf_ref after the shared reductions: reconstruction, tanh, specials
 __device__ __forceinline__ float tanh_tail(float x, int k, bool ge1, uint32_t hy, float y, float xr, float e2, float res0,
@@ -461,7 +470,7 @@ __device__ __forceinline__ float2 tanhf_ref2(float2 x) {
   const float2 tk = make_float2(static_cast<float>(ka), static_cast<float>(kb));
   const float2 hi = ssub2(y, pmul2(tk, f2c(ln2_hi))), lo = pmul2(tk, f2c(ln2_lo));
   const float2 xr = ssub2(hi, lo);
-  const float2 c = ssub2(ssub2(hi, xr), lo);
+  const float2 c = ssub2(psub2(hi, xr), lo);
   const float2 hfx = pmul2(f2c(0.5f), xr);
   const float2 hxs = pmul2(xr, hfx);
   float2 r1 = pmul2(hxs, f2c(Q5));
@@ -470,10 +479,10 @@ __device__ __forceinline__ float2 tanhf_ref2(float2 x) {
   r1 = pmul2(hxs, sadd2(f2c(Q2), r1));
   r1 = sadd2(f2c(1.0f), pmul2(hxs, sadd2(f2c(Q1), r1)));
   const float2 t = ssub2(f2c(3.0f), pmul2(r1, hfx));
-  const float2 e = pmul2(hxs, sdiv2(ssub2(r1, t), ssub2(f2c(6.0f), pmul2(xr, t))));
-  const float2 res0 = ssub2(xr, ssub2(pmul2(xr, e), hxs));
+  const float2 e = pmul2(hxs, sdiv2(psub2(r1, t), ssub2(f2c(6.0f), pmul2(xr, t))));
+  const float2 res0 = psub2(xr, ssub2(pmul2(xr, e), hxs));
   const float2 e2 = ssub2(ssub2(pmul2(xr, ssub2(e, c)), c), hxs);
-  const float2 resm1 = ssub2(pmul2(f2c(0.5f), ssub2(xr, e2)), f2c(0.5f));
+  const float2 resm1 = ssub2(pmul2(f2c(0.5f), psub2(xr, e2)), f2c(0.5f));
   return make_float2(tanh_tail(x.x, ka, ga, hya, y.x, xr.x, e2.x, res0.x, resm1.x),
                      tanh_tail(x.y, kb, gb, hyb, y.y, xr.y, e2.y, res0.y, resm1.y));
 }
