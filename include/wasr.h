@@ -132,6 +132,19 @@ int wasr_transcribe(WasrModel* m, const float* feats, const int64_t* n_frames, c
                     int n_utt, int prev, int blk, int post, uint32_t* ids, int64_t* ids_off,
                     int64_t ids_cap);
 
+/* wasr_transcribe with the features already on the GPU, e.g. wasr_fbank_device's output (no
+ * counterpart in the reference, whose fbank and window assembly run on the host,
+ * src/stream.rs:128-147).  feats [sum n_frames][40] and sil [n_utt][40] are device pointers on
+ * the model's device; n_frames, ids and ids_off are host arrays.  Each round's windows (frames
+ * plus the silence pad) are gathered on the device into a staging buffer the model keeps and
+ * grows, so the features never cross to the host; a round of whole utterances laid out back to
+ * back is read straight from feats.  Work already queued that writes feats or sil must be
+ * complete or ordered before the call (it runs on the model's stream).  Same ids, ids_off and
+ * return codes as wasr_transcribe on the same features. */
+int wasr_transcribe_device(WasrModel* m, const float* feats, const int64_t* n_frames,
+                           const float* sil, int n_utt, int prev, int blk, int post, uint32_t* ids,
+                           int64_t* ids_off, int64_t ids_cap);
+
 /* Host fbank (src/fbank.rs:79-161): int16 PCM -> CMS-normalised [frames][40] fp32 and the
  * utterance's silence frame.  Returns the frame count (or, if feats is NULL, the count only). */
 int64_t wasr_fbank(const int16_t* pcm, int64_t n, float* feats, int64_t cap, float* sil);

@@ -102,6 +102,7 @@ SIGNATURES = {
     "wasr_model_kernel_launches": (I64, [P]),
     "wasr_forward": (I, [P, P, P, I, P, P, I]),
     "wasr_transcribe": (I, [P, P, P, P, I, I, I, I, P, P, I64]),
+    "wasr_transcribe_device": (I, [P, P, P, P, I, I, I, I, P, P, I64]),
     "wasr_fbank": (I64, [P, I64, P, I64, P]),
     "wasr_fbank_device": (I, [P, P, P, I, I64, P, P, P, P]),
     "wasr_fbank_stream_create": (P, []),

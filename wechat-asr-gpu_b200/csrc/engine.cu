@@ -92,6 +92,11 @@ struct WasrModel {
   // pinned host staging
   float* h_feats = nullptr;
   size_t h_feats_cap = 0;
+  // device staging of wasr_transcribe_device: one round's gathered windows and their table
+  float* d_win = nullptr;
+  size_t d_win_cap = 0;
+  long long* d_wtab = nullptr;
+  size_t d_wtab_cap = 0;
   uint32_t* h_ids = nullptr;
   size_t h_ids_cap = 0;
   int* h_seg = nullptr;
@@ -116,6 +121,25 @@ bool hgrow(T** p, size_t* cap, size_t n) {
   *cap = n;
   return true;
 }
+
+// device buffer of at least n elements (contents not kept); callers grow it only while the
+// model's stream is idle
+template <typename T>
+bool dgrow(T** p, size_t* cap, size_t n) {
+  if (n <= *cap) return true;
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  *cap = 0;
+  if (cudaMalloc(reinterpret_cast<void**>(p), n * sizeof(T)) != cudaSuccess) {
+    *p = nullptr;
+    return false;
+  }
+  *cap = n;
+  return true;
+}
+
+// engine-internal forward flag: feats on the device, ids / logits on the host
+constexpr int F_FEATS_DEV = 1 << 16;
 
 struct DevGuard {
   int prev = -1;
@@ -429,7 +453,7 @@ int forward_impl(WasrModel* m, const float* feats, const int32_t* t, int n, uint
     const size_t fbytes = static_cast<size_t>(c.frames) * DIM * sizeof(float);
     if (fbytes) {
       const float* src = feats + f_off * DIM;
-      if (on_dev) {
+      if (on_dev || (flags & F_FEATS_DEV)) {
         if (cudaMemcpyAsync(m->feats, src, fbytes, cudaMemcpyDeviceToDevice, st) != cudaSuccess) return -4;
       } else {
         if (cudaMemcpyAsync(m->feats, src, fbytes, cudaMemcpyHostToDevice, st) != cudaSuccess) return -4;
@@ -546,7 +570,7 @@ void wasr_model_destroy(WasrModel* m) {
   free_graphs(m);
   free_recs(&m->eager_recs);
   void* dptrs[] = {m->w, m->feats, m->y1, m->y2, m->y3, m->xq, m->xs, m->h, m->qkv, m->att, m->f, m->rowmax,
-                   m->keys, m->ids, m->seg, m->c2pre, m->c3pre};
+                   m->keys, m->ids, m->seg, m->c2pre, m->c3pre, m->d_win, m->d_wtab};
   for (void* p : dptrs)
     if (p) cudaFree(p);
   for (int l = 0; l < WASR_MAX_LAYERS; l++) {
@@ -639,7 +663,7 @@ int wasr_forward(WasrModel* m, const float* feats, const int32_t* t, int n_win, 
   if (!m) return -1;
   std::lock_guard<std::mutex> lk(m->mu);
   DevGuard dg(m->dev);
-  return forward_impl(m, feats, t, n_win, ids, logits, flags);
+  return forward_impl(m, feats, t, n_win, ids, logits, flags & (WASR_F_DEVICE | WASR_F_NOSYNC));
 }
 
 int64_t wasr_fbank(const int16_t* pcm, int64_t n, float* feats, int64_t cap, float* sil) {
@@ -746,11 +770,30 @@ int64_t wasr_ctc_collapse(const uint32_t* ids, int64_t n, uint32_t* out) {
   return k;
 }
 
+}  // extern "C"
+
+namespace {
+
+// One block per window of a device transcription round (tab: 5 entries per window): frames
+// [src, src + n) of the features, then `pad` copies of utterance u's silence frame, written to
+// rows dst, dst + 1, ... of out.
+__global__ void gather_windows_k(const float* __restrict__ feats, const float* __restrict__ sil,
+                                 const long long* __restrict__ tab, float* __restrict__ out) {
+  const long long* e = tab + 5 * static_cast<long long>(blockIdx.x);
+  const long long src = e[0], n = e[1], pad = e[2], u = e[3], dst = e[4];
+  const long long total = (n + pad) * DIM;
+  for (long long i = threadIdx.x; i < total; i += blockDim.x) {
+    const long long r = i / DIM, c = i - r * DIM;
+    out[(dst + r) * DIM + c] = r < n ? feats[(src + r) * DIM + c] : sil[u * DIM + c];
+  }
+}
+
 // Batch transcription (src/stream.rs:58-70 push, 128-134 decode, 136-147 commit, 159-168
 // finish).  Every utterance keeps its own commit position; each round stacks one window per
-// unfinished utterance into a single wasr_forward.
-int wasr_transcribe(WasrModel* m, const float* feats, const int64_t* n_frames, const float* sil, int n_utt, int prev,
-                    int blk, int post, uint32_t* ids, int64_t* ids_off, int64_t ids_cap) {
+// unfinished utterance into a single forward.  dev: feats and sil are device pointers, and a
+// round's windows are gathered on the device instead of in pinned host staging.
+int transcribe_impl(WasrModel* m, const float* feats, const int64_t* n_frames, const float* sil, int n_utt, int prev,
+                    int blk, int post, uint32_t* ids, int64_t* ids_off, int64_t ids_cap, bool dev) {
   if (!m || !n_frames || !sil || !ids || !ids_off || n_utt < 0 || (!feats && n_utt > 0)) return -1;
   if (prev < 0 || blk <= 0 || post < 0) return -1;
   std::lock_guard<std::mutex> lk(m->mu);
@@ -800,7 +843,30 @@ int wasr_transcribe(WasrModel* m, const float* feats, const int64_t* n_frames, c
       contiguous = wins[i].kind == 0 && (i == 0 ? start[wins[i].u] == 0 : start[wins[i].u] == start[wins[i - 1].u] +
                                                                               (wins[i - 1].end - wins[i - 1].a));
     const float* src = feats;
-    if (!contiguous) {
+    std::vector<long long> wtab;  // device rounds: src, n, pad, u, dst per window
+    if (!contiguous && dev) {
+      wtab.resize(5 * wins.size());
+      int64_t d = 0;
+      for (size_t i = 0; i < wins.size(); i++) {
+        const Win& w = wins[i];
+        long long* e = wtab.data() + 5 * i;
+        e[0] = start[w.u] + w.a;
+        e[1] = w.end - w.a;
+        e[2] = w.pad;
+        e[3] = w.u;
+        e[4] = d;
+        d += tv[i];
+      }
+      if (!dgrow(&m->d_win, &m->d_win_cap, static_cast<size_t>(std::max<int64_t>(total, 1)) * DIM) ||
+          !dgrow(&m->d_wtab, &m->d_wtab_cap, wtab.size()))
+        return -5;
+      if (cudaMemcpyAsync(m->d_wtab, wtab.data(), wtab.size() * sizeof(long long), cudaMemcpyHostToDevice,
+                          m->stream) != cudaSuccess)
+        return -4;
+      gather_windows_k<<<static_cast<unsigned>(wins.size()), 256, 0, m->stream>>>(feats, sil, m->d_wtab, m->d_win);
+      if (cudaPeekAtLastError() != cudaSuccess) return -4;
+      src = m->d_win;
+    } else if (!contiguous) {
       if (!hgrow(&m->h_feats, &m->h_feats_cap, static_cast<size_t>(total) * DIM)) return -5;
       float* d = m->h_feats;
       for (const Win& w : wins) {
@@ -814,7 +880,7 @@ int wasr_transcribe(WasrModel* m, const float* feats, const int64_t* n_frames, c
     int64_t rows = 0;
     for (int32_t tt : tv) rows += t1_of(tt);
     if (!hgrow(&m->h_ids, &m->h_ids_cap, static_cast<size_t>(std::max<int64_t>(rows, 1)))) return -5;
-    TRY(forward_impl(m, src, tv.data(), static_cast<int>(wins.size()), m->h_ids, nullptr, 0));
+    TRY(forward_impl(m, src, tv.data(), static_cast<int>(wins.size()), m->h_ids, nullptr, dev ? F_FEATS_DEV : 0));
     int64_t r = 0;
     for (size_t i = 0; i < wins.size(); i++) {
       const Win& w = wins[i];
@@ -855,6 +921,20 @@ int wasr_transcribe(WasrModel* m, const float* feats, const int64_t* n_frames, c
     ids_off[u + 1] = k;
   }
   return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int wasr_transcribe(WasrModel* m, const float* feats, const int64_t* n_frames, const float* sil, int n_utt, int prev,
+                    int blk, int post, uint32_t* ids, int64_t* ids_off, int64_t ids_cap) {
+  return transcribe_impl(m, feats, n_frames, sil, n_utt, prev, blk, post, ids, ids_off, ids_cap, false);
+}
+
+int wasr_transcribe_device(WasrModel* m, const float* feats, const int64_t* n_frames, const float* sil, int n_utt,
+                           int prev, int blk, int post, uint32_t* ids, int64_t* ids_off, int64_t ids_cap) {
+  return transcribe_impl(m, feats, n_frames, sil, n_utt, prev, blk, post, ids, ids_off, ids_cap, true);
 }
 
 }  // extern "C"
