@@ -55,6 +55,11 @@ def test_transcribe_device_equals_host(pkg, gpu_lib, dev, small_model):
                                                 ids_d.ctypes.data, off_d.ctypes.data, cap) == 0
                 np.testing.assert_array_equal(off_d, off_h)
                 np.testing.assert_array_equal(ids_d[:off_h[-1]], ids_h[:off_h[-1]])
+        # the Engine wrappers: per-utterance ids, device features against host features
+        per_utt = [feats[foff[i]:foff[i + 1]] for i in range(n)]
+        want = eng.transcribe(per_utt, list(sil), prev=200, blk=400, post=100)
+        got = eng.transcribe_device(p_feats, nfr, p_sil, prev=200, blk=400, post=100)
+        assert len(got) == n and all(np.array_equal(a, b) for a, b in zip(got, want))
         # return codes shared with wasr_transcribe
         one = np.zeros(1, np.uint32)
         off = np.zeros(n + 1, np.int64)

@@ -131,6 +131,20 @@ class Engine:
             raise RuntimeError(f"wasr_transcribe rc={rc}")
         return [ids[off[i]:off[i + 1]].copy() for i in range(len(feats_list))]
 
+    def transcribe_device(self, feats_dev: int, n_frames, sil_dev: int, prev=200, blk=1600, post=100):
+        """transcribe() on device-resident features (e.g. wasr_fbank_device's output): feats_dev
+        holds the utterances' [frames][40] fp32 rows back to back, sil_dev their [n][40] silence
+        frames (device addresses on this engine's device).  Returns per-utterance raw ids."""
+        n = np.ascontiguousarray(n_frames, np.int64)
+        cap = int(n.sum() // 5 + 64 * n.size + 64)
+        ids = np.zeros(cap, np.uint32)
+        off = np.zeros(n.size + 1, np.int64)
+        rc = self.L.wasr_transcribe_device(self.m, feats_dev, ptr(n), sil_dev, n.size, prev, blk, post, ptr(ids),
+                                           ptr(off), cap)
+        if rc:
+            raise RuntimeError(f"wasr_transcribe_device rc={rc}")
+        return [ids[off[i]:off[i + 1]].copy() for i in range(n.size)]
+
     def error(self) -> int:
         return self.L.wasr_model_error(self.m)
 
