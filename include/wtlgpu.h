@@ -150,18 +150,31 @@ int wp_gemm2_pc(WpCtx* c, const int8_t* xq, const float* xs, int t, int k, size_
 int wp_gemm_i32(WpCtx* c, const int8_t* xq, int t, int k, size_t w_off, int n, void* stream,
                 int32_t* acc);
 
+/* ---- additive: failure-handling test hook ---------------------------------------- */
+/* No counterpart in the reference (its kernels have no bounded waits).  Every mbarrier wait in
+ * the tcgen05 GEMM gives up after a limit (2 s by default), records the cause in the context's
+ * error word and lets the kernel release its tensor memory and return; the next wp_sync then
+ * returns -21.  This entry point runs one int32 GEMM (as wp_gemm_i32) whose producer issues no
+ * loads, with every wait limited to wait_ns (1 ns .. 1 s), so that the waits run out with
+ * nothing in flight.  The output is not written meaningfully.  -2 for a wait_ns outside that
+ * range or k % 16 != 0 (the shapes without tensor-core waits). */
+int wp_gemm_i32_wait_probe(WpCtx* c, const int8_t* xq, int t, int k, size_t w_off, int n, void* stream,
+                           int32_t* acc, unsigned long long wait_ns);
+
 /* ---- additive: GEMM + per-row re-quantisation that allocates nothing ------------- */
 /* No counterpart in the reference.  Same result as wp_gemm_q, for callers that cannot
- * allocate device memory when they run it, such as code that runs while a CUDA graph is being
- * captured or a process whose device-memory budget is fixed up front.  wp_gemm_q may cudaMalloc
- * a larger staging buffer on demand.  This entry point stages through one fixed device array
+ * allocate device memory when they run it: a process whose framework has already handed the
+ * GPU's memory to its own caching allocator (a cudaMalloc outside that pool fails), or a
+ * latency-bound thread, such as the audio callback of a streaming recogniser, that must not
+ * block in cudaMalloc / cudaFree (both can synchronise the device).  wp_gemm_q may cudaMalloc a
+ * larger staging buffer on demand; this entry point stages through one fixed device array
  * inside the library instead, which every GPU that loads the library holds until the process
  * exits (4 MiB + 16 KiB).  Limits: t <= WP_NOALLOC_MAX_ROWS and t*n <= WP_NOALLOC_MAX_ELEMS;
- * larger calls return -22 and change nothing.  The first call on each device looks up the
- * array's device address (cudaGetSymbolAddress; -23 if that fails).  Make that first call
- * before any stream capture.  All calls share the one array, which keeps the last call's
- * values (the per-row maxima are cleared by every call).  Calls that overlap on the GPU (on
- * different streams) therefore race; serialise them. */
+ * larger calls return -22 and change nothing.  It runs on the context's device.  The first call
+ * on each device looks up the array's device address (cudaGetSymbolAddress; -23 if that
+ * fails); make that first call before any stream capture.  All calls share the one array,
+ * which keeps the last call's values (every call clears the per-row maxima it uses).  Calls
+ * that overlap on the GPU (on different streams or contexts) therefore race; serialise them. */
 #define WP_NOALLOC_MAX_ELEMS 1048576
 #define WP_NOALLOC_MAX_ROWS 4096
 int wp_gemm_q_noalloc(WpCtx* c, const int8_t* xq, const float* xs, int t, int k, size_t w_off, int n,

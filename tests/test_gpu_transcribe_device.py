@@ -2,8 +2,9 @@
 (src/stream.rs:58-168) on features that stay on the GPU (wasr_fbank_device's output), gathering
 each round's windows and silence pads on the device.
 
-Bar: the per-frame ids and their offsets equal wasr_transcribe's on the same features copied to
-the host, for a batch that mixes whole-utterance windows with block windows (26 s and 41 s
+Bar: the per-frame ids equal the oracle's transcription (oracle/, the C restatement of the
+reference's CPU path and schedule) of the same features, utterance by utterance; and ids and
+offsets equal wasr_transcribe's on the same features copied to the host, for a batch that mixes whole-utterance windows with block windows (26 s and 41 s
 utterances are longer than the 2000-frame whole-window limit, so their commit and finish
 windows carry the 50-frame silence pad), for a batch of whole utterances only (read straight
 from the caller's array), at two block sizes, and on a repeated call.
@@ -25,7 +26,7 @@ def small_model(pkg):
     return pkg.synth.make_model(seed=51, n_layers=2)
 
 
-def test_transcribe_device_equals_host(pkg, gpu_lib, dev, small_model):
+def test_transcribe_device_equals_host(pkg, orc, gpu_lib, dev, small_model):
     L = gpu_lib
     pcms = [pkg.synth.make_audio(900 + i, s) for i, s in enumerate(LENS)]
     n = len(pcms)
@@ -55,11 +56,20 @@ def test_transcribe_device_equals_host(pkg, gpu_lib, dev, small_model):
                                                 ids_d.ctypes.data, off_d.ctypes.data, cap) == 0
                 np.testing.assert_array_equal(off_d, off_h)
                 np.testing.assert_array_equal(ids_d[:off_h[-1]], ids_h[:off_h[-1]])
-        # the Engine wrappers: per-utterance ids, device features against host features
+        # the Engine wrappers: per-utterance ids, device features against host features, and
+        # both against the oracle's transcription of each utterance
         per_utt = [feats[foff[i]:foff[i + 1]] for i in range(n)]
         want = eng.transcribe(per_utt, list(sil), prev=200, blk=400, post=100)
         got = eng.transcribe_device(p_feats, nfr, p_sil, prev=200, blk=400, post=100)
         assert len(got) == n and all(np.array_equal(a, b) for a, b in zip(got, want))
+        for i in range(n):
+            ref, _ = orc.transcribe(blob, plan, per_utt[i], sil[i], prev=200, blk=400, post=100)
+            np.testing.assert_array_equal(got[i], ref, err_msg=f"utterance {i}")
+        for blk in (1600,):
+            got = eng.transcribe_device(p_feats, nfr, p_sil, prev=200, blk=blk, post=100)
+            for i in range(n):
+                ref, _ = orc.transcribe(blob, plan, per_utt[i], sil[i], prev=200, blk=blk, post=100)
+                np.testing.assert_array_equal(got[i], ref, err_msg=f"utterance {i}, blk {blk}")
         # return codes shared with wasr_transcribe
         one = np.zeros(1, np.uint32)
         off = np.zeros(n + 1, np.int64)

@@ -1,7 +1,8 @@
 """GPU test of wp_gemm_q_noalloc, the GEMM + per-row re-quantisation entry point that allocates
-no device memory.  It is meant for callers that cannot call cudaMalloc when they run it (code
-running inside a CUDA-graph capture, or a process with a fixed device-memory budget): instead of
-growing a staging buffer like wp_gemm_q, it stages through one fixed array inside the library.
+no device memory.  It is meant for callers that cannot call cudaMalloc when they run it: a
+process whose framework already handed the GPU's memory to its own caching allocator, or a
+latency-bound thread that must not block in cudaMalloc.  Instead of growing a staging buffer
+like wp_gemm_q, it stages through one fixed array inside the library.
 
 The test calls it through the C ABI and compares it with wp_gemm_q (the existing entry point)
 bit for bit, the tolerance every GEMM test here uses, on two calls in a row.  The second call

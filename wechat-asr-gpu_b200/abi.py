@@ -89,6 +89,7 @@ SIGNATURES = {
     "wk_attention_version": (C.c_char_p, []),
     "wp_gemm2_pc": (I, [P, P, P, I, I, Z, I, P, P, P, P]),
     "wp_gemm_i32": (I, [P, P, I, I, Z, I, P, P]),
+    "wp_gemm_i32_wait_probe": (I, [P, P, I, I, Z, I, P, P, C.c_uint64]),
     "wp_gemm_q_noalloc": (I, [P, P, P, I, I, Z, I, F, P, P, P, P]),
     # include/wasr.h
     "wasr_model_create": (P, [P, Z, C.POINTER(WasrPlan), I, I]),

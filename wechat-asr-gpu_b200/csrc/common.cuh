@@ -22,8 +22,9 @@ constexpr int W2 = 41, FLAT = 3840, K2 = C1 * 49, K3 = C2 * 9;
 // Device error codes written to a context's error word when a bounded wait gives up.
 enum : int { ERR_WAIT_FULL = 1, ERR_WAIT_EMPTY = 2, ERR_WAIT_ACC = 3 };
 
-// Upper bound for any spin-wait on an mbarrier: 2 s of %globaltimer.  A legitimate wait in
-// these kernels lasts microseconds; the bound only turns a bug into an error code.
+// Default upper bound for any spin-wait on an mbarrier: 2 s of %globaltimer.  A legitimate
+// wait in these kernels lasts microseconds; the bound only turns a bug into an error code.
+// Kernels take the bound as an argument (0 = this default), so a test can shorten it.
 constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;
 
 __device__ __forceinline__ unsigned long long globaltimer() {
@@ -58,12 +59,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait on phase `parity`; false if the 2 s limit passed.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Bounded wait on phase `parity`; false once limit_ns of %globaltimer passed without it.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          unsigned long long limit_ns = WAIT_LIMIT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer() - t0 > WAIT_LIMIT_NS) return false;
+    if (globaltimer() - t0 > limit_ns) return false;
   }
   return true;
 }

@@ -1,14 +1,19 @@
-// ctx.cu -- the reference's wp_* C ABI (csrc/wtlgpu.h) on top of the tcgen05 GEMM.
+// ctx.cu -- the wp_* C ABI of the reference's GEMM library (csrc/wtlgpu.h) on top of the
+// tcgen05 GEMM of gemm.cuh.
 //
-// Semantics mirrored from csrc/wtlgpu.cu: argument checks and return codes (:536-538,
-// :715-748), the legacy-default-stream call stream that switches for good to a private
-// capturable stream at the first capture (:751-775), capture end that always leaves the
-// stream out of capture mode (:777-825), replay / graph free / node count (:827-847).
-// What differs: no cuBLASLt handle, no algorithm search or disk cache, no padded weight
-// copies (the GEMM handles any n), and a device error word that wp_sync reports.
+// The ABI fixes the behaviour that the Rust shell (src/gpu.rs) relies on, and this file keeps
+// it: null arguments -> -1, empty shapes -> 0 with nothing enqueued, weight ranges outside the
+// blob -> -2; every op is enqueued on the context's call stream, which is the legacy default
+// stream until the first capture and the context's own capturable stream from then on; capture
+// is thread-local; whatever goes wrong while a capture is open, wp_capture_end leaves the stream
+// out of capture mode and returns one of -13 / -14 / -15; replay and graph release report -17 /
+// -18.  What is new: no cuBLASLt handle, algorithm search or disk cache (the GEMM handles any n
+// with compile-time tiles), and a device error word that wp_sync reports as -21.
 #include <cstdio>
 #include <cstring>
+#include <memory>
 #include <mutex>
+#include <type_traits>
 
 #include "../../include/wtlgpu.h"
 #include "gemm.cuh"
@@ -16,11 +21,60 @@
 
 using namespace wasr;
 
+namespace {
+
+// A failed runtime call leaves a sticky last-error value behind, which a later
+// cudaGetLastError() in the caller's own code would wrongly pick up.  Every failure path in
+// this file consumes it before it returns its ABI code.
+bool cuda_ok(cudaError_t e) {
+  if (e == cudaSuccess) return true;
+  cudaGetLastError();
+  return false;
+}
+
+struct GraphRelease {
+  void operator()(cudaGraph_t g) const { cudaGraphDestroy(g); }
+};
+using OwnedGraph = std::unique_ptr<std::remove_pointer_t<cudaGraph_t>, GraphRelease>;
+
+bool is_capturing(cudaStream_t s) {
+  if (s == nullptr) return false;  // the legacy stream is never put into capture mode here
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  return cuda_ok(cudaStreamIsCapturing(s, &st)) && st != cudaStreamCaptureStatusNone;
+}
+
+// Makes device `d` current for one call and restores the caller's device afterwards.
+class DeviceScope {
+ public:
+  explicit DeviceScope(int d) {
+    if (cudaGetDevice(&saved_) != cudaSuccess) {
+      cudaGetLastError();
+      saved_ = -1;
+    }
+    ok_ = saved_ == d || cuda_ok(cudaSetDevice(d));
+  }
+  ~DeviceScope() {
+    int cur = -1;
+    if (saved_ >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != saved_) cudaSetDevice(saved_);
+  }
+  bool ok() const { return ok_; }
+
+ private:
+  int saved_ = -1;
+  bool ok_ = false;
+};
+
+// sized at create for t <= 512 rows of n <= 4096, so engine shapes never grow it in capture
+constexpr size_t kScratchInit = 512ull * 4096 * 4;
+constexpr size_t kRowmaxInit = 4096;
+
+}  // namespace
+
 struct WpCtx {
   int dev = 0;
-  cudaStream_t call_stream = nullptr;  // nullptr == legacy default stream
-  cudaStream_t graph_stream = nullptr;
-  int capturing = 0;
+  cudaStream_t call_stream = nullptr;  // nullptr: the legacy default stream
+  cudaStream_t own_stream = nullptr;   // non-blocking, capturable; the call stream after a capture
+  bool capturing = false;
   size_t last_graph_nodes = 0;
   uint8_t* w = nullptr;
   size_t w_bytes = 0;
@@ -31,17 +85,76 @@ struct WpCtx {
   int* err_host = nullptr;  // mapped pinned error word
   int* err_dev = nullptr;
   std::mutex mu;
+
+  // Everything wp_create sets up; false leaves a partly built context for release().
+  bool init(const void* w_host, size_t bytes) {
+    if (!cuda_ok(cudaGetDevice(&dev))) return false;
+    gemm_prepare();
+    kern_prepare();
+    if (!cuda_ok(cudaStreamCreateWithFlags(&own_stream, cudaStreamNonBlocking))) return false;
+    if (!cuda_ok(cudaHostAlloc(reinterpret_cast<void**>(&err_host), sizeof(int), cudaHostAllocMapped)) ||
+        !cuda_ok(cudaHostGetDevicePointer(reinterpret_cast<void**>(&err_dev), err_host, 0)))
+      return false;
+    *err_host = 0;
+    if (!cuda_ok(cudaMalloc(&scratch, kScratchInit))) return false;
+    scratch_bytes = kScratchInit;
+    if (!cuda_ok(cudaMalloc(&rowmax, kRowmaxInit * sizeof(unsigned)))) return false;
+    rowmax_n = kRowmaxInit;
+    w_bytes = bytes;
+    if (bytes == 0) return true;
+    if (!cuda_ok(cudaMalloc(&w, bytes))) return false;
+    return cuda_ok(w_host ? cudaMemcpy(w, w_host, bytes, cudaMemcpyHostToDevice) : cudaMemset(w, 0, bytes));
+  }
+
+  void release() {
+    cudaDeviceSynchronize();
+    for (void* p : {static_cast<void*>(w), static_cast<void*>(scratch), static_cast<void*>(rowmax)})
+      if (p) cudaFree(p);
+    if (err_host) cudaFreeHost(err_host);
+    if (own_stream) cudaStreamDestroy(own_stream);
+    cudaGetLastError();
+  }
+
+  // Capture needs a stream other than the legacy one.  The first capture drains the legacy
+  // stream and moves the context to its own stream, which then stays the call stream (callers
+  // re-query wp_stream, so their own kernels land in the same graphs).
+  int open_capture() {
+    if (capturing || own_stream == nullptr) return -10;
+    if (call_stream == nullptr) {
+      if (!cuda_ok(cudaStreamSynchronize(nullptr))) return -10;
+      call_stream = own_stream;
+    }
+    if (!cuda_ok(cudaStreamBeginCapture(call_stream, cudaStreamCaptureModeThreadLocal))) return -10;
+    capturing = true;
+    return 0;
+  }
+
+  // Ends the open capture.  On every path the stream leaves capture mode; only a graph with at
+  // least one node that instantiates becomes an exec.
+  int close_capture(cudaGraphExec_t* exec) {
+    if (!capturing) return -12;
+    capturing = false;
+    cudaGraph_t raw = nullptr;
+    const bool ended = cuda_ok(cudaStreamEndCapture(call_stream, &raw));
+    OwnedGraph graph(raw);
+    if (!ended) {
+      // an error inside the region invalidated the capture; make sure it is really closed
+      while (is_capturing(call_stream)) {
+        cudaGraph_t rest = nullptr;
+        const bool closed = cuda_ok(cudaStreamEndCapture(call_stream, &rest));
+        OwnedGraph drop(rest);
+        if (!closed) break;
+      }
+      return -13;
+    }
+    if (!graph) return -14;
+    size_t nodes = 0;
+    if (!cuda_ok(cudaGraphGetNodes(graph.get(), nullptr, &nodes))) nodes = 0;
+    last_graph_nodes = nodes;
+    if (nodes == 0) return -14;  // nothing was enqueued: no use handing back an empty graph
+    return cuda_ok(cudaGraphInstantiateWithFlags(exec, graph.get(), 0)) ? 0 : -15;
+  }
 };
-
-static bool stream_capturing(cudaStream_t s) {
-  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-  if (s) cudaStreamIsCapturing(s, &cs);
-  return cs != cudaStreamCaptureStatusNone;
-}
-
-// sized at create for t <= 512 rows of n <= 4096, so engine shapes never grow it in capture
-static constexpr size_t kScratchInit = 512ull * 4096 * 4;
-static constexpr size_t kRowmaxInit = 4096;
 
 extern "C" {
 
@@ -50,95 +163,74 @@ const char* wp_version(void) {
 }
 
 WpCtx* wp_create(const void* w_host, size_t bytes) {
-  WpCtx* c = new WpCtx();
-  cudaGetDevice(&c->dev);
-  gemm_prepare();
-  kern_prepare();
-  if (cudaStreamCreateWithFlags(&c->graph_stream, cudaStreamNonBlocking) != cudaSuccess) {
-    delete c;
+  std::unique_ptr<WpCtx> c(new WpCtx());
+  if (!c->init(w_host, bytes)) {
+    c->release();
     return nullptr;
   }
-  c->call_stream = nullptr;
-  if (cudaHostAlloc(reinterpret_cast<void**>(&c->err_host), sizeof(int), cudaHostAllocMapped) != cudaSuccess ||
-      cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->err_dev), c->err_host, 0) != cudaSuccess) {
-    wp_destroy(c);
-    return nullptr;
-  }
-  *c->err_host = 0;
-  c->scratch_bytes = kScratchInit;
-  c->rowmax_n = kRowmaxInit;
-  if (cudaMalloc(&c->scratch, c->scratch_bytes) != cudaSuccess ||
-      cudaMalloc(&c->rowmax, c->rowmax_n * sizeof(unsigned)) != cudaSuccess) {
-    wp_destroy(c);
-    return nullptr;
-  }
-  c->w_bytes = bytes;
-  if (bytes > 0) {
-    if (cudaMalloc(&c->w, bytes) != cudaSuccess) {
-      wp_destroy(c);
-      return nullptr;
-    }
-    if (w_host) {
-      if (cudaMemcpy(c->w, w_host, bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
-        wp_destroy(c);
-        return nullptr;
-      }
-    } else {
-      cudaMemset(c->w, 0, bytes);
-    }
-  }
-  return c;
+  return c.release();
 }
 
 void wp_destroy(WpCtx* c) {
-  if (!c) return;
-  cudaDeviceSynchronize();
-  if (c->w) cudaFree(c->w);
-  if (c->scratch) cudaFree(c->scratch);
-  if (c->rowmax) cudaFree(c->rowmax);
-  if (c->err_host) cudaFreeHost(c->err_host);
-  if (c->graph_stream) cudaStreamDestroy(c->graph_stream);
+  if (c == nullptr) return;
+  c->release();
   delete c;
 }
 
 void* wp_alloc(size_t bytes) {
   void* p = nullptr;
-  if (bytes == 0) return nullptr;
-  return cudaMalloc(&p, bytes) == cudaSuccess ? p : nullptr;
-}
-void wp_free(void* p) {
-  if (p) cudaFree(p);
+  if (bytes > 0 && !cuda_ok(cudaMalloc(&p, bytes))) p = nullptr;
+  return p;
 }
 
+void wp_free(void* p) {
+  if (p != nullptr) cuda_ok(cudaFree(p));
+}
+
+}  // extern "C"
+
+// The synchronous copies of the ABI: -1 for a null pointer, -2 if the copy fails.
+static int blocking_copy(void* dst, const void* src, size_t bytes, cudaMemcpyKind kind) {
+  if (dst == nullptr || src == nullptr) return -1;
+  if (bytes == 0) return 0;
+  return cuda_ok(cudaMemcpy(dst, src, bytes, kind)) ? 0 : -2;
+}
+
+extern "C" {
+
 int wp_h2d(void* dev, const void* host, size_t bytes) {
-  if (!dev || !host) return -1;
-  return cudaMemcpy(dev, host, bytes, cudaMemcpyHostToDevice) == cudaSuccess ? 0 : -2;
+  return blocking_copy(dev, host, bytes, cudaMemcpyHostToDevice);
 }
+
 int wp_d2h(void* host, const void* dev, size_t bytes) {
-  if (!host || !dev) return -1;
-  return cudaMemcpy(host, dev, bytes, cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -2;
+  return blocking_copy(host, dev, bytes, cudaMemcpyDeviceToHost);
 }
+
 void* wp_devptr(WpCtx* c, size_t off) {
-  if (!c || off > c->w_bytes) return nullptr;
-  return c->w + off;
+  return (c != nullptr && off <= c->w_bytes) ? static_cast<void*>(c->w + off) : nullptr;
 }
+
 int wp_sync(WpCtx* c) {
-  if (!c) return -1;
-  if (cudaStreamSynchronize(c->call_stream) != cudaSuccess) return -2;
-  if (*reinterpret_cast<volatile int*>(c->err_host)) {
-    *c->err_host = 0;
+  if (c == nullptr) return -1;
+  if (!cuda_ok(cudaStreamSynchronize(c->call_stream))) return -2;
+  // a kernel of this context gave up a bounded wait since the last sync
+  volatile int* word = c->err_host;
+  if (*word != 0) {
+    *word = 0;
     return -21;
   }
   return 0;
 }
+
 int wp_set_stream(WpCtx* c, void* stream) {
-  if (!c) return -1;
+  if (c == nullptr) return -1;
   if (c->capturing) return -16;
   c->call_stream = static_cast<cudaStream_t>(stream);
   return 0;
 }
-void* wp_stream(WpCtx* c) { return c ? static_cast<void*>(c->call_stream) : nullptr; }
-size_t wp_scratch_bytes(WpCtx* c) { return c ? c->scratch_bytes : 0; }
+
+void* wp_stream(WpCtx* c) { return c == nullptr ? nullptr : static_cast<void*>(c->call_stream); }
+size_t wp_scratch_bytes(WpCtx* c) { return c == nullptr ? 0 : c->scratch_bytes; }
 
 }  // extern "C"
 
@@ -180,7 +272,7 @@ static int gemm_impl(WpCtx* c, const int8_t* xq, const float* xs, int t, int k, 
   // re-quant modes: fp32 staging + per-row |max|, then quantise with that max
   const size_t need = static_cast<size_t>(t) * n * sizeof(float);
   if (need > c->scratch_bytes || static_cast<size_t>(t) > c->rowmax_n) {
-    if (stream_capturing(stream)) return -5;
+    if (is_capturing(stream)) return -5;
     cudaStreamSynchronize(stream);
     if (need > c->scratch_bytes) {
       float* ns = nullptr;
@@ -254,23 +346,24 @@ int wp_gemm_i32(WpCtx* c, const int8_t* xq, int t, int k, size_t w_off, int n, v
 }  // extern "C"
 
 // ------------------------------------------------------------------------ no-allocation GEMM+quant
-// Some callers cannot call cudaMalloc at the time they run a GEMM: code running while a CUDA
-// graph is being captured (an allocation is not a capturable operation), or an embedding
-// process whose memory budget is fixed up front.  wp_gemm_q grows its fp32 staging buffer on
-// demand; wp_gemm_q_noalloc instead stages through this fixed array, which every GPU that loads
-// the library holds until the process exits: WP_NOALLOC_MAX_ELEMS fp32 values of GEMM output
-// (t*n <= 1,048,576, 4 MiB) followed by WP_NOALLOC_MAX_ROWS per-row maxima (t <= 4096).
+// Some callers cannot allocate device memory at the time they run a GEMM.  An embedding process
+// may have handed the whole GPU to its own caching allocator up front, so that a cudaMalloc
+// outside that pool fails; a latency-bound caller (the audio thread of a streaming recogniser)
+// must not block, and cudaMalloc / cudaFree may synchronise the device and wait on the driver.
+// wp_gemm_q grows its fp32 staging buffer on demand; wp_gemm_q_noalloc instead stages through
+// this fixed array, which every GPU that loads the library holds until the process exits:
+// WP_NOALLOC_MAX_ELEMS fp32 values of GEMM output (t*n <= 1,048,576, 4 MiB) followed by
+// WP_NOALLOC_MAX_ROWS per-row maxima (t <= 4096).
 static __device__ __align__(256) float g_noalloc_scratch[WP_NOALLOC_MAX_ELEMS + WP_NOALLOC_MAX_ROWS];
 
-// Device address of g_noalloc_scratch per device.  In host code the array's name is only a
+// Device address of g_noalloc_scratch on each device.  In host code the array's name is only a
 // host-side stand-in, so the address is looked up with cudaGetSymbolAddress once per device,
-// with that device current.
+// with that device current (the caller holds a DeviceScope for it).
 static std::mutex g_noalloc_mu;
 static float* g_noalloc_addr[64] = {};
 
-static int noalloc_scratch(float** out) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -23;
+static int noalloc_scratch(int dev, float** out) {
+  if (dev < 0 || dev >= 64) return -23;
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (!g_noalloc_addr[dev]) {
     void* p = nullptr;
@@ -302,8 +395,11 @@ int wp_gemm_q_noalloc(WpCtx* c, const int8_t* xq, const float* xs, int t, int k,
             t, n, WP_NOALLOC_MAX_ROWS, WP_NOALLOC_MAX_ELEMS);
     return -22;
   }
+  // the weights, the error word and the scratch all live on the context's device
+  DeviceScope on(c->dev);
+  if (!on.ok()) return -23;
   float* scratch = nullptr;
-  if (const int rc = noalloc_scratch(&scratch)) return rc;
+  if (const int rc = noalloc_scratch(c->dev, &scratch)) return rc;
   unsigned* rowmax = reinterpret_cast<unsigned*>(scratch + WP_NOALLOC_MAX_ELEMS);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   std::lock_guard<std::mutex> lock(c->mu);
@@ -329,6 +425,35 @@ int wp_gemm_q_noalloc(WpCtx* c, const int8_t* xq, const float* xs, int t, int k,
   return launch_quant_rows_max(scratch, t, n, rowmax, out_q, out_s, st);
 }
 
+// Failure-handling test hook: one int32 GEMM whose producer warp issues no loads, so the MMA
+// and epilogue warps' mbarrier waits run out after wait_ns with no copy or MMA in flight; the
+// kernel records ERR_WAIT_* in the context's error word, releases its TMEM and returns, and
+// the next wp_sync reports -21.
+int wp_gemm_i32_wait_probe(WpCtx* c, const int8_t* xq, int t, int k, size_t w_off, int n, void* stream,
+                           int32_t* acc, unsigned long long wait_ns) {
+  if (!c || !xq || !acc) return -1;
+  if (t <= 0 || k <= 0 || n <= 0) return 0;
+  if (wait_ns == 0 || wait_ns > 1000000000ull || k % 16 != 0) return -2;  // the tcgen05 path only
+  if (static_cast<size_t>(n) * static_cast<size_t>(k) > c->w_bytes ||
+      w_off > c->w_bytes - static_cast<size_t>(n) * static_cast<size_t>(k))
+    return -2;
+  std::lock_guard<std::mutex> lock(c->mu);
+  GemmArgs g{};
+  g.a = xq;
+  g.b = reinterpret_cast<const int8_t*>(c->w + w_off);
+  g.M = t;
+  g.N = n;
+  g.K = k;
+  g.n_store = n;
+  g.ldo = n;
+  g.err = c->err_dev;
+  g.out_i32 = acc;
+  g.epi = EPI_I32;
+  g.wait_ns = wait_ns;
+  g.idle_producer = 1;
+  return gemm_run(g, static_cast<cudaStream_t>(stream));
+}
+
 int wp_quant_rows(const float* y, int t, int n, void* stream, int8_t* out_q, float* out_s) {
   if (!y || !out_q || !out_s) return -1;
   if (t <= 0 || n <= 0) return 0;
@@ -338,86 +463,31 @@ int wp_quant_rows(const float* y, int t, int n, void* stream, int8_t* out_q, flo
 
 // ------------------------------------------------------------------------ CUDA graphs
 int wp_capture_begin(WpCtx* c) {
-  if (!c) return -1;
-  if (c->capturing) {
-    fprintf(stderr, "[wasr] capture already in progress\n");
-    return -10;
-  }
-  if (!c->graph_stream) return -10;
-  if (c->call_stream == nullptr) {
-    // the legacy stream cannot be captured: drain it, then move to the private stream for good
-    cudaError_t se = cudaStreamSynchronize(nullptr);
-    if (se != cudaSuccess) {
-      cudaGetLastError();
-      return -10;
-    }
-    c->call_stream = c->graph_stream;
-  }
-  if (cudaStreamBeginCapture(c->call_stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
-    cudaGetLastError();
-    return -10;
-  }
-  c->capturing = 1;
-  return 0;
+  if (c == nullptr) return -1;
+  const int rc = c->open_capture();
+  if (rc != 0 && c->capturing) fprintf(stderr, "[wasr] wp_capture_begin: a capture is already open\n");
+  return rc;
 }
 
 int wp_capture_end(WpCtx* c, void** out_exec) {
-  if (!c || !out_exec) return -1;
-  *out_exec = nullptr;
-  if (!c->capturing) return -12;
-  cudaStream_t s = c->call_stream;
-  c->capturing = 0;
-  cudaGraph_t g = nullptr;
-  cudaError_t e = cudaStreamEndCapture(s, &g);
-  if (e != cudaSuccess) {
-    cudaGetLastError();
-    if (stream_capturing(s)) {
-      cudaGraph_t g2 = nullptr;
-      cudaStreamEndCapture(s, &g2);
-      if (g2) cudaGraphDestroy(g2);
-      cudaGetLastError();
-    }
-    return -13;
-  }
-  if (!g) return -14;
-  size_t nodes = 0;
-  cudaGraphGetNodes(g, nullptr, &nodes);
-  c->last_graph_nodes = nodes;
-  if (nodes == 0) {
-    cudaGraphDestroy(g);
-    return -14;
-  }
-  cudaGraphExec_t ex = nullptr;
-  e = cudaGraphInstantiate(&ex, g, 0);
-  cudaGraphDestroy(g);
-  if (e != cudaSuccess) {
-    cudaGetLastError();
-    return -15;
-  }
-  *out_exec = ex;
-  return 0;
+  if (c == nullptr || out_exec == nullptr) return -1;
+  cudaGraphExec_t exec = nullptr;
+  const int rc = c->close_capture(&exec);
+  *out_exec = rc == 0 ? static_cast<void*>(exec) : nullptr;
+  return rc;
 }
 
 int wp_replay(WpCtx* c, void* exec) {
-  if (!c || !exec) return -1;
-  if (cudaGraphLaunch(static_cast<cudaGraphExec_t>(exec), c->call_stream) != cudaSuccess) {
-    cudaGetLastError();
-    return -17;
-  }
-  return 0;
+  if (c == nullptr || exec == nullptr) return -1;
+  return cuda_ok(cudaGraphLaunch(static_cast<cudaGraphExec_t>(exec), c->call_stream)) ? 0 : -17;
 }
 
-int wp_graph_free(WpCtx* c, void* exec) {
-  (void)c;
-  if (!exec) return 0;
-  if (cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(exec)) != cudaSuccess) {
-    cudaGetLastError();
-    return -18;
-  }
-  return 0;
+int wp_graph_free(WpCtx*, void* exec) {
+  if (exec == nullptr) return 0;
+  return cuda_ok(cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(exec))) ? 0 : -18;
 }
 
-size_t wp_graph_count(WpCtx* c) { return c ? c->last_graph_nodes : 0; }
-int wp_is_capturing(WpCtx* c) { return c ? c->capturing : 0; }
+size_t wp_graph_count(WpCtx* c) { return c == nullptr ? 0 : c->last_graph_nodes; }
+int wp_is_capturing(WpCtx* c) { return (c != nullptr && c->capturing) ? 1 : 0; }
 
 }  // extern "C"

@@ -45,6 +45,9 @@ struct GemmArgs {
   int* err;            // device error word
   int epi;             // Epi kind
   int tma_out;         // 1: out / out_i32 blocks move by TMA (tensor map passed to the kernel)
+  unsigned long long wait_ns;  // limit of every mbarrier wait (0: WAIT_LIMIT_NS)
+  int idle_producer;   // failure-handling test only: the producer issues no loads, so the
+                       // consumers' waits run out with nothing in flight
 };
 
 template <int EPI>
@@ -339,6 +342,7 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI, EW>::THREADS, 1)
   const int tiles = n_tiles * ((g.M + Cfg::BM - 1) / Cfg::BM);
   const int nk = (g.K + Cfg::BK - 1) / Cfg::BK;
   const bool tma_out = g.tma_out != 0 && EPI != EPI_ARGMAX;
+  const unsigned long long lim = g.wait_ns ? g.wait_ns : WAIT_LIMIT_NS;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < ST; s++) {
@@ -368,11 +372,11 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI, EW>::THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       int kc = 0;
-      for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
+      for (int tile = blockIdx.x; tile < tiles && !*abort_flag && !g.idle_producer; tile += gridDim.x) {
         const int m0 = (tile / n_tiles) * Cfg::BM, n0 = (tile % n_tiles) * BN;
         for (int kb = 0; kb < nk; kb++, kc++) {
           const int s = kc % ST;
-          if (kc >= ST && !mbar_wait(empty + s, ((kc / ST) - 1) & 1)) {
+          if (kc >= ST && !mbar_wait(empty + s, ((kc / ST) - 1) & 1, lim)) {
             atomicExch(g.err, ERR_WAIT_EMPTY);
             *abort_flag = 1;
             break;
@@ -384,7 +388,7 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI, EW>::THREADS, 1)
       }
       // drain: never leave the CTA while a bulk copy may still write its shared memory
       for (int k = kc > ST ? kc - ST : 0; k < kc; k++)
-        if (!mbar_wait(full + k % ST, (k / ST) & 1)) atomicExch(g.err, ERR_WAIT_FULL);
+        if (!mbar_wait(full + k % ST, (k / ST) & 1, lim)) atomicExch(g.err, ERR_WAIT_FULL);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -392,7 +396,7 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI, EW>::THREADS, 1)
       int kc = 0, it = 0;
       for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x, it++) {
         const int b = it & 1, u = it >> 1;
-        if (it >= 2 && !mbar_wait(tempty + b, (u - 1) & 1)) {
+        if (it >= 2 && !mbar_wait(tempty + b, (u - 1) & 1, lim)) {
           atomicExch(g.err, ERR_WAIT_ACC);
           *abort_flag = 1;
           break;
@@ -401,7 +405,7 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI, EW>::THREADS, 1)
         const uint32_t d = tmem + static_cast<uint32_t>(b * BN);
         for (int kb = 0; kb < nk; kb++, kc++) {
           const int s = kc % ST;
-          if (!mbar_wait(full + s, (kc / ST) & 1)) {
+          if (!mbar_wait(full + s, (kc / ST) & 1, lim)) {
             atomicExch(g.err, ERR_WAIT_FULL);
             *abort_flag = 1;
             break;
@@ -473,7 +477,7 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI, EW>::THREADS, 1)
       const int m0 = (tile / n_tiles) * Cfg::BM, n0 = (tile % n_tiles) * BN;
       // this thread's row scale, loaded while the accumulator is still being computed
       const float xs_row = (EPI != EPI_I32 && m0 + q * 32 + lane < g.M) ? g.xs[m0 + q * 32 + lane] : 0.0f;
-      const bool ok = mbar_wait(tfull + b, u & 1);
+      const bool ok = mbar_wait(tfull + b, u & 1, lim);
       if (!ok) {
         atomicExch(g.err, ERR_WAIT_ACC);
         *abort_flag = 1;
@@ -502,7 +506,7 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI, EW>::THREADS, 1)
             const int bi = cc % Cfg::NBUF;
             float* buf = wb + bi * Cfg::STG_FLOATS;
             if constexpr (EPI == EPI_F32_ADD) {
-              if (!mbar_wait(hb + bi, (hpar >> bi) & 1)) {
+              if (!mbar_wait(hb + bi, (hpar >> bi) & 1, lim)) {
                 atomicExch(g.err, ERR_WAIT_FULL);
                 *abort_flag = 1;
               }
@@ -540,7 +544,7 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI, EW>::THREADS, 1)
       bulk_wait_all();
       // h loads issued ahead but never consumed (abort): let them land before the CTA exits
       for (int bi = 0; bi < Cfg::NBUF; bi++)
-        if ((pend >> bi) & 1u) mbar_wait(hb + bi, (hpar >> bi) & 1);
+        if ((pend >> bi) & 1u) mbar_wait(hb + bi, (hpar >> bi) & 1, lim);
     }
   }
   tc_fence_before();
