@@ -191,6 +191,28 @@ def gemm_probe(pkg, local, stream, peak_tops, M=16384, N=2048, K=2048, reps=20):
         L.wp_destroy(ctx)
 
 
+def int8_peak(pkg, local, stream, iters=2048, reps=5):
+    """Dense int8 tensor-core rate of this GPU, measured: wasr_i8_mma_peak issues back-to-back
+    tcgen05.mma kind::i8 (M 128, N 256, K 32) from shared memory on every SM with no loads;
+    CUDA events on the launching stream around `reps` launches after a warm-up."""
+    import torch
+    L = pkg.abi.load()
+    sms = torch.cuda.get_device_properties(local).multi_processor_count
+    err = torch.zeros(1, dtype=torch.int32, device=f"cuda:{local}")
+    torch.cuda.synchronize()
+    rc = L.wasr_i8_mma_peak(iters, sms, err.data_ptr(), stream.cuda_stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        rc |= L.wasr_i8_mma_peak(iters, sms, err.data_ptr(), stream.cuda_stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    ops = float(sms) * iters * 4 * 2 * 128 * 256 * 32
+    return {"tops": round(ops / (ms / 1e3) / 1e12, 1), "ms": round(ms, 4), "rc": int(rc), "wait_error": int(err.item()),
+            "how": f"{sms} CTAs x {iters} x 4 tcgen05.mma kind::i8 M128 N256 K32 from shared memory, no loads"}
+
+
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -365,6 +387,43 @@ def text_line(pkg, ids_list):
             "impl": "Python restatement of Model::text + tidy (src/model.rs:620-642, src/stream.rs:203-210)"}
 
 
+def gather_and_check(pkg, eng, blob, plan, lengths, shard, local_ids, rank, world, local):
+    """After the timed steps: each rank hands its shard's ids (from the e2e run) to the node
+    driver, which gathers every utterance on rank 0 through the rendezvous store, re-queueing
+    the shard of a rank that does not deliver.  Rank 0 then transcribes all utterances on its
+    one GPU and counts the utterances whose gathered ids are identical."""
+    import torch.distributed as dist
+    store = dist.distributed_c10d._get_default_store()
+
+    def features(idx):
+        fs = [pkg.fbank(pkg.synth.make_audio(100000 + i, lengths[i])) for i in idx]
+        return [f for f, _ in fs], [x for _, x in fs]
+
+    def transcribe(idx):  # this rank's own shard comes from the e2e run; a re-queued one is redone
+        if all(i in local_ids for i in idx):
+            return [local_ids[i] for i in idx]
+        f, x = features(idx)
+        return eng.transcribe(f, x, blk=1600)
+
+    t0 = time.perf_counter()
+    allids = pkg.dist.run_sharded(transcribe, lengths, rank, world, store, timeout_s=120.0, tag="bench_gather")
+    gather_ms = (time.perf_counter() - t0) * 1e3
+    if rank != 0:
+        return None
+    f, x = features(range(len(lengths)))
+    rows = sum((a.shape[0] - 5) // 5 + 1 for a in f if a.shape[0] >= 5)
+    one = pkg.Engine(blob, plan, device=local, max_rows=max(rows, 1024))
+    try:
+        ref = one.transcribe(f, x, blk=1600)
+    finally:
+        one.close()
+    same = sum(bool(np.array_equal(a, b)) for a, b in zip(allids, ref))
+    return {"utterances": len(ref), "ids_identical_to_one_gpu": int(same), "gather_ms": round(gather_ms, 3),
+            "failed_ranks": list(pkg.dist.run_sharded.last_failed),
+            "how": "dist.run_sharded: per-rank ids through the rendezvous store to rank 0; "
+                   "reference = all utterances transcribed on rank 0's GPU alone"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -487,13 +546,22 @@ def main():
         if dist_on:
             dist.all_reduce(e_t, op=dist.ReduceOp.MAX)
         ids_bytes = 4 * sum(len(o) for o in out)
+        local_ids = dict(zip(shard, out))
         e2e_ids = out if world == 1 else None  # rank 0 of one rank holds every utterance, in order
         e2e = {"value": round(total_audio / float(e_t.item()), 3), "unit": "audio-s/s",
                "h2d_bytes_per_step": int(cat.nbytes), "d2h_bytes_per_step": int(ids_bytes),
                "api": "wasr_transcribe (pinned host features in, host ids out)"}
 
+    # ---- N > 1: every rank's ids gathered on rank 0 through the rendezvous store (the node
+    # driver dist.run_sharded, src/bin/wasr.rs:147-169 collects per file), checked against one GPU
+    gather = None
+    if dist_on and e2e is not None:
+        gather = gather_and_check(pkg, eng, blob, plan, lengths, shard, local_ids, rank, world, local)
+
     # ---- roofline of the dominant kernel class (last timed step, CUDA events on its stream)
     hbm, bf16, src = peaks()
+    i8 = int8_peak(pkg, local, stream)
+    i8_peak = i8["tops"] if i8["rc"] == 0 and i8["wait_error"] == 0 else 2 * bf16
     names = pkg.abi.KERNEL_CLASSES
     ops, byts, flops, rows, macs = algorithmic_work(t1, plan.n_layers)
     dom = max(range(len(names)), key=lambda i: prof_ms[i])
@@ -508,33 +576,51 @@ def main():
             1 if dname in ("conv1", "conv2", "conv3", "gemm_lin", "gemm_out_argmax") else plan.n_layers)
         if tr and prof_n[dom]:
             traffic = round(tr * rows * per_layer / prof_n[dom])
+    sms = torch.cuda.get_device_properties(local).multi_processor_count
+    mhz = (clocks or {}).get("sm_mhz") or 1965.0
+    peak_mac = sms * 128 * mhz * 1e6 / 2 / 1e12
+    mac_basis = (f"{sms} SMs x 128 fp32 lanes x {mhz:.0f} MHz / 2 ops per exactly rounded MAC (packed and "
+                 f"scalar fp32 ops both measured at 127 lane-ops/clk/SM)")
     if dname in ops:
         ach = ops[dname] / prof_n[dom] / (dms / prof_n[dom] / 1e3) / 1e12
-        roof = {"kernel": dname, "bound": "tensor", "achieved": round(ach, 2), "peak": round(2 * bf16, 1),
-                "unit": "TOPS", "frac": round(ach / (2 * bf16), 4), "traffic": traffic,
-                "peak_source": f"int8 dense = 2 x bf16 dense burst ({src} {bf16} TF/s)",
+        roof = {"kernel": dname, "bound": "tensor", "achieved": round(ach, 2), "peak": round(i8_peak, 1),
+                "unit": "TOPS", "frac": round(ach / i8_peak, 4), "traffic": traffic,
+                "peak_source": "measured int8 dense (int8_peak)",
                 "launches": int(prof_n[dom]), "avg_launch_us": round(dms / prof_n[dom] * 1e3, 2)}
+    elif dname in macs and prof_n[dom]:
+        # the exact-arithmetic kernels (attention, conv2, conv3) are bound by the CUDA-core fp32
+        # pipe: every MAC is a rounded multiply then a rounded add, in the CPU's order
+        ach_mac = macs[dname] / (dms / 1e3) / 1e12
+        b = byts.get(dname, 0.0)
+        roof = {"kernel": dname, "bound": "fp32", "achieved": round(ach_mac, 3), "peak": round(peak_mac, 2),
+                "unit": "TMAC/s", "frac": round(ach_mac / peak_mac, 4), "traffic": traffic,
+                "peak_source": mac_basis, "launches": int(prof_n[dom]),
+                "avg_launch_us": round(dms / prof_n[dom] * 1e3, 2),
+                "hbm": {"achieved": round(b / (dms / 1e3) / 1e9, 1), "peak": hbm, "unit": "GB/s",
+                        "frac": round(b / (dms / 1e3) / 1e9 / hbm, 4), "peak_source": f"{src} hbm_gbs"}}
     else:
         b = byts.get(dname, 0.0)
         ach = b / prof_n[dom] / (dms / prof_n[dom] / 1e3) / 1e9 if prof_n[dom] else 0.0
         roof = {"kernel": dname, "bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(ach / hbm, 4), "traffic": traffic, "peak_source": f"{src} hbm_gbs",
                 "launches": int(prof_n[dom]), "avg_launch_us": round(dms / prof_n[dom] * 1e3, 2)}
-    if dname in macs and prof_n[dom]:
-        # CUDA-core roofline: 128 fp32 lanes per SM per clock at the sampled SM clock, 2 per MAC
-        sms = torch.cuda.get_device_properties(local).multi_processor_count
-        mhz = (clocks or {}).get("sm_mhz") or 1965.0
-        peak_mac = sms * 128 * mhz * 1e6 / 2 / 1e12
-        ach_mac = macs[dname] / (dms / 1e3) / 1e12
-        roof["fp32_exact"] = {"achieved": round(ach_mac, 3), "peak": round(peak_mac, 2), "unit": "TMAC/s",
-                              "frac": round(ach_mac / peak_mac, 4),
-                              "basis": f"{sms} SMs x 128 fp32 lanes x {mhz:.0f} MHz / 2 ops per exactly rounded MAC"}
     gemm_ops = sum(ops.values())
     gemm_ms = sum(prof_ms[names.index(k)] for k in ops)
     roof["all_gemms_tops"] = round(gemm_ops / (gemm_ms / 1e3) / 1e12, 2) if gemm_ms else None
+    # every int8 GEMM of the model at its real shape (M = this rank's rows) and epilogue, against
+    # the measured int8 peak (BASELINE's target: >= 60 % of dense int8 peak at M >= 1600)
+    roof["int8_peak"] = i8
+    roof["gemms"] = {k: {"tops": round(ops[k] / (prof_ms[names.index(k)] / 1e3) / 1e12, 1),
+                         "frac": round(ops[k] / (prof_ms[names.index(k)] / 1e3) / 1e12 / i8_peak, 4),
+                         "ms": round(prof_ms[names.index(k)], 3), "M": int(rows)}
+                     for k in ops if prof_ms[names.index(k)] > 0}
+    roof["exact_fp32"] = {k: {"tmac_s": round(macs[k] / (prof_ms[names.index(k)] / 1e3) / 1e12, 3),
+                              "frac": round(macs[k] / (prof_ms[names.index(k)] / 1e3) / 1e12 / peak_mac, 4),
+                              "ms": round(prof_ms[names.index(k)], 3)}
+                          for k in macs if prof_ms[names.index(k)] > 0}
     roof["kernel_ms_last_step"] = {names[i]: round(prof_ms[i], 3) for i in range(len(names)) if prof_n[i]}
 
-    gprobe = gemm_probe(pkg, local, stream, 2 * bf16) if (rank == 0 and not args.no_gemm_probe) else None
+    gprobe = gemm_probe(pkg, local, stream, i8_peak) if (rank == 0 and not args.no_gemm_probe) else None
     fbg = gpu_fbank_line(pkg, pcms, feats, local, stream) if (rank == 0 and not args.no_gemm_probe) else None
 
     # single-stream latency does not depend on N: measured at N = 1 only
@@ -561,7 +647,7 @@ def main():
                            "rows_rank0": int(sum(t1)), "n_layers": plan.n_layers, "max_rows_per_chunk": args.max_rows,
                            "l2": "flushed (256 MiB write) before every timed step",
                            "parallelism": f"utterance-sharded LPT over {world} GPU(s), no collective"},
-                "roofline": roof, "gemm_probe": gprobe, "cpu_baseline": cpu, "e2e": e2e,
+                "roofline": roof, "gemm_probe": gprobe, "cpu_baseline": cpu, "e2e": e2e, "gather": gather,
                 "fbank_host": {"value": round(my_audio / fbank_s, 1) if fbank_s > 0 else None, "unit": "audio-s/s",
                                "threads": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count())),
                                "scope": "rank 0's utterances, one call per utterance",

@@ -189,6 +189,14 @@ int64_t wasr_ctc_collapse(const uint32_t* ids, int64_t n, uint32_t* out);
  * device floats, so tests can compare them bit for bit with the host's glibc / IEEE division. */
 int wasr_eval_math(int fn, const float* x, float* y, int n, void* stream);
 
+/* Measurement hook, no counterpart in the reference: the dense int8 tensor-core rate of this
+ * GPU.  Launches `ctas` CTAs (one per SM) on `stream`; each issues iters x 4 back-to-back
+ * tcgen05.mma kind::i8 of M = 128, N = 256, K = 32 from shared memory with no loads, i.e.
+ * ctas * iters * 4 * 2 * 128 * 256 * 32 int8 ops; the caller times it with events.  *err (device
+ * int, zeroed by the caller) receives a nonzero code if the completion wait ran out.  0, -1 for
+ * bad arguments, -4 if the launch failed. */
+int wasr_i8_mma_peak(int iters, int ctas, int* err, void* stream);
+
 const char* wasr_version(void);
 
 #ifdef __cplusplus

@@ -133,9 +133,12 @@ def test_wk_front_bit_exact(gpu_lib, dev, orc, pkg, t):
     np.testing.assert_array_equal(got, orc.frontend(x, c1, c2, c3))
 
 
-# t covers every key-tail width of a 32-key chunk (1, 2, 3 and 4 groups of 8: t mod 32 = 1, 13,
-# 22, 31) and 1-, 2-, 3-, 7- and 8-tile segments (65 and 100: tiles of 33 and 50 rows)
-@pytest.mark.parametrize("t", [1, 5, 13, 31, 32, 33, 45, 65, 100, 150, 390, 512])
+# t covers every key-tail width of a key chunk (1 to 4 groups of 8 in a 32-key chunk and 1 to 8
+# in a 64-key one: t mod 64 = 1, 13, 22, 31, 33, 45, 63, 0 and 8-key boundaries), 1- to 8-tile
+# segments (65 and 100: tiles of 33 and 50 rows; tiles whose last warp holds 1 to 7 rows) and the
+# largest shapes
+@pytest.mark.parametrize("t", [1, 5, 8, 13, 31, 32, 33, 45, 63, 64, 65, 100, 127, 128, 129, 150, 200, 265,
+                               390, 512])
 def test_wk_attention(gpu_lib, dev, orc, t):
     L = gpu_lib
     rng = np.random.default_rng(t + 100)

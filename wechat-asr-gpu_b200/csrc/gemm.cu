@@ -174,4 +174,67 @@ int gemm_run(const GemmArgs& g, cudaStream_t s) {
   return -1;
 }
 
+// Dense int8 tensor-core throughput probe: one CTA per SM, one elected thread issues `iters`
+// rounds of 4 back-to-back tcgen05.mma kind::i8 (M = 128, N = 256, K = 32; 2 * 128 * 256 * 128
+// ops a round) from fixed 128B-swizzled shared-memory tiles into two alternating TMEM
+// accumulators, with no loads at all, then waits (bounded) for their completion.  Operand values
+// do not affect the rate.  The denominator for the int8 GEMMs' tensor-core fractions.
+constexpr int I8_PEAK_SMEM = 120 * 1024;  // more than the tiles need: keeps one CTA per SM
+__global__ void __launch_bounds__(128, 1) i8_mma_peak_k(int iters, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;           // [128 rows][128 B]
+  uint8_t* sB = smem + 16384;   // [256 rows][128 B]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sB + 32768);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(bar + 1);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  for (int i = tid; i < 49152 / 4; i += 128) reinterpret_cast<uint32_t*>(smem)[i] = 0x01010101u * (i & 7);
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(slot, 512);
+    tmem_relinquish();
+  }
+  fence_proxy_async_smem();  // the operand stores before the tensor core reads them
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *slot;
+  if (tid == 0) {
+    constexpr uint32_t idesc = idesc_i8(256);
+    const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
+    for (int it = 0; it < iters; it++) {
+      const uint32_t d = tmem + static_cast<uint32_t>((it & 1) * 256);
+#pragma unroll
+      for (int kk = 0; kk < 4; kk++)
+        mma_i8(d, desc_sw128(a0 + kk * 32), desc_sw128(b0 + kk * 32), idesc, (it >= 2 || kk > 0) ? 1u : 0u);
+    }
+    mma_commit(bar);
+    if (!mbar_wait(bar, 0)) atomicExch(err, ERR_WAIT_ACC);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 }  // namespace wasr
+
+extern "C" int wasr_i8_mma_peak(int iters, int ctas, int* err, void* stream) {
+  using namespace wasr;
+  if (iters <= 0 || ctas <= 0 || err == nullptr) return -1;
+  static unsigned done = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(done & (1u << (dev & 31)))) {
+    if (cudaFuncSetAttribute(i8_mma_peak_k, cudaFuncAttributeMaxDynamicSharedMemorySize, I8_PEAK_SMEM) != cudaSuccess)
+      return -4;
+    done |= 1u << (dev & 31);
+  }
+  i8_mma_peak_k<<<ctas, 128, I8_PEAK_SMEM, static_cast<cudaStream_t>(stream)>>>(iters, err);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}

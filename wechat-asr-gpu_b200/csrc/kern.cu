@@ -574,14 +574,15 @@ __device__ __forceinline__ void cp_async_wait_n(int n) {  // n in 0..7, a run-ti
   }
 }
 
+// rpb <= LR_ROWS rows per block (the launcher sizes it so that a small M still fills the GPU)
 __global__ void __launch_bounds__(LR_THREADS, 2) ln_rows_k(const float* __restrict__ h, const float* __restrict__ g,
-                                                           const float* __restrict__ b, int m,
+                                                           const float* __restrict__ b, int m, int rpb,
                                                            int8_t* __restrict__ xq, float* __restrict__ xs) {
   extern __shared__ __align__(16) float sm[];
   float4* S = reinterpret_cast<float4*>(sm);
-  float* mean = sm + LR_ROWS * D;
-  float* rinv = mean + LR_ROWS;
-  const int r0 = blockIdx.x * LR_ROWS, nr = min(LR_ROWS, m - r0), tid = threadIdx.x;
+  float* mean = sm + rpb * D;
+  float* rinv = mean + rpb;
+  const int r0 = blockIdx.x * rpb, nr = min(rpb, m - r0), tid = threadIdx.x;
   for (int c = 0; c < 8; c++) {  // chunk c: columns 64c .. 64c+63 of every row
     for (int e = tid; e < nr * 16; e += LR_THREADS) {
       const int rr = e >> 4, c4 = 16 * c + (e & 15);
@@ -1299,8 +1300,16 @@ int launch_ln_quant(float* h, const float* o, const float* g, const float* b, in
     set_smem(reinterpret_cast<const void*>(ln_quant_k<true>), LnCfg<true>::SMEM);
     ln_quant_k<true><<<blocks, LN_THREADS, LnCfg<true>::SMEM, st>>>(h, o, g, b, m, xq, xs);
   } else {
+    // two blocks fit an SM: as many rows per block as fill every slot once, at most LR_ROWS
+    // (a small M, e.g. one GPU's shard of a multi-GPU job, otherwise leaves SMs idle)
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+      sms = 148;
+    const int rpb = std::max(8, std::min(LR_ROWS, (m + 2 * sms - 1) / (2 * sms)));
+    const size_t smem = static_cast<size_t>(rpb) * D * 4 + 2 * rpb * 4;
     set_smem(reinterpret_cast<const void*>(ln_rows_k), LR_SMEM);
-    ln_rows_k<<<(m + LR_ROWS - 1) / LR_ROWS, LR_THREADS, LR_SMEM, st>>>(h, g, b, m, xq, xs);
+    ln_rows_k<<<(m + rpb - 1) / rpb, LR_THREADS, smem, st>>>(h, g, b, m, rpb, xq, xs);
   }
   return launched();
 }
