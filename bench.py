@@ -296,13 +296,10 @@ def run_reference(args, rank):
     blob, plan = pkg.synth.make_model(seed=1, n_layers=40)
     cores = os.cpu_count() or 1
     orc.set_threads(cores)
-    # each step transcribes the same bounded sample: the first config-4 utterances up to ~20 s of audio
-    sample, tot = [], 0.0
-    for i, L in enumerate(lengths):
-        sample.append(i)
-        tot += L
-        if tot >= 20.0:
-            break
+    # each step transcribes the same bounded sample with config 4's length distribution: the
+    # utterances at 12 evenly spaced quantiles of the length (about 84 s of audio)
+    order = sorted(range(len(lengths)), key=lambda i: lengths[i])
+    sample = sorted({order[int((k + 0.5) * len(order) / 12)] for k in range(12)})
     data = []
     for i in sample:
         pcm = pkg.synth.make_audio(100000 + i, lengths[i])
@@ -324,7 +321,8 @@ def run_reference(args, rank):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": WORKLOAD, "sample": f"first {len(sample)} utterances, {audio:.2f} s of audio per step"},
+            "config": {"workload": WORKLOAD,
+                       "sample": f"{len(sample)} utterances at evenly spaced length quantiles, {audio:.2f} s of audio per step"},
             "cpu_baseline": {"value": round(val, 3), "unit": "audio-s/s", "cores": cores, "kind": "port",
                              "sample": f"oracle restatement of src/kernels.rs + src/model.rs CPU path, "
                                        f"{len(sample)} utterances / {audio:.2f} s audio per step"},

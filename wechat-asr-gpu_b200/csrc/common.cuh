@@ -223,6 +223,30 @@ __device__ __forceinline__ int8_t quant_one(float v, float inv) {
 // Exhaustive comparison against glibc on every float input: tanhf identical for all
 // 4,278,190,082 non-NaN inputs; expf identical for all inputs except two, which are special-
 // cased below with glibc's values.
+//
+// Upstream sources of the restated algorithms and their constants, with their notices:
+// * tanhf_ref / expm1f_ref follow fdlibm's s_tanh.c / s_expm1.c as converted to float
+//   (s_tanhf.c / s_expm1f.c, conversion by Ian Lance Taylor, Cygnus Support), the versions
+//   glibc ships in sysdeps/ieee754/flt-32:
+//     Copyright (C) 1993 by Sun Microsystems, Inc. All rights reserved.
+//     Developed at SunPro, a Sun Microsystems, Inc. business.
+//     Permission to use, copy, modify, and distribute this software is freely granted,
+//     provided that this notice is preserved.
+// * expf_body follows the expf of Arm's optimized-routines (math/expf.c, its 2^(i/32) table
+//   and polynomial), which glibc ships as sysdeps/ieee754/flt-32/e_expf.c:
+//     Copyright (c) 2017-2018, Arm Limited.  SPDX-License-Identifier: MIT.
+//     Permission is hereby granted, free of charge, to any person obtaining a copy of this
+//     software and associated documentation files (the "Software"), to deal in the Software
+//     without restriction, including without limitation the rights to use, copy, modify,
+//     merge, publish, distribute, sublicense, and/or sell copies of the Software, and to
+//     permit persons to whom the Software is furnished to do so, subject to the following
+//     conditions: The above copyright notice and this permission notice shall be included in
+//     all copies or substantial portions of the Software.  THE SOFTWARE IS PROVIDED "AS IS",
+//     WITHOUT WARRANTY OF ANY KIND, EXPRESS OR IMPLIED, INCLUDING BUT NOT LIMITED TO THE
+//     WARRANTIES OF MERCHANTABILITY, FITNESS FOR A PARTICULAR PURPOSE AND NONINFRINGEMENT. IN
+//     NO EVENT SHALL THE AUTHORS OR COPYRIGHT HOLDERS BE LIABLE FOR ANY CLAIM, DAMAGES OR OTHER
+//     LIABILITY, WHETHER IN AN ACTION OF CONTRACT, TORT OR OTHERWISE, ARISING FROM, OUT OF OR
+//     IN CONNECTION WITH THE SOFTWARE OR THE USE OR OTHER DEALINGS IN THE SOFTWARE.
 __device__ __forceinline__ float f_from_bits(uint32_t u) { return __uint_as_float(u); }
 
 // expm1f, branch-free: every path of the fdlibm algorithm shares the argument reduction
