@@ -249,6 +249,42 @@ __device__ __forceinline__ void epi_chunk(const GemmArgs& g, float* stg, int lan
   }
 }
 
+// The argmax epilogue of one 32-column chunk of this thread's row (output layer, src/model.rs:
+// 498-501): v = (acc * xs) * ws[col] + bias[col], then the first maximum.  The chunk's column
+// scales / biases come from the warp's staged colc (four at a time, the same address for every
+// lane); two interleaved partial maxima (4-column groups alternately) shorten the dependent
+// compare chain and merge with first-max-wins; columns >= n_store (the tail chunk) never win.
+__device__ __forceinline__ void argmax_upd(float v, uint32_t c, float& b, uint32_t& i) {
+  const bool w = v > b;
+  b = w ? v : b;
+  i = w ? c : i;
+}
+template <bool FULL>
+__device__ __forceinline__ void epi_argmax_chunk(const GemmArgs& g, const float* colc, bool cw, bool cb, float xs,
+                                                 int col0, const uint32_t (&r)[32], float& best, uint32_t& bidx) {
+  const int ncols = FULL ? 32 : min(32, g.n_store - col0);
+  float b2 = -3.40282347e+38f;
+  uint32_t i2 = 0xFFFFFFFFu;
+#pragma unroll
+  for (int j4 = 0; j4 < 8; j4++) {
+    const float4 w4 = cw ? *reinterpret_cast<const float4*>(colc + 4 * j4) : make_float4(g.ws, g.ws, g.ws, g.ws);
+    const float4 c4 = cb ? *reinterpret_cast<const float4*>(colc + 32 + 4 * j4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float wk[4] = {w4.x, w4.y, w4.z, w4.w}, bk[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const int j = 4 * j4 + k;
+      float v = dequant(static_cast<int32_t>(r[j]), xs, wk[k], bk[k]);
+      if (!FULL) v = j < ncols ? v : -__int_as_float(0x7f800000);  // never beats -FLT_MAX
+      if (j4 & 1) argmax_upd(v, static_cast<uint32_t>(col0 + j), b2, i2);
+      else argmax_upd(v, static_cast<uint32_t>(col0 + j), best, bidx);
+    }
+  }
+  // merge: the larger value wins; equal values keep the lower column
+  const bool take = b2 > best || (b2 == best && i2 < bidx);
+  best = take ? b2 : best;
+  bidx = take ? i2 : bidx;
+}
+
 // One 32 x 32 block on the TMA path: thread `lane` owns row `row` (columns col0..col0+31).
 // On entry `buf` holds the block's h values (EPI_F32_ADD); on exit it holds the output block
 // in the 128-byte-swizzled layout of the output tensor map.  Columns >= n_store and rows
@@ -461,7 +497,7 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI, EW>::THREADS, 1)
     }
     // column constants (per-channel scale, bias) of the next block, one per lane, fetched a
     // block ahead so the loads never stall the dequant
-    const bool colconst = tma_out && EPI != EPI_I32 && (g.ws_vec || g.bias);
+    const bool colconst = (tma_out || EPI == EPI_ARGMAX) && EPI != EPI_I32 && (g.ws_vec || g.bias);
     float nws = 0.0f, nbias = 0.0f;
     auto fetch_cols = [&](int cc) {
       int row, col;
@@ -524,7 +560,17 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI, EW>::THREADS, 1)
               bulk_commit();
             }
           } else {
-            epi_chunk<EPI>(g, wb, lane, rowbase, col, r, rmax, best, bidx);
+            if constexpr (EPI == EPI_ARGMAX) {
+              if (rowbase + lane < g.M) {
+                if (col + 32 <= g.n_store)
+                  epi_argmax_chunk<true>(g, colc, g.ws_vec != nullptr, g.bias != nullptr, xs_row, col, r, best, bidx);
+                else
+                  epi_argmax_chunk<false>(g, colc, g.ws_vec != nullptr, g.bias != nullptr, xs_row, col, r, best, bidx);
+              }
+              __syncwarp();  // colc is rewritten for the next chunk
+            } else {
+              epi_chunk<EPI>(g, wb, lane, rowbase, col, r, rmax, best, bidx);
+            }
           }
         }
         if constexpr (EPI == EPI_F32_ADD) {
