@@ -308,10 +308,11 @@ __device__ __forceinline__ void epi_block_tma(const GemmArgs& g, float* buf, con
 #pragma unroll
       for (int k = 0; k < 4; k++) {
         const int j = 4 * j4 + k;
-        const bool in = j < ncols;
-        v[j] = dequant(static_cast<int32_t>(r[j]), xs, in ? wk[k] : 0.0f, bk[k]);
+        // columns past n_store have zero accumulators (the weight rows past N are zero-filled
+        // by TMA) and zero staged constants; the store clips them, only the row max skips them
+        v[j] = dequant(static_cast<int32_t>(r[j]), xs, wk[k], bk[k]);
         if constexpr (EPI == EPI_F32_ROWMAX) {
-          if (in) rmax = fmaxf(rmax, fabsf(v[j]));
+          if (j < ncols) rmax = fmaxf(rmax, fabsf(v[j]));
         }
       }
     }
@@ -525,12 +526,24 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI, EW>::THREADS, 1)
       const int rowbase = m0 + q * 32;
       float rmax = 0.0f, best = -3.40282347e+38f;
       uint32_t bidx = 0xFFFFFFFFu;
-#pragma unroll 1
+      // the accumulator chunk c + 1 is read from TMEM while chunk c is processed (measured: a gain
+      // for the fp32 and 8-warp residual epilogues, a loss for the 4-warp one and the argmax)
+      constexpr bool kOverlap = EPI == EPI_F32 || (EPI == EPI_F32_ADD && EW == 8);
+      const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * BN + half * HW);
+      uint32_t ra[32], rb[32];
+      tmem_ld32_issue(trow, ra);
+      tmem_ld32_wait(ra);
+#pragma unroll(kOverlap ? CPT : 1)
       for (int c = 0; c < CPT; c++, cc++) {
         const int c0 = half * HW + 32 * c;
         const int col = n0 + c0;
-        uint32_t r[32];
-        tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * BN + c0), r);
+        uint32_t(&r)[32] = (kOverlap && (c & 1)) ? rb : ra;
+        uint32_t(&rn)[32] = (kOverlap && (c & 1)) ? ra : rb;
+        if (kOverlap && c + 1 < CPT) tmem_ld32_issue(trow + static_cast<uint32_t>(32 * (c + 1)), rn);
+        if (!kOverlap && c > 0) {
+          tmem_ld32_issue(trow + static_cast<uint32_t>(32 * c), r);
+          tmem_ld32_wait(r);
+        }
         if (colconst) {
           colc[lane] = nws;
           colc[32 + lane] = nbias;
@@ -580,6 +593,7 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI, EW>::THREADS, 1)
             prefetch_h(cc + 2 + CPT);
           }
         }
+        if (kOverlap && c + 1 < CPT) tmem_ld32_wait(rn);
       }
       if (rowbase + lane < g.M) epi_finish_row<EPI>(g, rowbase + lane, rmax, best, bidx);
       tc_fence_before();
