@@ -377,6 +377,10 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI, EW>::THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles = (g.n_store + BN - 1) / BN;
   const int tiles = n_tiles * ((g.M + Cfg::BM - 1) / Cfg::BM);
+  // tile -> (m, n) without a run-time division: q = (tile * ceil(2^40 / n_tiles)) >> 40 is exact
+  // for tile < 2^24 and n_tiles < 2^16 (the error tile / 2^40 stays below 1 / n_tiles)
+  const unsigned long long tmagic = ((1ull << 40) + static_cast<unsigned>(n_tiles) - 1) / static_cast<unsigned>(n_tiles);
+  auto tile_m = [&](int tile) { return static_cast<int>((static_cast<unsigned long long>(tile) * tmagic) >> 40); };
   const int nk = (g.K + Cfg::BK - 1) / Cfg::BK;
   const bool tma_out = g.tma_out != 0 && EPI != EPI_ARGMAX;
   const unsigned long long lim = g.wait_ns ? g.wait_ns : WAIT_LIMIT_NS;
@@ -410,7 +414,8 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI, EW>::THREADS, 1)
     if (lane == 0) {
       int kc = 0;
       for (int tile = blockIdx.x; tile < tiles && !*abort_flag && !g.idle_producer; tile += gridDim.x) {
-        const int m0 = (tile / n_tiles) * Cfg::BM, n0 = (tile % n_tiles) * BN;
+        const int tm = tile_m(tile);
+        const int m0 = tm * Cfg::BM, n0 = (tile - tm * n_tiles) * BN;
         for (int kb = 0; kb < nk; kb++, kc++) {
           const int s = kc % ST;
           if (kc >= ST && !mbar_wait(empty + s, ((kc / ST) - 1) & 1, lim)) {
@@ -470,8 +475,9 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI, EW>::THREADS, 1)
       const int k = cc / CPT;
       const int tile = blockIdx.x + k * gridDim.x;
       if (tile >= tiles) return false;
-      row = (tile / n_tiles) * Cfg::BM + q * 32;
-      col = (tile % n_tiles) * BN + half * HW + 32 * (cc - k * CPT);
+      const int tm = tile_m(tile);
+      row = tm * Cfg::BM + q * 32;
+      col = (tile - tm * n_tiles) * BN + half * HW + 32 * (cc - k * CPT);
       return col < g.n_store;
     };
     uint32_t hpar = 0, pend = 0;  // per-buffer phase parity (all lanes); loads in flight (lane 0)
@@ -511,7 +517,8 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI, EW>::THREADS, 1)
     int it = 0, cc = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, it++) {
       const int b = it & 1, u = it >> 1;
-      const int m0 = (tile / n_tiles) * Cfg::BM, n0 = (tile % n_tiles) * BN;
+      const int tm = tile_m(tile);
+      const int m0 = tm * Cfg::BM, n0 = (tile - tm * n_tiles) * BN;
       // this thread's row scale, loaded while the accumulator is still being computed
       const float xs_row = (EPI != EPI_I32 && m0 + q * 32 + lane < g.M) ? g.xs[m0 + q * 32 + lane] : 0.0f;
       const bool ok = mbar_wait(tfull + b, u & 1, lim);
