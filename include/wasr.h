@@ -189,6 +189,26 @@ int64_t wasr_ctc_collapse(const uint32_t* ids, int64_t n, uint32_t* out);
  * device floats, so tests can compare them bit for bit with the host's glibc / IEEE division. */
 int wasr_eval_math(int fn, const float* x, float* y, int n, void* stream);
 
+/* GELU + per-row int8 quantisation of a read-only device input y [m][k] (quant(gelu(f)) of
+ * src/model.rs:495-496, src/kernels.rs:11-25, without writing the GELU values back; no
+ * counterpart in the reference ABI, whose wk_gelu_quant works in place).  exact = 0 runs the
+ * engine's kernel: for k = 2048 the certified one, which evaluates GELU with a cheap
+ * approximation of bounded error, takes the row maximum from the exact GELU of the candidate
+ * elements and quantises the elements whose scaled value lies within the error bound of a
+ * rounding boundary again from the exact GELU -- the int8 row and scale are identical to the
+ * exact computation's.  exact = 1 runs the all-exact kernel.  0, -1 for a null pointer, -2
+ * for k too large, -4 for a launch failure. */
+int wasr_gelu_quant(const float* y, int m, int k, int8_t* xq, float* xs, int exact, void* stream);
+
+/* Parity hook for the certified GELU's error bound: scans the float bit patterns
+ * [start, start + count) (start + count <= 2^32) and accumulates into the device array
+ * stats[4] (zeroed by the caller): [0] the largest |g~ - g| - B |g~| over inputs where both
+ * are finite (the bits of a double), [1] inputs where the exact GELU is non-finite and the
+ * approximation finite, [2] inputs where |g~ - g| > A + B |g~|, [3] inputs where only the
+ * approximation is non-finite. */
+int wasr_gelu_cert_scan(unsigned long long start, unsigned long long count, unsigned long long* stats,
+                        void* stream);
+
 /* Measurement hook, no counterpart in the reference: the dense int8 tensor-core rate of this
  * GPU.  Launches `ctas` CTAs (one per SM) on `stream`; each issues iters x 4 back-to-back
  * tcgen05.mma kind::i8 of M = 128, N = 256, K = 32 from shared memory with no loads, i.e.

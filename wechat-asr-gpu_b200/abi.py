@@ -113,6 +113,8 @@ SIGNATURES = {
     "wasr_fbank_stream_silence": (I, [P, P]),
     "wasr_ctc_collapse": (I64, [P, I64, P]),
     "wasr_eval_math": (I, [I, P, P, I, P]),
+    "wasr_gelu_quant": (I, [P, I, I, P, P, I, P]),
+    "wasr_gelu_cert_scan": (I, [U64, U64, P, P]),
     "wasr_i8_mma_peak": (I, [I, I, P, P]),
     "wasr_version": (C.c_char_p, []),
 }

@@ -545,6 +545,32 @@ __device__ __forceinline__ float2 gelu_ref2(float2 x) {
   return pmul2(pmul2(f2c(0.5f), x), sadd2(f2c(1.0f), tanhf_ref2(u)));
 }
 
+// ---- certified approximate GELU.  The GELU output is consumed only by its row's int8
+// quantisation (src/model.rs:495-496: quant(gelu(f))), so the quantised row equals the exact
+// one whenever (a) the row maximum is taken from exact values and (b) no element's scaled value
+// lies within the approximation's error of a rounding boundary.  gelu_fast2 takes the same
+// rounded steps as gelu_ref2 for 0.5*x, the cubic and the tanh argument u, and replaces
+// tanhf(u) by sign(u) (1 - 2 / (1 + 2^(2|u|/ln 2))) from the hardware exp2 and reciprocal
+// approximations.  For every float x with gelu_ref(x) finite:
+//     gelu_fast(x) finite  =>  |gelu_fast(x) - gelu_ref(x)| <= GELU_CERT_A + GELU_CERT_B |gelu_fast(x)|
+//     gelu_fast(x) non-finite is allowed (the kernel then runs the row exactly),
+// and gelu_fast(x) is non-finite wherever gelu_ref(x) is.  Checked on all 2^32 inputs on the
+// GPU (wasr_gelu_cert_scan).
+constexpr float GELU_CERT_A = 0x1p-19f;
+constexpr float GELU_CERT_B = 0x1p-22f;
+__device__ __forceinline__ float2 gelu_fast2(float2 x) {
+  const float2 c = pmul2(pmul2(pmul2(f2c(0.044715f), x), x), x);
+  const float2 u = pmul2(f2c(0.7978846f), sadd2(x, c));
+  const float2 a = pmul2(make_float2(fabsf(u.x), fabsf(u.y)), f2c(2.88539008f));  // 2|u| / ln 2
+  float ex, ey, rx, ry;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(ex) : "f"(a.x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(ey) : "f"(a.y));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(rx) : "f"(__fadd_rn(1.0f, ex)));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(ry) : "f"(__fadd_rn(1.0f, ey)));
+  const float tx = copysignf(__fmaf_rn(-2.0f, rx, 1.0f), u.x), ty = copysignf(__fmaf_rn(-2.0f, ry, 1.0f), u.y);
+  return pmul2(pmul2(f2c(0.5f), x), sadd2(f2c(1.0f), make_float2(tx, ty)));
+}
+
 // a / b rounded to nearest for a in [0, 1] and b in [1, 2^24) (a softmax numerator and row
 // sum), given yb = __frcp_rn(b): Markstein's correction (P. Markstein, IBM J. Res. Dev. 34(1),
 // 1990, "Computation of elementary functions on the IBM RISC System/6000 processor"): with yb

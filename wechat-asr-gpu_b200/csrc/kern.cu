@@ -805,6 +805,151 @@ __global__ void __launch_bounds__(256) gelu_quant_ro_k(const float* __restrict__
   if (lane == 0) xs[row] = sc;
 }
 
+// One row of GELU + quant done exactly by warp `lane`s (two passes of gelu_ref over the
+// row): the certified kernel's path for rows holding a non-finite approximate value.
+__device__ __noinline__ void gelu_quant_row_exact(const float* __restrict__ r, int k, int lane, int8_t* __restrict__ q,
+                                                  float* __restrict__ xs) {
+  float mx = 0.0f;
+  for (int j = lane; j < k; j += 32) mx = fmaxf(mx, fabsf(gelu_ref(r[j])));
+  mx = warp_max(mx);
+  const float sc = quant_scale(mx), inv = quant_inv(sc);
+  for (int j = lane; j < k; j += 32) q[j] = quant_one(gelu_ref(r[j]), inv);
+  if (lane == 0) *xs = sc;
+}
+
+// GELU + per-row quant with the certified approximation (gelu_fast2, common.cuh): one warp per
+// row of k = 128 NV columns, lane l holding columns 4l + 128i + c in registers.
+//  1. g~ = gelu_fast(x) for the row, its maximum mt.  Every |g~ - g| <= E = A + B mt.
+//  2. The exact maximum M = max |g| is attained at an element with |g~| >= mt - 2E (it has
+//     |g| >= |g~_a| - E = mt - E for the approximate argmax a, so |g~| >= mt - 2E); every other
+//     element has |g| < mt - E <= M.  So M is the maximum of gelu_ref over those candidates
+//     (usually one element), and sc, inv follow from it exactly as in quant.
+//  3. v~ = RN(g~ * inv) differs from the exact v = RN(g * inv) by at most D = E inv + 2^-16
+//     (the two half-ulps of values below 128).  If the distance of v~ to its nearest integer is
+//     below 1/2 - D, no rounding boundary (a half-integer) lies within D of v~, so round(v) =
+//     round(v~) = rint(v~), and |v| <= 127 needs no clamp.  The other elements (rare) are
+//     quantised again from gelu_ref.
+// The int8 row and its scale are therefore identical to quant(gelu(x)) on every input.
+template <int NV>
+__global__ void __launch_bounds__(256) gelu_quant_cert_k(const float* __restrict__ y, int m, int8_t* __restrict__ xq,
+                                                         float* __restrict__ xs) {
+  static_assert(NV >= 1 && NV <= 16, "a lane's candidate mask holds 64 elements");
+  constexpr int K = 128 * NV;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  if (row >= m) return;
+  const float* r = y + static_cast<int64_t>(row) * K + 4 * lane;
+  int8_t* q = xq + static_cast<int64_t>(row) * K + 4 * lane;
+  float g[NV][4];
+#pragma unroll
+  for (int i = 0; i < NV; i++) {
+    const float4 v = __ldcs(reinterpret_cast<const float4*>(r + 128 * i));
+    g[i][0] = v.x, g[i][1] = v.y, g[i][2] = v.z, g[i][3] = v.w;
+  }
+  float mt = 0.0f;
+  bool bad = false;
+#pragma unroll
+  for (int i = 0; i < NV; i++)
+#pragma unroll
+    for (int c = 0; c < 4; c += 2) {
+      const float2 v = gelu_fast2(make_float2(g[i][c], g[i][c + 1]));
+      g[i][c] = v.x, g[i][c + 1] = v.y;
+      mt = fmaxf(mt, fmaxf(fabsf(v.x), fabsf(v.y)));
+      bad |= !(fabsf(v.x) <= 3.40282347e+38f) || !(fabsf(v.y) <= 3.40282347e+38f);
+    }
+  if (__any_sync(0xffffffffu, bad)) {
+    gelu_quant_row_exact(y + static_cast<int64_t>(row) * K, K, lane, xq + static_cast<int64_t>(row) * K, xs + row);
+    return;
+  }
+  const float lane_mt = mt;
+  mt = warp_max(mt);
+  const float E = __fmaf_ru(GELU_CERT_B, mt, GELU_CERT_A);
+  const float L = __fsub_rd(mt, __fmul_ru(2.0f, E));
+  float mx = 0.0f;
+  if (lane_mt >= L) {  // this lane holds candidates for the maximum
+    unsigned long long cand = 0;
+#pragma unroll
+    for (int i = 0; i < NV; i++)
+#pragma unroll
+      for (int c = 0; c < 4; c++) cand |= static_cast<unsigned long long>(fabsf(g[i][c]) >= L) << (4 * i + c);
+    while (cand) {
+      const int b = __ffsll(static_cast<long long>(cand)) - 1;
+      cand &= cand - 1;
+      mx = fmaxf(mx, fabsf(gelu_ref(r[128 * (b >> 2) + (b & 3)])));
+    }
+  }
+  mx = warp_max(mx);
+  const float sc = quant_scale(mx), inv = quant_inv(sc);
+  const float lim = __fsub_rd(0.5f, __fadd_ru(__fmul_ru(E, inv), 0x1p-16f));
+  bool amb = false;
+#pragma unroll
+  for (int i = 0; i < NV; i++) {
+    int qi[4];
+#pragma unroll
+    for (int c = 0; c < 4; c += 2) {
+      const float2 v = mul2_rn(make_float2(g[i][c], g[i][c + 1]), f2c(inv));
+      const float r0 = rintf(v.x), r1 = rintf(v.y);
+      amb |= (fabsf(__fsub_rn(v.x, r0)) >= lim) || (fabsf(__fsub_rn(v.y, r1)) >= lim);
+      qi[c] = __float2int_rz(r0), qi[c + 1] = __float2int_rz(r1);
+    }
+    const uint32_t p = __byte_perm(__byte_perm(qi[0], qi[1], 0x0040), __byte_perm(qi[2], qi[3], 0x0040), 0x5410);
+    *reinterpret_cast<uint32_t*>(q + 128 * i) = p;
+  }
+  if (lane == 0) xs[row] = sc;
+  if (amb) {  // quantise the elements near a rounding boundary again from the exact GELU
+    unsigned long long mask = 0;
+#pragma unroll
+    for (int i = 0; i < NV; i++)
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        const float v = __fmul_rn(g[i][c], inv);
+        mask |= static_cast<unsigned long long>(fabsf(__fsub_rn(v, rintf(v))) >= lim) << (4 * i + c);
+      }
+    while (mask) {
+      const int b = __ffsll(static_cast<long long>(mask)) - 1;
+      mask &= mask - 1;
+      const int col = 128 * (b >> 2) + (b & 3);
+      q[col] = quant_one(gelu_ref(r[col]), inv);
+    }
+  }
+}
+
+// Exhaustive check of the bound gelu_quant_cert_k relies on, over the float bit patterns
+// [start, start + count): stats[0] = max over inputs with both values finite of
+// |g~ - g| - GELU_CERT_B |g~| (a non-negative double's bits, 0 when none exceeds 0);
+// stats[1] = inputs where gelu_ref is non-finite and gelu_fast finite; stats[2] = inputs with
+// both finite and |g~ - g| > GELU_CERT_A + GELU_CERT_B |g~|; stats[3] = inputs where gelu_fast
+// is non-finite and gelu_ref finite (allowed: such rows run exactly).
+__global__ void gelu_cert_scan_k(unsigned long long start, unsigned long long count,
+                                 unsigned long long* __restrict__ stats) {
+  double worst = 0.0;
+  unsigned long long n_nf = 0, n_viol = 0, n_fast_nf = 0;
+  const unsigned long long stride = 2ull * gridDim.x * blockDim.x;
+  for (unsigned long long i = 2ull * (blockIdx.x * blockDim.x + threadIdx.x); i < count; i += stride) {
+    const float x0 = __uint_as_float(static_cast<uint32_t>(start + i));
+    const float x1 = __uint_as_float(static_cast<uint32_t>(start + min(i + 1, count - 1)));
+    const float2 gf = gelu_fast2(make_float2(x0, x1));
+    const float gx[2] = {gelu_ref(x0), gelu_ref(x1)}, fx[2] = {gf.x, gf.y};
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+      const bool fin_r = fabsf(gx[u]) <= 3.40282347e+38f, fin_f = fabsf(fx[u]) <= 3.40282347e+38f;
+      if (!fin_r && fin_f) n_nf++;
+      if (fin_r && !fin_f) n_fast_nf++;
+      if (fin_r && fin_f) {
+        const double err = fabs(static_cast<double>(fx[u]) - static_cast<double>(gx[u]));
+        const double rel = static_cast<double>(GELU_CERT_B) * fabs(static_cast<double>(fx[u]));
+        worst = fmax(worst, err - rel);
+        if (err > static_cast<double>(GELU_CERT_A) + rel) n_viol++;
+      }
+      if (i + 1 >= count) break;
+    }
+  }
+  atomicMax(stats, static_cast<unsigned long long>(__double_as_longlong(worst)));
+  if (n_nf) atomicAdd(stats + 1, n_nf);
+  if (n_viol) atomicAdd(stats + 2, n_viol);
+  if (n_fast_nf) atomicAdd(stats + 3, n_fast_nf);
+}
+
 __global__ void add_k(float* __restrict__ h, const float* __restrict__ a, size_t n) {
   const size_t i = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
   if (i + 3 < n && ((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(a)) & 15) == 0) {
@@ -1318,8 +1463,15 @@ int launch_gelu_quant(float* x, int m, int k, int8_t* xq, float* xs, cudaStream_
   gelu_quant_k<<<(m + 7) / 8, 256, 0, st>>>(x, m, k, xq, xs);
   return launched();
 }
-int launch_gelu_quant_ro(const float* y, int m, int k, int8_t* xq, float* xs, cudaStream_t st) {
+// GELU + quant of a read-only [m][k] input: the certified kernel for the model's FF width (rows of
+// 2048 floats, 16-byte aligned), the all-exact kernel otherwise or when `exact` is set.
+int launch_gelu_quant_ro(const float* y, int m, int k, int8_t* xq, float* xs, cudaStream_t st, bool exact) {
   if (m <= 0 || k <= 0) return 0;
+  if (!exact && k == 16 * 128 && (reinterpret_cast<uintptr_t>(y) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(xq) & 3) == 0) {
+    gelu_quant_cert_k<16><<<(m + 7) / 8, 256, 0, st>>>(y, m, xq, xs);
+    return launched();
+  }
   const size_t smem = static_cast<size_t>(GQ_ROWS) * k * sizeof(float);
   if (smem > 227 * 1024) return -2;
   set_smem(reinterpret_cast<const void*>(gelu_quant_ro_k), 227 * 1024);
@@ -1482,6 +1634,20 @@ int wk_attention_cublas_part(int part, void* stream, const float* q, const float
   (void)scratch;
   if (part == 0 || part == 1) return 0;
   return attention_abi(stream, q, k, v, t, d, heads, out);
+}
+
+// Parity hooks for the certified GELU + quant: the engine's kernel choice (exact = 0) or the
+// all-exact kernel (exact = 1) on a read-only [m][k] input; and the exhaustive bound scan.
+int wasr_gelu_quant(const float* y, int m, int k, int8_t* xq, float* xs, int exact, void* stream) {
+  if (!y || !xq || !xs) return -1;
+  return launch_gelu_quant_ro(y, m, k, xq, xs, static_cast<cudaStream_t>(stream), exact != 0);
+}
+int wasr_gelu_cert_scan(unsigned long long start, unsigned long long count, unsigned long long* stats,
+                        void* stream) {
+  if (!stats || start + count > (1ull << 32)) return -1;
+  if (count == 0) return 0;
+  gelu_cert_scan_k<<<148 * 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(start, count, stats);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 
 // Parity hook: evaluate the device restatements of the libm functions the reference calls

@@ -60,7 +60,7 @@ int launch_ln_quant(float* h, const float* o, const float* g, const float* b, in
                     cudaStream_t st);
 int launch_gelu_quant(float* x, int m, int k, int8_t* xq, float* xs, cudaStream_t st);
 // GELU + per-row quant of a read-only input (the GELU values are not written back)
-int launch_gelu_quant_ro(const float* y, int m, int k, int8_t* xq, float* xs, cudaStream_t st);
+int launch_gelu_quant_ro(const float* y, int m, int k, int8_t* xq, float* xs, cudaStream_t st, bool exact = false);
 int launch_add(float* h, const float* a, size_t n, cudaStream_t st);
 int launch_argmax_rows(const float* x, int m, int n, uint32_t* out, cudaStream_t st);
 int launch_keys_to_ids(const unsigned long long* keys, int m, uint32_t* ids, cudaStream_t st);
