@@ -200,12 +200,14 @@ int wasr_eval_math(int fn, const float* x, float* y, int n, void* stream);
  * for k too large, -4 for a launch failure. */
 int wasr_gelu_quant(const float* y, int m, int k, int8_t* xq, float* xs, int exact, void* stream);
 
-/* Parity hook for the certified GELU's error bound: scans the float bit patterns
- * [start, start + count) (start + count <= 2^32) and accumulates into the device array
- * stats[4] (zeroed by the caller): [0] the largest |g~ - g| - B |g~| over inputs where both
- * are finite (the bits of a double), [1] inputs where the exact GELU is non-finite and the
- * approximation finite, [2] inputs where |g~ - g| > A + B |g~|, [3] inputs where only the
- * approximation is non-finite. */
+/* Parity hook for the certified GELU: scans the float bit patterns [start, start + count)
+ * (both even, start + count <= 2^32) and accumulates into the device array stats[8] (zeroed by
+ * the caller), with g~ the approximation and g the exact GELU: [0] the largest |g~ - g| - B |g~|
+ * over inputs where both are finite (the bits of a double), [1] inputs where g is non-finite and
+ * g~ finite, [2] inputs where |g~ - g| > A + B |g~|, [3] inputs where only g~ is non-finite,
+ * [4] the largest |g~ - g| / |g~| over |g~| >= 2^-20 and [5] the largest |g~ - g| below it
+ * (double bits), [6] adjacent floats 0 <= x < x' <= inf with g(x') < g(x), [7] the largest
+ * |g(x)| over non-NaN x < 0 (double bits).  0, or -1 for bad arguments. */
 int wasr_gelu_cert_scan(unsigned long long start, unsigned long long count, unsigned long long* stats,
                         void* stream);
 

@@ -34,16 +34,21 @@ def _check(L, dev, orc, x):
 
 
 def test_gelu_cert_bound_on_every_float(gpu_lib, dev):
-    """|gelu_fast(x) - gelu(x)| <= A + B |gelu_fast(x)| on all 2^32 inputs where both are finite,
-    and the approximation is non-finite wherever the exact GELU is."""
+    """On all 2^32 inputs: |gelu_fast(x) - gelu(x)| <= A + B |gelu_fast(x)| where both are finite;
+    the approximation is non-finite wherever the exact GELU is; the exact GELU is non-decreasing
+    on [0, inf] and at most 0.171 in magnitude below 0 (the kernel's exact row maximum)."""
     L = gpu_lib
-    stats = dev.put(np.zeros(4, np.uint64))
+    stats = dev.put(np.zeros(8, np.uint64))
     assert L.wasr_gelu_cert_scan(0, 1 << 32, stats, None) == 0
-    st = dev.get(stats, (4,), np.uint64)
-    worst = st[:1].view(np.float64)[0]
-    print(f"gelu cert scan: max |g~ - g| - B|g~| = {worst:.3e}; only-approx-non-finite inputs {int(st[3])}")
+    st = dev.get(stats, (8,), np.uint64)
+    f = st.view(np.float64)
+    print(f"gelu cert scan: max |g~ - g| - B|g~| = {f[0]:.3e}; max rel err (|g~| >= 1/16) {f[4]:.3e}; "
+          f"max abs err (|g~| < 1/16) {f[5]:.3e}; max |g| below 0 {f[7]:.6f}; "
+          f"only-approx-non-finite inputs {int(st[3])}")
     assert int(st[1]) == 0, "exact GELU non-finite where the approximation is finite"
-    assert int(st[2]) == 0, f"bound exceeded on {int(st[2])} inputs (worst excess {worst:.3e})"
+    assert int(st[2]) == 0, f"bound exceeded on {int(st[2])} inputs (worst excess {f[0]:.3e})"
+    assert int(st[6]) == 0, f"exact GELU decreases between {int(st[6])} adjacent non-negative floats"
+    assert f[7] <= 0.171, f"|gelu| below 0 reaches {f[7]}"
 
 
 @pytest.mark.parametrize("sigma", [0.5, 1.0, 2.0, 4.0])
@@ -100,8 +105,9 @@ def test_gelu_cert_near_tied_maxima(gpu_lib, dev, orc):
 
 def test_gelu_cert_special_rows(gpu_lib, dev, orc):
     """Rows with NaN / inf / huge values (the exact-row path), rows whose GELU vanishes or is
-    tiny everywhere (every element a candidate and near a boundary), an all-zero row, and a row
-    count that is not a multiple of the block's 8 rows."""
+    tiny everywhere (every element a candidate and near a boundary), an all-zero row, rows whose
+    largest |gelu| lies on the negative side or just above it, and a row count that is not a
+    multiple of the block's 8 rows."""
     rng = np.random.default_rng(9)
     x = rng.standard_normal((13, K)).astype(np.float32)
     x[0, 5] = np.nan
@@ -113,4 +119,6 @@ def test_gelu_cert_special_rows(gpu_lib, dev, orc):
     x[6, :] = 0.0
     x[7, :] = rng.uniform(-1e-30, 1e-30, K).astype(np.float32)
     x[8, :] = -x[8, :] ** 2 - 3.0
+    x[9, :] = rng.uniform(-2.0, 0.28, K).astype(np.float32)   # largest |gelu| on the negative side
+    x[10, :] = rng.uniform(-1.0, 0.4, K).astype(np.float32)   # largest |gelu| just above 0.171
     _check(gpu_lib, dev, orc, x)

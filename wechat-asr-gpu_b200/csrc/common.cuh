@@ -545,32 +545,6 @@ __device__ __forceinline__ float2 gelu_ref2(float2 x) {
   return pmul2(pmul2(f2c(0.5f), x), sadd2(f2c(1.0f), tanhf_ref2(u)));
 }
 
-// ---- certified approximate GELU.  The GELU output is consumed only by its row's int8
-// quantisation (src/model.rs:495-496: quant(gelu(f))), so the quantised row equals the exact
-// one whenever (a) the row maximum is taken from exact values and (b) no element's scaled value
-// lies within the approximation's error of a rounding boundary.  gelu_fast2 takes the same
-// rounded steps as gelu_ref2 for 0.5*x, the cubic and the tanh argument u, and replaces
-// tanhf(u) by sign(u) (1 - 2 / (1 + 2^(2|u|/ln 2))) from the hardware exp2 and reciprocal
-// approximations.  For every float x with gelu_ref(x) finite:
-//     gelu_fast(x) finite  =>  |gelu_fast(x) - gelu_ref(x)| <= GELU_CERT_A + GELU_CERT_B |gelu_fast(x)|
-//     gelu_fast(x) non-finite is allowed (the kernel then runs the row exactly),
-// and gelu_fast(x) is non-finite wherever gelu_ref(x) is.  Checked on all 2^32 inputs on the
-// GPU (wasr_gelu_cert_scan).
-constexpr float GELU_CERT_A = 0x1p-19f;
-constexpr float GELU_CERT_B = 0x1p-22f;
-__device__ __forceinline__ float2 gelu_fast2(float2 x) {
-  const float2 c = pmul2(pmul2(pmul2(f2c(0.044715f), x), x), x);
-  const float2 u = pmul2(f2c(0.7978846f), sadd2(x, c));
-  const float2 a = pmul2(make_float2(fabsf(u.x), fabsf(u.y)), f2c(2.88539008f));  // 2|u| / ln 2
-  float ex, ey, rx, ry;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(ex) : "f"(a.x));
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(ey) : "f"(a.y));
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(rx) : "f"(__fadd_rn(1.0f, ex)));
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(ry) : "f"(__fadd_rn(1.0f, ey)));
-  const float tx = copysignf(__fmaf_rn(-2.0f, rx, 1.0f), u.x), ty = copysignf(__fmaf_rn(-2.0f, ry, 1.0f), u.y);
-  return pmul2(pmul2(f2c(0.5f), x), sadd2(f2c(1.0f), make_float2(tx, ty)));
-}
-
 // a / b rounded to nearest for a in [0, 1] and b in [1, 2^24) (a softmax numerator and row
 // sum), given yb = __frcp_rn(b): Markstein's correction (P. Markstein, IBM J. Res. Dev. 34(1),
 // 1990, "Computation of elementary functions on the IBM RISC System/6000 processor"): with yb
@@ -612,6 +586,40 @@ __device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
   unsigned long long r;
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
   return bits_f2(r);
+}
+
+// ---- certified approximate GELU.  The GELU output is consumed only by its row's int8
+// quantisation (src/model.rs:495-496: quant(gelu(f))), so the quantised row equals the exact
+// one whenever (a) the row maximum is taken from exact values and (b) no element's scaled value
+// lies within the approximation's error of a rounding boundary.  gelu_fast2 evaluates
+// 0.5 x (1 + tanh u) = x / (1 + e^(-2u)), u = 0.7978846 (x + 0.044715 x^3), as
+// x * rcp(1 + 2^(x (k1 + k3 x^2))) with k1 = -2 * 0.7978846 / ln 2, k3 = 0.044715 k1, from the
+// hardware exp2 and reciprocal approximations.  For every float x with gelu_ref(x) finite:
+//     gelu_fast(x) finite  =>  |gelu_fast(x) - gelu_ref(x)| <= GELU_CERT_A + GELU_CERT_B |gelu_fast(x)|
+//     gelu_fast(x) non-finite is allowed (the kernel then runs the row exactly),
+// and gelu_fast(x) is non-finite wherever gelu_ref(x) is.  Checked on all 2^32 inputs on the
+// GPU (wasr_gelu_cert_scan).
+constexpr float GELU_CERT_A = 0x1p-23f;
+constexpr float GELU_CERT_B = 0x1p-21f;
+// |gelu_ref(x)| <= GELU_NEG_MAX for every x < 0, and gelu_ref is non-decreasing on [0, inf]
+// (both checked on every float by wasr_gelu_cert_scan)
+constexpr float GELU_NEG_MAX = 0.171f;
+// packed fused multiply-add, one rounding per element
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+  return bits_f2(r);
+}
+__device__ __forceinline__ float2 gelu_fast2(float2 x) {
+  const float2 x2 = pmul2(x, x);
+  const float2 a = pmul2(fma2_rn(x2, f2c(-0x1.a5a7d0p-4f), f2c(-0x1.26aec4p+1f)), x);  // -2u / ln 2
+  float ex, ey, rx, ry;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(ex) : "f"(a.x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(ey) : "f"(a.y));
+  const float2 d = add2_rn(f2c(1.0f), make_float2(ex, ey));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(rx) : "f"(d.x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(ry) : "f"(d.y));
+  return pmul2(x, make_float2(rx, ry));
 }
 
 // Order-preserving map of a float to uint32 (for packed argmax keys).

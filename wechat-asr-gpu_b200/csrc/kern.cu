@@ -819,117 +819,156 @@ __device__ __noinline__ void gelu_quant_row_exact(const float* __restrict__ r, i
 
 // GELU + per-row quant with the certified approximation (gelu_fast2, common.cuh): one warp per
 // row of k = 128 NV columns, lane l holding columns 4l + 128i + c in registers.
-//  1. g~ = gelu_fast(x) for the row, its maximum mt.  Every |g~ - g| <= E = A + B mt.
-//  2. The exact maximum M = max |g| is attained at an element with |g~| >= mt - 2E (it has
-//     |g| >= |g~_a| - E = mt - E for the approximate argmax a, so |g~| >= mt - 2E); every other
-//     element has |g| < mt - E <= M.  So M is the maximum of gelu_ref over those candidates
-//     (usually one element), and sc, inv follow from it exactly as in quant.
-//  3. v~ = RN(g~ * inv) differs from the exact v = RN(g * inv) by at most D = E inv + 2^-16
-//     (the two half-ulps of values below 128).  If the distance of v~ to its nearest integer is
-//     below 1/2 - D, no rounding boundary (a half-integer) lies within D of v~, so round(v) =
-//     round(v~) = rint(v~), and |v| <= 127 needs no clamp.  The other elements (rare) are
+//  1. g~ = gelu_fast(x) for the row, and max x.
+//  2. The exact maximum M = max |g|: gelu_ref is non-decreasing on [0, inf] and |gelu_ref| <=
+//     GELU_NEG_MAX below 0 (both checked on every float), so M = gelu_ref(max x) whenever that is
+//     >= GELU_NEG_MAX.  Otherwise (rows of small or negative values) M is attained at an element
+//     with |g~| >= mt - 2E, mt = max |g~|, E = A + B mt (it has |g| >= |g~_a| - E = mt - E for
+//     the approximate argmax a, so |g~| >= mt - 2E; every other element has |g| < mt - E <= M),
+//     and is the maximum of gelu_ref over those candidates.  sc, inv follow from M as in quant,
+//     and every |g~ - g| <= E = A + B (M + A)(1 + 2B), since |g~| <= (M + A) / (1 - B).
+//  3. With w = g~ * inv (exact real product), the exact v = RN(g * inv) lies within
+//     E inv + 2^-18 of w (half an ulp of values below 128).  s = fma(g~, inv, 1.5 * 2^23) rounds
+//     w to the nearest integer n (ties to even), held in the low mantissa bits of s for
+//     |w| < 2^22; n = s - 1.5 * 2^23 exactly, and d = fma(g~, inv, -n) is w - n within 2^-25.
+//     If |d| < lim = 1/2 - (E inv + 2^-16), then |v - n| < 1/2: round(v) = n, and |v| <= 127
+//     needs no clamp; the low byte of s's bits is n as an int8, without conversions.  The other
+//     elements (rare; every element of a row whose bound reaches 1/2, and NaN distances) are
 //     quantised again from gelu_ref.
 // The int8 row and its scale are therefore identical to quant(gelu(x)) on every input.
+// Persistent warps: each takes rows w, w + W, ...; while it works on one row, the next streams
+// into the other half of its two-row shared-memory buffer by cp.async (each lane copies and
+// later reads only its own 16-byte pieces, so no synchronisation beyond the copy wait).
+constexpr float GQ_MAGIC = 12582912.0f;  // 1.5 * 2^23
+constexpr int GQ_WARPS = 4;              // warps per block
 template <int NV>
-__global__ void __launch_bounds__(256) gelu_quant_cert_k(const float* __restrict__ y, int m, int8_t* __restrict__ xq,
-                                                         float* __restrict__ xs) {
+__global__ void __launch_bounds__(32 * GQ_WARPS, 3) gelu_quant_cert_k(const float* __restrict__ y, int m,
+                                                                      int8_t* __restrict__ xq,
+                                                                      float* __restrict__ xs) {
   static_assert(NV >= 1 && NV <= 16, "a lane's candidate mask holds 64 elements");
   constexpr int K = 128 * NV;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * 8 + warp;
-  if (row >= m) return;
-  const float* r = y + static_cast<int64_t>(row) * K + 4 * lane;
-  int8_t* q = xq + static_cast<int64_t>(row) * K + 4 * lane;
-  float g[NV][4];
+  extern __shared__ __align__(16) float gq_sm[];
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5, nwarps = gridDim.x * GQ_WARPS;
+  float* buf = gq_sm + wib * 2 * K + 4 * lane;  // [2][K] per warp, this lane's columns
+  int row = blockIdx.x * GQ_WARPS + wib;
+  if (row < m) {
 #pragma unroll
-  for (int i = 0; i < NV; i++) {
-    const float4 v = __ldcs(reinterpret_cast<const float4*>(r + 128 * i));
-    g[i][0] = v.x, g[i][1] = v.y, g[i][2] = v.z, g[i][3] = v.w;
+    for (int i = 0; i < NV; i++) cp_async16(buf + 128 * i, y + static_cast<int64_t>(row) * K + 4 * lane + 128 * i);
   }
-  float mt = 0.0f;
-  bool bad = false;
+  cp_async_commit();
+  for (int it = 0; row < m; row += nwarps, it ^= 1) {
+    cp_async_wait<0>();
+    if (row + nwarps < m) {
 #pragma unroll
-  for (int i = 0; i < NV; i++)
-#pragma unroll
-    for (int c = 0; c < 4; c += 2) {
-      const float2 v = gelu_fast2(make_float2(g[i][c], g[i][c + 1]));
-      g[i][c] = v.x, g[i][c + 1] = v.y;
-      mt = fmaxf(mt, fmaxf(fabsf(v.x), fabsf(v.y)));
-      bad |= !(fabsf(v.x) <= 3.40282347e+38f) || !(fabsf(v.y) <= 3.40282347e+38f);
+      for (int i = 0; i < NV; i++)
+        cp_async16(buf + (it ^ 1) * K + 128 * i, y + static_cast<int64_t>(row + nwarps) * K + 4 * lane + 128 * i);
     }
-  if (__any_sync(0xffffffffu, bad)) {
-    gelu_quant_row_exact(y + static_cast<int64_t>(row) * K, K, lane, xq + static_cast<int64_t>(row) * K, xs + row);
-    return;
-  }
-  const float lane_mt = mt;
-  mt = warp_max(mt);
-  const float E = __fmaf_ru(GELU_CERT_B, mt, GELU_CERT_A);
-  const float L = __fsub_rd(mt, __fmul_ru(2.0f, E));
-  float mx = 0.0f;
-  if (lane_mt >= L) {  // this lane holds candidates for the maximum
-    unsigned long long cand = 0;
+    cp_async_commit();
+    const float* r = y + static_cast<int64_t>(row) * K + 4 * lane;
+    int8_t* q = xq + static_cast<int64_t>(row) * K + 4 * lane;
+    float g[NV][4];
+    float xm = -3.40282347e+38f;
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      const float4 v = *reinterpret_cast<const float4*>(buf + it * K + 128 * i);
+      g[i][0] = v.x, g[i][1] = v.y, g[i][2] = v.z, g[i][3] = v.w;
+      xm = fmaxf(fmaxf(xm, fmaxf(v.x, v.y)), fmaxf(v.z, v.w));
+    }
+    float2 chk = make_float2(0.0f, 0.0f);  // stays 0 unless some g~ is inf or NaN (inf * 0 = NaN)
 #pragma unroll
     for (int i = 0; i < NV; i++)
 #pragma unroll
-      for (int c = 0; c < 4; c++) cand |= static_cast<unsigned long long>(fabsf(g[i][c]) >= L) << (4 * i + c);
-    while (cand) {
-      const int b = __ffsll(static_cast<long long>(cand)) - 1;
-      cand &= cand - 1;
-      mx = fmaxf(mx, fabsf(gelu_ref(r[128 * (b >> 2) + (b & 3)])));
-    }
-  }
-  mx = warp_max(mx);
-  const float sc = quant_scale(mx), inv = quant_inv(sc);
-  const float lim = __fsub_rd(0.5f, __fadd_ru(__fmul_ru(E, inv), 0x1p-16f));
-  bool amb = false;
-#pragma unroll
-  for (int i = 0; i < NV; i++) {
-    int qi[4];
-#pragma unroll
-    for (int c = 0; c < 4; c += 2) {
-      const float2 v = mul2_rn(make_float2(g[i][c], g[i][c + 1]), f2c(inv));
-      const float r0 = rintf(v.x), r1 = rintf(v.y);
-      amb |= (fabsf(__fsub_rn(v.x, r0)) >= lim) || (fabsf(__fsub_rn(v.y, r1)) >= lim);
-      qi[c] = __float2int_rz(r0), qi[c + 1] = __float2int_rz(r1);
-    }
-    const uint32_t p = __byte_perm(__byte_perm(qi[0], qi[1], 0x0040), __byte_perm(qi[2], qi[3], 0x0040), 0x5410);
-    *reinterpret_cast<uint32_t*>(q + 128 * i) = p;
-  }
-  if (lane == 0) xs[row] = sc;
-  if (amb) {  // quantise the elements near a rounding boundary again from the exact GELU
-    unsigned long long mask = 0;
-#pragma unroll
-    for (int i = 0; i < NV; i++)
-#pragma unroll
-      for (int c = 0; c < 4; c++) {
-        const float v = __fmul_rn(g[i][c], inv);
-        mask |= static_cast<unsigned long long>(fabsf(__fsub_rn(v, rintf(v))) >= lim) << (4 * i + c);
+      for (int c = 0; c < 4; c += 2) {
+        const float2 v = gelu_fast2(make_float2(g[i][c], g[i][c + 1]));
+        g[i][c] = v.x, g[i][c + 1] = v.y;
+        chk = fma2_rn(v, f2c(0.0f), chk);
       }
-    while (mask) {
-      const int b = __ffsll(static_cast<long long>(mask)) - 1;
-      mask &= mask - 1;
-      const int col = 128 * (b >> 2) + (b & 3);
-      q[col] = quant_one(gelu_ref(r[col]), inv);
+    if (__any_sync(0xffffffffu, !(chk.x == 0.0f) || !(chk.y == 0.0f))) {
+      gelu_quant_row_exact(y + static_cast<int64_t>(row) * K, K, lane, xq + static_cast<int64_t>(row) * K, xs + row);
+      continue;
+    }
+    float mx = gelu_ref(warp_max(xm));
+    if (!(mx >= GELU_NEG_MAX)) {  // the maximum from the exact GELU of the candidates
+      float mt = 0.0f;
+#pragma unroll
+      for (int i = 0; i < NV; i++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) mt = fmaxf(mt, fabsf(g[i][c]));
+      const float lane_mt = mt;
+      mt = warp_max(mt);
+      const float L = __fsub_rd(mt, __fmul_ru(2.0f, __fmaf_ru(GELU_CERT_B, mt, GELU_CERT_A)));
+      mx = 0.0f;
+      if (lane_mt >= L) {  // this lane holds candidates
+        unsigned long long cand = 0;
+#pragma unroll
+        for (int i = 0; i < NV; i++)
+#pragma unroll
+          for (int c = 0; c < 4; c++) cand |= static_cast<unsigned long long>(fabsf(g[i][c]) >= L) << (4 * i + c);
+        while (cand) {
+          const int b = __ffsll(static_cast<long long>(cand)) - 1;
+          cand &= cand - 1;
+          mx = fmaxf(mx, fabsf(gelu_ref(r[128 * (b >> 2) + (b & 3)])));
+        }
+      }
+      mx = warp_max(mx);
+    }
+    const float E = __fmaf_ru(GELU_CERT_B, __fmul_ru(__fadd_ru(mx, GELU_CERT_A), 1.0f + 2.0f * GELU_CERT_B), GELU_CERT_A);
+    const float sc = quant_scale(mx), inv = quant_inv(sc);
+    const float lim = __fsub_rd(0.5f, __fadd_ru(__fmul_ru(E, inv), 0x1p-16f));
+    bool amb = false;
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      uint32_t b[4];
+#pragma unroll
+      for (int c = 0; c < 4; c += 2) {
+        const float2 gg = make_float2(g[i][c], g[i][c + 1]);
+        const float2 sv = fma2_rn(gg, f2c(inv), f2c(GQ_MAGIC));
+        const float2 d = fma2_rn(gg, f2c(inv), psub2(f2c(GQ_MAGIC), sv));
+        amb |= !(fabsf(d.x) < lim) || !(fabsf(d.y) < lim);
+        b[c] = __float_as_uint(sv.x), b[c + 1] = __float_as_uint(sv.y);
+      }
+      *reinterpret_cast<uint32_t*>(q + 128 * i) =
+          __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
+    }
+    if (lane == 0) xs[row] = sc;
+    if (amb) {  // quantise the elements near a rounding boundary again from the exact GELU
+      unsigned long long mask = 0;
+#pragma unroll
+      for (int i = 0; i < NV; i++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          const float d = __fmaf_rn(g[i][c], inv, __fsub_rn(GQ_MAGIC, __fmaf_rn(g[i][c], inv, GQ_MAGIC)));
+          mask |= static_cast<unsigned long long>(!(fabsf(d) < lim)) << (4 * i + c);
+        }
+      while (mask) {
+        const int b = __ffsll(static_cast<long long>(mask)) - 1;
+        mask &= mask - 1;
+        const int col = 128 * (b >> 2) + (b & 3);
+        q[col] = quant_one(gelu_ref(r[col]), inv);
+      }
     }
   }
 }
 
-// Exhaustive check of the bound gelu_quant_cert_k relies on, over the float bit patterns
-// [start, start + count): stats[0] = max over inputs with both values finite of
-// |g~ - g| - GELU_CERT_B |g~| (a non-negative double's bits, 0 when none exceeds 0);
-// stats[1] = inputs where gelu_ref is non-finite and gelu_fast finite; stats[2] = inputs with
-// both finite and |g~ - g| > GELU_CERT_A + GELU_CERT_B |g~|; stats[3] = inputs where gelu_fast
-// is non-finite and gelu_ref finite (allowed: such rows run exactly).
+// Exhaustive check of the facts gelu_quant_cert_k relies on, over the float bit patterns
+// [start, start + count) (both even), into stats[8]:
+//   [0] max over inputs with both values finite of |g~ - g| - GELU_CERT_B |g~| (a non-negative
+//       double's bits), [1] inputs where gelu_ref is non-finite and gelu_fast finite, [2] inputs
+//       with both finite and |g~ - g| > GELU_CERT_A + GELU_CERT_B |g~|, [3] inputs where only
+//       gelu_fast is non-finite (allowed: such rows run exactly), [4] max |g~ - g| / |g~| over
+//       |g~| >= 2^-4 and [5] max |g~ - g| over |g~| < 2^-4 (double bits, for choosing A and B),
+//   [6] pairs of adjacent floats 0 <= x < x' <= inf with gelu_ref(x') < gelu_ref(x), [7] max of
+//       |gelu_ref(x)| over non-NaN x < 0 (double bits).
 __global__ void gelu_cert_scan_k(unsigned long long start, unsigned long long count,
                                  unsigned long long* __restrict__ stats) {
-  double worst = 0.0;
-  unsigned long long n_nf = 0, n_viol = 0, n_fast_nf = 0;
+  double worst = 0.0, rel_max = 0.0, abs_small = 0.0, neg_max = 0.0;
+  unsigned long long n_nf = 0, n_viol = 0, n_fast_nf = 0, n_mono = 0;
   const unsigned long long stride = 2ull * gridDim.x * blockDim.x;
   for (unsigned long long i = 2ull * (blockIdx.x * blockDim.x + threadIdx.x); i < count; i += stride) {
-    const float x0 = __uint_as_float(static_cast<uint32_t>(start + i));
-    const float x1 = __uint_as_float(static_cast<uint32_t>(start + min(i + 1, count - 1)));
-    const float2 gf = gelu_fast2(make_float2(x0, x1));
-    const float gx[2] = {gelu_ref(x0), gelu_ref(x1)}, fx[2] = {gf.x, gf.y};
+    const uint32_t b0 = static_cast<uint32_t>(start + i);
+    const float x[2] = {__uint_as_float(b0), __uint_as_float(b0 + 1)};
+    const float2 gf = gelu_fast2(make_float2(x[0], x[1]));
+    const float gx[2] = {gelu_ref(x[0]), gelu_ref(x[1])}, fx[2] = {gf.x, gf.y};
 #pragma unroll
     for (int u = 0; u < 2; u++) {
       const bool fin_r = fabsf(gx[u]) <= 3.40282347e+38f, fin_f = fabsf(fx[u]) <= 3.40282347e+38f;
@@ -937,17 +976,29 @@ __global__ void gelu_cert_scan_k(unsigned long long start, unsigned long long co
       if (fin_r && !fin_f) n_fast_nf++;
       if (fin_r && fin_f) {
         const double err = fabs(static_cast<double>(fx[u]) - static_cast<double>(gx[u]));
-        const double rel = static_cast<double>(GELU_CERT_B) * fabs(static_cast<double>(fx[u]));
+        const double af = fabs(static_cast<double>(fx[u]));
+        const double rel = static_cast<double>(GELU_CERT_B) * af;
         worst = fmax(worst, err - rel);
         if (err > static_cast<double>(GELU_CERT_A) + rel) n_viol++;
+        if (af >= 0x1p-4) rel_max = fmax(rel_max, err / af);
+        else abs_small = fmax(abs_small, err);
       }
-      if (i + 1 >= count) break;
+      const uint32_t bu = b0 + u;
+      if (bu > 0x80000000u && bu <= 0xff800000u) neg_max = fmax(neg_max, fabs(static_cast<double>(gx[u])));
+    }
+    if (b0 < 0x7f800000u) {  // x0 < x1 <= inf, and x1 < x2 when x1 is finite
+      if (gx[1] < gx[0]) n_mono++;
+      if (b0 + 1 < 0x7f800000u && gelu_ref(__uint_as_float(b0 + 2)) < gx[1]) n_mono++;
     }
   }
   atomicMax(stats, static_cast<unsigned long long>(__double_as_longlong(worst)));
   if (n_nf) atomicAdd(stats + 1, n_nf);
   if (n_viol) atomicAdd(stats + 2, n_viol);
   if (n_fast_nf) atomicAdd(stats + 3, n_fast_nf);
+  atomicMax(stats + 4, static_cast<unsigned long long>(__double_as_longlong(rel_max)));
+  atomicMax(stats + 5, static_cast<unsigned long long>(__double_as_longlong(abs_small)));
+  if (n_mono) atomicAdd(stats + 6, n_mono);
+  atomicMax(stats + 7, static_cast<unsigned long long>(__double_as_longlong(neg_max)));
 }
 
 __global__ void add_k(float* __restrict__ h, const float* __restrict__ a, size_t n) {
@@ -1376,6 +1427,7 @@ bool kern_prepare() {
   set_smem(reinterpret_cast<const void*>(conv3_k), CV3_SMEM);
   set_smem(reinterpret_cast<const void*>(attn_k), 227 * 1024);
   set_smem(reinterpret_cast<const void*>(gelu_quant_ro_k), 227 * 1024);
+  set_smem(reinterpret_cast<const void*>(gelu_quant_cert_k<16>), GQ_WARPS * 2 * 2048 * 4);
   set_smem(reinterpret_cast<const void*>(ln_rows_k), LR_SMEM);
   set_smem(reinterpret_cast<const void*>(ln_quant_k<true>), LnCfg<true>::SMEM);
   return cudaGetLastError() == cudaSuccess;
@@ -1469,7 +1521,14 @@ int launch_gelu_quant_ro(const float* y, int m, int k, int8_t* xq, float* xs, cu
   if (m <= 0 || k <= 0) return 0;
   if (!exact && k == 16 * 128 && (reinterpret_cast<uintptr_t>(y) & 15) == 0 &&
       (reinterpret_cast<uintptr_t>(xq) & 3) == 0) {
-    gelu_quant_cert_k<16><<<(m + 7) / 8, 256, 0, st>>>(y, m, xq, xs);
+    // persistent warps: as many blocks as are resident at once (two per SM), at most one row each
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+      sms = 148;
+    constexpr int smem = GQ_WARPS * 2 * 2048 * 4;
+    set_smem(reinterpret_cast<const void*>(gelu_quant_cert_k<16>), smem);
+    gelu_quant_cert_k<16><<<std::min((m + GQ_WARPS - 1) / GQ_WARPS, 3 * sms), 32 * GQ_WARPS, smem, st>>>(y, m, xq, xs);
     return launched();
   }
   const size_t smem = static_cast<size_t>(GQ_ROWS) * k * sizeof(float);
@@ -1644,7 +1703,7 @@ int wasr_gelu_quant(const float* y, int m, int k, int8_t* xq, float* xs, int exa
 }
 int wasr_gelu_cert_scan(unsigned long long start, unsigned long long count, unsigned long long* stats,
                         void* stream) {
-  if (!stats || start + count > (1ull << 32)) return -1;
+  if (!stats || start + count > (1ull << 32) || (start | count) & 1) return -1;
   if (count == 0) return 0;
   gelu_cert_scan_k<<<148 * 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(start, count, stats);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
