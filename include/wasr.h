@@ -200,6 +200,17 @@ int wasr_eval_math(int fn, const float* x, float* y, int n, void* stream);
  * for k too large, -4 for a launch failure. */
 int wasr_gelu_quant(const float* y, int m, int k, int8_t* xq, float* xs, int exact, void* stream);
 
+/* conv3 followed by the per-row int8 quantisation of its output (src/model.rs:446-468 and 489:
+ * quant(y3, FLAT)) as the engine runs it, on device buffers: y2 [rows][64][41], c3 [192][576],
+ * prep scratch of 576 * 192 + 192 floats (filled here), roff device row offsets of nseg windows
+ * (NULL: one window of `rows`), xq [rows][3840] int8 and xs [rows].  No counterpart in the
+ * reference ABI.  The products are summed with fused multiply-adds and bounded against the
+ * reference's dotf order; the row maximum and every element whose scaled value lies within the
+ * bound of a rounding boundary are evaluated in the reference's order, so xq and xs equal
+ * quant(conv3(y2)) exactly.  0, -1 for bad arguments, -4 for a launch failure. */
+int wasr_conv3_quant(const float* y2, const float* c3, float* prep, const int* roff, int nseg, int rows,
+                     int8_t* xq, float* xs, void* stream);
+
 /* Parity hook for the certified GELU: scans the float bit patterns [start, start + count)
  * (both even, start + count <= 2^32) and accumulates into the device array stats[8] (zeroed by
  * the caller), with g~ the approximation and g the exact GELU: [0] the largest |g~ - g| - B |g~|

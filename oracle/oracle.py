@@ -44,6 +44,7 @@ def lib():
             "wo_gelu_array": (None, [P, P, I64]),
             "wo_attention": (None, [P, P, P, I, P]),
             "wo_frontend": (I, [P, I, P, P, P, P]),
+            "wo_conv3": (None, [P, I, P, P]),
             "wo_forward": (I, [P, P, P, I, P, P]),
             "wo_run_post": (I, [P, P, I, P, P, P]),
             "wo_argmax": (C.c_uint32, [P, I]),
@@ -161,6 +162,15 @@ def frontend(x, c1, c2, c3):
     lib().wo_frontend(_p(x), t, _p(np.ascontiguousarray(c1, np.float32)),
                       _p(np.ascontiguousarray(c2, np.float32)),
                       _p(np.ascontiguousarray(c3, np.float32)), _p(y3))
+    return y3[:t1]
+
+
+def conv3(y2, c3):
+    """The conv3 stage alone (src/model.rs:446-468): y2 [t1][64][41] -> y3 [t1][3840]."""
+    y2 = np.ascontiguousarray(y2, np.float32)
+    t1 = y2.shape[0]
+    y3 = np.zeros((max(t1, 1), 3840), np.float32)
+    lib().wo_conv3(_p(y2), t1, _p(np.ascontiguousarray(c3, np.float32)), _p(y3))
     return y3[:t1]
 
 

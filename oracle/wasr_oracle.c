@@ -242,6 +242,32 @@ void wo_attention(const float* q, const float* k, const float* v, int t, float* 
   }
 }
 
+/* src/model.rs:446-468: conv 3x3, 64->192, frequency stride 2, time pad 1 of one window's
+ * y2 [t1][64][41] -> y3 [t1][192*20] (im2col + dotf + ReLU) */
+void wo_conv3(const float* y2, int t1, const float* c3, float* y3) {
+#pragma omp parallel
+  {
+    float* p = (float*)malloc(sizeof(float) * 20 * K3);
+#pragma omp for schedule(static)
+    for (int ti = 0; ti < t1; ti++) {
+      memset(p, 0, sizeof(float) * 20 * K3);
+      for (int i = 0; i < 3; i++) {
+        int tt = ti + i - 1;
+        if (tt < 0 || tt >= t1) continue;
+        const float* row = y2 + (int64_t)tt * F2 * W2;
+        for (int c = 0; c < F2; c++)
+          for (int f = 0; f < 20; f++)
+            for (int j = 0; j < 3; j++) p[f * K3 + c * 9 + i * 3 + j] = row[c * W2 + 2 * f + j];
+      }
+      float* y = y3 + (int64_t)ti * FLAT;
+      for (int o = 0; o < F3; o++)
+        for (int f = 0; f < 20; f++)
+          y[o * 20 + f] = fmaxf(wo_dotf(c3 + (int64_t)o * K3, p + f * K3, K3), 0.0f);
+    }
+    free(p);
+  }
+}
+
 /* src/model.rs:389-478 (im2col + dotf + ReLU) */
 int wo_frontend(const float* x, int t, const float* c1, const float* c2, const float* c3,
                 float* y3) {
@@ -292,28 +318,7 @@ int wo_frontend(const float* x, int t, const float* c1, const float* c2, const f
     }
     free(p);
   }
-  /* conv 3x3, 64->192, frequency stride 2, time pad 1 -> [t1][192*20] */
-#pragma omp parallel
-  {
-    float* p = (float*)malloc(sizeof(float) * 20 * K3);
-#pragma omp for schedule(static)
-    for (int ti = 0; ti < t1; ti++) {
-      memset(p, 0, sizeof(float) * 20 * K3);
-      for (int i = 0; i < 3; i++) {
-        int tt = ti + i - 1;
-        if (tt < 0 || tt >= t1) continue;
-        const float* row = y2 + (int64_t)tt * F2 * W2;
-        for (int c = 0; c < F2; c++)
-          for (int f = 0; f < 20; f++)
-            for (int j = 0; j < 3; j++) p[f * K3 + c * 9 + i * 3 + j] = row[c * W2 + 2 * f + j];
-      }
-      float* y = y3 + (int64_t)ti * FLAT;
-      for (int o = 0; o < F3; o++)
-        for (int f = 0; f < 20; f++)
-          y[o * 20 + f] = fmaxf(wo_dotf(c3 + (int64_t)o * K3, p + f * K3, K3), 0.0f);
-    }
-    free(p);
-  }
+  wo_conv3(y2, t1, c3, y3);
   free(y1);
   free(y2);
   return t1;

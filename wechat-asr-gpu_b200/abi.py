@@ -114,6 +114,7 @@ SIGNATURES = {
     "wasr_ctc_collapse": (I64, [P, I64, P]),
     "wasr_eval_math": (I, [I, P, P, I, P]),
     "wasr_gelu_quant": (I, [P, I, I, P, P, I, P]),
+    "wasr_conv3_quant": (I, [P, P, P, P, I, I, P, P, P]),
     "wasr_gelu_cert_scan": (I, [U64, U64, P, P]),
     "wasr_i8_mma_peak": (I, [I, I, P, P]),
     "wasr_version": (C.c_char_p, []),

@@ -604,6 +604,9 @@ constexpr float GELU_CERT_B = 0x1p-21f;
 // |gelu_ref(x)| <= GELU_NEG_MAX for every x < 0, and gelu_ref is non-decreasing on [0, inf]
 // (both checked on every float by wasr_gelu_cert_scan)
 constexpr float GELU_NEG_MAX = 0.171f;
+// fma(v, inv, RINT_MAGIC) rounds v * inv to the nearest integer n (ties to even), held in the
+// low mantissa bits for |v * inv| < 2^22: the result's low byte is n as an int8
+constexpr float RINT_MAGIC = 12582912.0f;  // 1.5 * 2^23
 // packed fused multiply-add, one rounding per element
 __device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
   unsigned long long r;

@@ -71,8 +71,9 @@ struct WasrModel {
   float* qkv_bias[WASR_MAX_LAYERS] = {};
   bool qkv_fused[WASR_MAX_LAYERS] = {};
   // activations
-  float *feats = nullptr, *y1 = nullptr, *y2 = nullptr, *y3 = nullptr;
-  float *c2pre = nullptr, *c3pre = nullptr;  // conv2 / conv3 weights laid out per conv stage
+  float *feats = nullptr, *y1 = nullptr, *y2 = nullptr;
+  float* c2pre = nullptr;   // conv2 weights laid out per conv stage
+  float* c3cert = nullptr;  // conv3 weights transposed for conv3_cert_k, and their row norms
   int8_t* xq = nullptr;
   float* xs = nullptr;
   float *h = nullptr, *qkv = nullptr, *att = nullptr, *f = nullptr;
@@ -231,11 +232,11 @@ int enqueue_chunk(WasrModel* m, const Chunk& c, const int* seg, float* logits, L
   const int* tord = seg + 3 * (n + 1);
   const int M = c.rows;
   const WasrPlan& P = m->plan;
-  // conv frontend -> y3 -> int8 -> linear (src/model.rs:389-478,489)
+  // conv frontend -> int8 rows of y3 -> linear (src/model.rs:389-478,489)
   TRY(K(WASR_K_CONV1, [&] { return launch_conv1(m->feats, fptr(m, P.c1), s, c.frames, m->y1, st); }));
   TRY(K(WASR_K_CONV2, [&] { return launch_conv2(m->y1, fptr(m, P.c2), m->c2pre, s, M, m->y2, st); }));
-  TRY(K(WASR_K_CONV3, [&] { return launch_conv3(m->y2, fptr(m, P.c3), m->c3pre, s, M, m->y3, st); }));
-  TRY(K(WASR_K_QUANT, [&] { return launch_quant_rows(m->y3, M, FLAT, FLAT, m->xq, m->xs, st); }));
+  // conv3 with its row quantisation fused and certified (int8 rows identical to quant(conv3))
+  TRY(K(WASR_K_CONV3, [&] { return launch_conv3_cert(m->y2, fptr(m, P.c3), m->c3cert, s, M, m->xq, m->xs, st); }));
   TRY(K(WASR_K_GEMM_LIN, [&] { return gemm_run(gemm_args(m, m->xq, m->xs, M, FLAT, P.lin, D, P.lin_b, EPI_F32, m->h, D), st); }));
   for (int l = 0; l < P.n_layers; l++) {
     const WasrLayer& L = P.layers[l];
@@ -523,7 +524,7 @@ WasrModel* wasr_model_create(const void* blob, size_t bytes, const WasrPlan* pla
   ok = ok && dmalloc(&m->w, bytes) && cudaMemcpy(m->w, blob, bytes, cudaMemcpyHostToDevice) == cudaSuccess;
   const size_t R = static_cast<size_t>(max_rows), Fr = static_cast<size_t>(m->max_frames);
   ok = ok && dmalloc(&m->feats, Fr * DIM) && dmalloc(&m->y1, Fr * C1 * DIM) && dmalloc(&m->y2, R * C2 * W2) &&
-       dmalloc(&m->y3, R * FLAT) && dmalloc(&m->xq, R * FLAT) && dmalloc(&m->xs, R) && dmalloc(&m->h, R * D) &&
+       dmalloc(&m->xq, R * FLAT) && dmalloc(&m->xs, R) && dmalloc(&m->h, R * D) &&
        dmalloc(&m->qkv, R * 3 * D) && dmalloc(&m->att, R * D) && dmalloc(&m->f, R * FF) &&
        dmalloc(&m->rowmax, R) && dmalloc(&m->keys, R) && dmalloc(&m->ids, R);
   // q/k/v fusion: the three [512][512] matrices must sit back to back in the blob
@@ -553,8 +554,9 @@ WasrModel* wasr_model_create(const void* blob, size_t bytes, const WasrPlan* pla
     m->qkv_fused[l] = ok;
   }
   // conv2 / conv3 weights in the per-stage layout their kernels stage from (once per model)
-  ok = ok && dmalloc(&m->c2pre, conv_pre_floats(2)) && dmalloc(&m->c3pre, conv_pre_floats(3)) &&
-       conv_prepare(fptr(m, plan->c2), fptr(m, plan->c3), m->c2pre, m->c3pre, m->stream) == 0 &&
+  ok = ok && dmalloc(&m->c2pre, conv_pre_floats(2)) && dmalloc(&m->c3cert, conv3_cert_prep_floats()) &&
+       conv_prepare(fptr(m, plan->c2), nullptr, m->c2pre, nullptr, m->stream) == 0 &&
+       conv3_cert_prepare(fptr(m, plan->c3), m->c3cert, m->stream) == 0 &&
        cudaStreamSynchronize(m->stream) == cudaSuccess;
   if (!ok) {
     wasr_model_destroy(m);
@@ -569,8 +571,8 @@ void wasr_model_destroy(WasrModel* m) {
   cudaDeviceSynchronize();
   free_graphs(m);
   free_recs(&m->eager_recs);
-  void* dptrs[] = {m->w, m->feats, m->y1, m->y2, m->y3, m->xq, m->xs, m->h, m->qkv, m->att, m->f, m->rowmax,
-                   m->keys, m->ids, m->seg, m->c2pre, m->c3pre, m->d_win, m->d_wtab};
+  void* dptrs[] = {m->w, m->feats, m->y1, m->y2, m->xq, m->xs, m->h, m->qkv, m->att, m->f, m->rowmax,
+                   m->keys, m->ids, m->seg, m->c2pre, m->c3cert, m->d_win, m->d_wtab};
   for (void* p : dptrs)
     if (p) cudaFree(p);
   for (int l = 0; l < WASR_MAX_LAYERS; l++) {

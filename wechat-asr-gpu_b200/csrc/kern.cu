@@ -728,6 +728,338 @@ __global__ void __launch_bounds__(256) ln_quant_any_k(float* __restrict__ h, con
   if (threadIdx.x == 0) xs[blockIdx.x] = sc;
 }
 
+// ------------------------------------------------------------------------ conv3 + certified quant
+// The engine's conv3: y3 feeds only its row's int8 quantisation (src/model.rs:489,
+// quant(y3, FLAT)), so the kernel computes y3 with fused multiply-adds in any order, bounds
+// the difference to the reference's dotf result, and quantises exactly as in quant, taking
+// the row maximum and every element near a rounding boundary from the reference-order value
+// (the same reasoning as the certified GELU).
+//
+// Bound.  For output (o, f) with patch a and weight row w: the dotf result (one rounded product
+// and at most 72 + 7 + 1 rounded adds per term) is within g80 * sum |a_k w_k| of the exact sum;
+// the fused multiply-add value (per 36-tap stage a chain of at most 36 roundings from zero, then
+// 16 adds of the stage partials) within g52 * sum |a_k w_k|; relu is 1-Lipschitz; and
+// sum |a_k w_k| <= |a|_2 |w|_2.  So |y~ - y| <= E = C3C_BOUND * na(f) * nw(o), g_n = n u / (1 - n u),
+// u = 2^-24, with na and nw upper bounds of the norms.
+//
+// Work split: a block owns 4 output rows (80 positions) and all 192 channels, 16 stages of 4
+// input channels (36 taps).  Per stage the weights [36 taps][192] (pre-transposed once per model)
+// and the 6 input rows' 4 channels stream in by cp.async (double-buffered), the im2col tile
+// P[36][80] is built in shared memory, and thread (cg, pg) < 240 accumulates channels
+// {4cg+a, 96+4cg+a} x positions {4pg+b, 40+4pg+b} (a, b < 4) from two 16-byte loads of each.
+// Epilogue: the 6 input rows are staged whole for the reference-order values, then per row the
+// maximum candidates (y~ + E >= max(y~ - E)) and the near-boundary elements are evaluated in
+// dotf order by groups of 8 threads (one per dotf lane, folded in lane order).
+constexpr int C3C_R = 4;                 // output rows per block
+constexpr int C3C_N = C3C_R * 20;        // positions per block
+constexpr int C3C_CC = 4;                // input channels per stage
+constexpr int C3C_KS = C3C_CC * 9;       // taps per stage
+constexpr int C3C_NST = C2 / C3C_CC;     // stages
+constexpr int C3C_RAWR = C3C_CC * W2;    // floats of one staged input row (4 channels x 41)
+constexpr int C3C_IN = C3C_R + 2;        // input rows per block
+constexpr int C3C_THREADS = 256;
+constexpr int C3C_CAP = 2048;            // entries of the reference-order list
+constexpr int C3C_YROW = C2 * W2;        // floats of one y2 row (2624)
+// shared-memory layout, in floats
+constexpr int C3C_OFF_W = 0;                                      // [2][36][192]
+constexpr int C3C_OFF_RAW = C3C_OFF_W + 2 * C3C_KS * C3;          // [2][6][164]
+constexpr int C3C_OFF_P = C3C_OFF_RAW + 2 * C3C_IN * C3C_RAWR;    // [36][80]
+constexpr int C3C_OFF_Q = C3C_OFF_P + C3C_KS * C3C_N;             // int8 [4][3840]
+constexpr int C3C_OFF_LIST = C3C_OFF_Q + C3C_R * FLAT / 4;        // int [cap] + float [cap]
+constexpr int C3C_OFF_KO = C3C_OFF_LIST + 2 * C3C_CAP;            // int [576]: (i << 16) | (i * 2624 + c * 41 + j)
+constexpr int C3C_OFF_NA = C3C_OFF_KO + K3;                       // [80]
+constexpr int C3C_OFF_NW = C3C_OFF_NA + C3C_N;                    // [192]
+constexpr int C3C_OFF_MISC = C3C_OFF_NW + C3;                     // ints: valid[12], L[4], M[4], cnt, ovf
+constexpr int C3C_SMEM = (C3C_OFF_MISC + 32) * 4;
+static_assert(C3C_IN * C3C_YROW <= C3C_OFF_P, "the staged y2 rows reuse the weight / raw buffers");
+// (80 + 52 + 1) * 2^-24 * (1 + 2^-10): the two g_n above, with margin for their 1/(1 - n u)
+constexpr float C3C_BOUND = 133.2f * 0x1p-24f;
+
+// lane l's dotf chain (taps l, l+8, ..., l+568) of output (row rho, channel o, position f) from
+// the staged y2 rows; valid[rho*3 + i] says whether input row rho+i-1 is inside the segment
+__device__ __forceinline__ float c3c_lane(const float* y2s, const float* __restrict__ c3, const int* ko,
+                                          const int* valid, int rho, int o, int f, int l) {
+  const float* wr = c3 + static_cast<int64_t>(o) * K3;
+  const float* base = y2s + rho * C3C_YROW + 2 * f;
+  float acc = 0.0f;
+#pragma unroll 8
+  for (int c = 0; c < K3 / 8; c++) {
+    const int k = 8 * c + l, e = ko[k];
+    const float a = valid[rho * 3 + (e >> 16)] ? base[e & 0xffff] : 0.0f;
+    acc = __fadd_rn(acc, __fmul_rn(__ldg(wr + k), a));
+  }
+  return acc;
+}
+// fold the 8 lanes of a group in lane order and apply relu (every lane of the group gets it)
+__device__ __forceinline__ float c3c_fold(float v) {
+  float s = __fadd_rn(__shfl_sync(0xffffffffu, v, 0, 8), __shfl_sync(0xffffffffu, v, 1, 8));
+#pragma unroll
+  for (int l = 2; l < 8; l++) s = __fadd_rn(s, __shfl_sync(0xffffffffu, v, l, 8));
+  return fmaxf(s, 0.0f);
+}
+
+__global__ void __launch_bounds__(C3C_THREADS, 1) conv3_cert_k(const float* __restrict__ y2,
+                                                              const float* __restrict__ c3,
+                                                              const float* __restrict__ c3t,
+                                                              const float* __restrict__ nw_g, Segs s, int total,
+                                                              int8_t* __restrict__ xq, float* __restrict__ xs) {
+  extern __shared__ __align__(16) float sm[];
+  float* Wst = sm + C3C_OFF_W;
+  float* raw = sm + C3C_OFF_RAW;
+  float* P = sm + C3C_OFF_P;
+  int8_t* qo = reinterpret_cast<int8_t*>(sm + C3C_OFF_Q);
+  int* lst = reinterpret_cast<int*>(sm + C3C_OFF_LIST);
+  float* lval = sm + C3C_OFF_LIST + C3C_CAP;
+  int* ko = reinterpret_cast<int*>(sm + C3C_OFF_KO);
+  float* na = sm + C3C_OFF_NA;
+  float* nw = sm + C3C_OFF_NW;
+  int* misc = reinterpret_cast<int*>(sm + C3C_OFF_MISC);
+  int* valid = misc;            // [12]
+  float* rowL = sm + C3C_OFF_MISC + 12;  // [4]
+  float* rowM = sm + C3C_OFF_MISC + 16;  // [4]
+  int* cnt = misc + 20;
+  int* ovf = misc + 21;
+  float* rowInv = sm + C3C_OFF_MISC + 24;  // [4]
+  const int t = threadIdx.x, r0 = blockIdx.x * C3C_R;
+  if (t < 12) {
+    const int rho = t / 3, i = t % 3, r = r0 + rho;
+    bool ok = false;
+    if (r < total) {
+      const int w = s.seg_of_row(r), tt = r - s.row_begin(w) + i - 1;
+      ok = tt >= 0 && tt < s.rows(w);
+    }
+    valid[t] = ok;
+  }
+  if (t < C3C_R) rowL[t] = 0.0f, rowM[t] = 0.0f;
+  if (t == 0) *cnt = 0, *ovf = 0;
+  for (int k = t; k < K3; k += C3C_THREADS) {
+    const int c = k / 9, tap = k - 9 * c, i = tap / 3, j = tap - 3 * i;
+    ko[k] = (i << 16) | (i * C3C_YROW + c * W2 + j);
+  }
+  for (int o = t; o < C3; o += C3C_THREADS) nw[o] = nw_g[o];
+  auto load_stage = [&](int st, int buf) {
+    const float4* src = reinterpret_cast<const float4*>(c3t + static_cast<int64_t>(st) * C3C_KS * C3);
+    float4* dst = reinterpret_cast<float4*>(Wst + buf * C3C_KS * C3);
+    for (int e = t; e < C3C_KS * C3 / 4; e += C3C_THREADS) cp_async16(dst + e, src + e);
+    for (int e = t; e < C3C_IN * (C3C_RAWR / 4); e += C3C_THREADS) {
+      const int ri = e / (C3C_RAWR / 4), q = e - ri * (C3C_RAWR / 4), g = r0 - 1 + ri;
+      if (g >= 0 && g < total)
+        cp_async16(raw + (buf * C3C_IN + ri) * C3C_RAWR + 4 * q,
+                   y2 + static_cast<int64_t>(g) * C3C_YROW + st * C3C_RAWR + 4 * q);
+    }
+    cp_async_commit();
+  };
+  load_stage(0, 0);
+  const bool act = t < 240;
+  const int cg = t % 24, pg = t / 24;
+  float tot[8][8];
+#pragma unroll
+  for (int a = 0; a < 8; a++)
+#pragma unroll
+    for (int b = 0; b < 8; b++) tot[a][b] = 0.0f;
+#pragma unroll 1
+  for (int st = 0; st < C3C_NST; st++) {
+    cp_async_wait<0>();
+    __syncthreads();  // stage st visible; the previous stage's P and buffers consumed
+    if (st + 1 < C3C_NST) load_stage(st + 1, (st + 1) & 1);
+    const float* rw = raw + (st & 1) * C3C_IN * C3C_RAWR;
+    for (int e = t; e < C3C_KS * C3C_N; e += C3C_THREADS) {
+      const int kk = e / C3C_N, n = e - kk * C3C_N, rho = n / 20, f = n - 20 * rho;
+      const int cl = kk / 9, tap = kk - 9 * cl, i = tap / 3, j = tap - 3 * i;
+      P[e] = valid[rho * 3 + i] ? rw[(rho + i) * C3C_RAWR + cl * W2 + 2 * f + j] : 0.0f;
+    }
+    __syncthreads();
+    if (act) {
+      const float* wb = Wst + (st & 1) * C3C_KS * C3 + 4 * cg;
+      const float* pb = P + 4 * pg;
+      float acc[8][8];
+#pragma unroll
+      for (int a = 0; a < 8; a++)
+#pragma unroll
+        for (int b = 0; b < 8; b++) acc[a][b] = 0.0f;
+#pragma unroll 4
+      for (int kk = 0; kk < C3C_KS; kk++) {
+        const float4 w0 = *reinterpret_cast<const float4*>(wb + kk * C3);
+        const float4 w1 = *reinterpret_cast<const float4*>(wb + kk * C3 + 96);
+        const float4 p0 = *reinterpret_cast<const float4*>(pb + kk * C3C_N);
+        const float4 p1 = *reinterpret_cast<const float4*>(pb + kk * C3C_N + 40);
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+        for (int a = 0; a < 8; a++)
+#pragma unroll
+          for (int b = 0; b < 8; b++) acc[a][b] = __fmaf_rn(wv[a], pv[b], acc[a][b]);
+      }
+#pragma unroll
+      for (int a = 0; a < 8; a++)
+#pragma unroll
+        for (int b = 0; b < 8; b++) tot[a][b] = __fadd_rn(tot[a][b], acc[a][b]);
+    }
+  }
+  __syncthreads();  // every stage consumed: the weight / raw region takes the whole y2 rows
+  float* y2s = sm;
+  for (int e = t; e < C3C_IN * (C3C_YROW / 4); e += C3C_THREADS) {
+    const int ri = e / (C3C_YROW / 4), q = e - ri * (C3C_YROW / 4), g = r0 - 1 + ri;
+    if (g >= 0 && g < total)
+      cp_async16(y2s + ri * C3C_YROW + 4 * q, y2 + static_cast<int64_t>(g) * C3C_YROW + 4 * q);
+    else
+      *reinterpret_cast<float4*>(y2s + ri * C3C_YROW + 4 * q) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+  {  // patch norms: warp w takes positions w, w+8, ...; lanes split the 576 taps
+    const int warp = t >> 5, lane = t & 31;
+    for (int n = warp; n < C3C_N; n += C3C_THREADS / 32) {
+      const int rho = n / 20, f = n - 20 * rho;
+      float ss = 0.0f;
+      for (int k = lane; k < K3; k += 32) {
+        const int e = ko[k];
+        const float a = valid[rho * 3 + (e >> 16)] ? y2s[rho * C3C_YROW + 2 * f + (e & 0xffff)] : 0.0f;
+        ss = __fmaf_rn(a, a, ss);
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+      // fp32 sum of 576 squares: relative error below 2^-14; inflate past it
+      if (lane == 0) na[n] = __fmul_ru(__fsqrt_ru(ss), 1.0f + 0x1p-12f);
+    }
+  }
+  __syncthreads();
+  // per-element bound and each row's lower bound of its maximum
+  float E[8][8];
+#pragma unroll
+  for (int a = 0; a < 8; a++)
+#pragma unroll
+    for (int b = 0; b < 8; b++) {
+      const int o = (a < 4 ? 0 : 96) + 4 * cg + (a & 3), n = (b < 4 ? 0 : 40) + 4 * pg + (b & 3);
+      tot[a][b] = fmaxf(tot[a][b], 0.0f);
+      E[a][b] = act ? __fmul_ru(__fmul_ru(C3C_BOUND, na[n]), nw[o]) : 0.0f;
+    }
+  if (act) {  // positions 4pg..4pg+3 lie in row pA, 40+4pg.. in row pB
+    float loA = 0.0f, loB = 0.0f;
+#pragma unroll
+    for (int a = 0; a < 8; a++)
+#pragma unroll
+      for (int b = 0; b < 4; b++) {
+        loA = fmaxf(loA, __fsub_rd(tot[a][b], E[a][b]));
+        loB = fmaxf(loB, __fsub_rd(tot[a][b + 4], E[a][b + 4]));
+      }
+    if (loA > 0.0f) atomicMax(reinterpret_cast<int*>(rowL + (4 * pg) / 20), __float_as_int(loA));
+    if (loB > 0.0f) atomicMax(reinterpret_cast<int*>(rowL + (40 + 4 * pg) / 20), __float_as_int(loB));
+  }
+  __syncthreads();
+  // candidates for each row's maximum -> the list (overflow: the whole block runs exactly)
+  auto push = [&](int rho, int o, int f) {
+    const int e = atomicAdd(cnt, 1);
+    if (e < C3C_CAP) lst[e] = (rho << 16) | (o << 5) | f; else *ovf = 1;
+  };
+  if (act) {
+#pragma unroll
+    for (int a = 0; a < 8; a++)
+#pragma unroll
+      for (int b = 0; b < 8; b++) {
+        const int o = (a < 4 ? 0 : 96) + 4 * cg + (a & 3), n = (b < 4 ? 0 : 40) + 4 * pg + (b & 3);
+        const int rho = n / 20;
+        if (r0 + rho < total && __fadd_ru(tot[a][b], E[a][b]) >= rowL[rho]) push(rho, o, n - 20 * rho);
+      }
+  }
+  __syncthreads();
+  const int ncand = min(*cnt, C3C_CAP);
+  const bool overflow = *ovf != 0;
+  const int grp = t >> 3, l = t & 7;
+  if (!overflow) {  // reference-order values of the candidates; each row's exact maximum
+    for (int b0 = 0; b0 < ncand; b0 += C3C_THREADS / 8) {
+      const int e = b0 + grp, en = lst[min(e, ncand - 1)];
+      const float v = c3c_fold(c3c_lane(y2s, c3, ko, valid, en >> 16, (en >> 5) & 255, en & 31, l));
+      if (e < ncand && l == 0) {
+        lval[e] = v;
+        atomicMax(reinterpret_cast<int*>(rowM + (en >> 16)), __float_as_int(v));
+      }
+    }
+  }
+  __syncthreads();
+  if (t < C3C_R) rowInv[t] = quant_inv(quant_scale(rowM[t]));
+  __syncthreads();
+  if (overflow) {  // every element in reference order (rows whose bounds cannot separate anything)
+    for (int b0 = 0; b0 < C3C_R * FLAT; b0 += C3C_THREADS / 8) {
+      const int e = b0 + grp, rho = e / FLAT, rem = e - rho * FLAT, o = rem / 20, f = rem - 20 * o;
+      const float v = c3c_fold(c3c_lane(y2s, c3, ko, valid, rho, o, f, l));
+      if (l == 0 && r0 + rho < total) atomicMax(reinterpret_cast<int*>(rowM + rho), __float_as_int(v));
+    }
+    __syncthreads();
+    for (int b0 = 0; b0 < C3C_R * FLAT; b0 += C3C_THREADS / 8) {
+      const int e = b0 + grp, rho = e / FLAT, rem = e - rho * FLAT, o = rem / 20, f = rem - 20 * o;
+      const float v = c3c_fold(c3c_lane(y2s, c3, ko, valid, rho, o, f, l));
+      if (l == 0 && r0 + rho < total) qo[rho * FLAT + o * 20 + f] = quant_one(v, quant_inv(quant_scale(rowM[rho])));
+    }
+  } else {
+    // every element that is neither a candidate nor near a rounding boundary is quantised from
+    // y~; the rest join the list after the candidates
+    if (act) {
+#pragma unroll
+      for (int a = 0; a < 8; a++)
+#pragma unroll
+        for (int b = 0; b < 8; b++) {
+          const int o = (a < 4 ? 0 : 96) + 4 * cg + (a & 3), n = (b < 4 ? 0 : 40) + 4 * pg + (b & 3);
+          const int rho = n / 20, f = n - 20 * rho;
+          if (r0 + rho >= total || __fadd_ru(tot[a][b], E[a][b]) >= rowL[rho]) continue;
+          const float inv = rowInv[rho];
+          const float lim = __fsub_rd(0.5f, __fadd_ru(__fmul_ru(E[a][b], inv), 0x1p-16f));
+          const float sv = __fmaf_rn(tot[a][b], inv, RINT_MAGIC);
+          const float d = __fmaf_rn(tot[a][b], inv, __fsub_rn(RINT_MAGIC, sv));
+          if (fabsf(d) < lim)
+            qo[rho * FLAT + o * 20 + f] = static_cast<int8_t>(__float_as_uint(sv) & 0xffu);
+          else
+            push(rho, o, f);
+        }
+    }
+    __syncthreads();
+    const int ntot = min(*cnt, C3C_CAP);
+    if (*ovf) {  // the near-boundary list overflowed: its entries past the cap are not recorded
+      for (int b0 = 0; b0 < C3C_R * FLAT; b0 += C3C_THREADS / 8) {
+        const int e = b0 + grp, rho = e / FLAT, rem = e - rho * FLAT, o = rem / 20, f = rem - 20 * o;
+        const float v = c3c_fold(c3c_lane(y2s, c3, ko, valid, rho, o, f, l));
+        if (l == 0 && r0 + rho < total) qo[rho * FLAT + o * 20 + f] = quant_one(v, rowInv[rho]);
+      }
+    } else {
+      for (int e = t; e < ncand; e += C3C_THREADS) {  // the candidates' values are known
+        const int en = lst[e], rho = en >> 16;
+        qo[rho * FLAT + ((en >> 5) & 255) * 20 + (en & 31)] = quant_one(lval[e], rowInv[rho]);
+      }
+      for (int b0 = ncand; b0 < ntot; b0 += C3C_THREADS / 8) {
+        const int e = b0 + grp, en = lst[min(e, ntot - 1)], rho = en >> 16;
+        const float v = c3c_fold(c3c_lane(y2s, c3, ko, valid, rho, (en >> 5) & 255, en & 31, l));
+        if (e < ntot && l == 0)
+          qo[rho * FLAT + ((en >> 5) & 255) * 20 + (en & 31)] = quant_one(v, rowInv[rho]);
+      }
+    }
+  }
+  __syncthreads();
+  for (int rho = 0; rho < C3C_R; rho++) {
+    const int r = r0 + rho;
+    if (r >= total) break;
+    const int4* src = reinterpret_cast<const int4*>(qo + rho * FLAT);
+    int4* dst = reinterpret_cast<int4*>(xq + static_cast<int64_t>(r) * FLAT);
+    for (int e = t; e < FLAT / 16; e += C3C_THREADS) dst[e] = src[e];
+    if (t == 0) xs[r] = quant_scale(rowM[rho]);
+  }
+}
+
+// c3t[k][o] = c3[o][k] (the stage tiles of conv3_cert_k) and nw[o] >= |c3[o]|_2 (the square
+// root of the double sum of squares, rounded up), once per model
+__global__ void conv3_cert_prep_k(const float* __restrict__ c3, float* __restrict__ c3t, float* __restrict__ nw) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < K3 * C3) {
+    const int k = i / C3, o = i - k * C3;
+    c3t[i] = c3[static_cast<int64_t>(o) * K3 + k];
+  }
+  if (i < C3) {
+    double ss = 0.0;
+    for (int k = 0; k < K3; k++) ss += static_cast<double>(c3[static_cast<int64_t>(i) * K3 + k]) * c3[static_cast<int64_t>(i) * K3 + k];
+    nw[i] = __double2float_ru(__dsqrt_ru(ss) * (1.0 + 0x1p-40));
+  }
+}
+
 // ------------------------------------------------------------------------ GELU + quant
 // in place x = gelu(x) (src/model.rs:495,710-712), then per-row quant; one warp per row.
 __global__ void __launch_bounds__(256) gelu_quant_k(float* __restrict__ x, int m, int k, int8_t* __restrict__ xq,
@@ -839,7 +1171,6 @@ __device__ __noinline__ void gelu_quant_row_exact(const float* __restrict__ r, i
 // Persistent warps: each takes rows w, w + W, ...; while it works on one row, the next streams
 // into the other half of its two-row shared-memory buffer by cp.async (each lane copies and
 // later reads only its own 16-byte pieces, so no synchronisation beyond the copy wait).
-constexpr float GQ_MAGIC = 12582912.0f;  // 1.5 * 2^23
 constexpr int GQ_WARPS = 4;              // warps per block
 template <int NV>
 __global__ void __launch_bounds__(32 * GQ_WARPS, 3) gelu_quant_cert_k(const float* __restrict__ y, int m,
@@ -922,8 +1253,8 @@ __global__ void __launch_bounds__(32 * GQ_WARPS, 3) gelu_quant_cert_k(const floa
 #pragma unroll
       for (int c = 0; c < 4; c += 2) {
         const float2 gg = make_float2(g[i][c], g[i][c + 1]);
-        const float2 sv = fma2_rn(gg, f2c(inv), f2c(GQ_MAGIC));
-        const float2 d = fma2_rn(gg, f2c(inv), psub2(f2c(GQ_MAGIC), sv));
+        const float2 sv = fma2_rn(gg, f2c(inv), f2c(RINT_MAGIC));
+        const float2 d = fma2_rn(gg, f2c(inv), psub2(f2c(RINT_MAGIC), sv));
         amb |= !(fabsf(d.x) < lim) || !(fabsf(d.y) < lim);
         b[c] = __float_as_uint(sv.x), b[c + 1] = __float_as_uint(sv.y);
       }
@@ -937,7 +1268,7 @@ __global__ void __launch_bounds__(32 * GQ_WARPS, 3) gelu_quant_cert_k(const floa
       for (int i = 0; i < NV; i++)
 #pragma unroll
         for (int c = 0; c < 4; c++) {
-          const float d = __fmaf_rn(g[i][c], inv, __fsub_rn(GQ_MAGIC, __fmaf_rn(g[i][c], inv, GQ_MAGIC)));
+          const float d = __fmaf_rn(g[i][c], inv, __fsub_rn(RINT_MAGIC, __fmaf_rn(g[i][c], inv, RINT_MAGIC)));
           mask |= static_cast<unsigned long long>(!(fabsf(d) < lim)) << (4 * i + c);
         }
       while (mask) {
@@ -1428,6 +1759,7 @@ bool kern_prepare() {
   set_smem(reinterpret_cast<const void*>(attn_k), 227 * 1024);
   set_smem(reinterpret_cast<const void*>(gelu_quant_ro_k), 227 * 1024);
   set_smem(reinterpret_cast<const void*>(gelu_quant_cert_k<16>), GQ_WARPS * 2 * 2048 * 4);
+  set_smem(reinterpret_cast<const void*>(conv3_cert_k), C3C_SMEM);
   set_smem(reinterpret_cast<const void*>(ln_rows_k), LR_SMEM);
   set_smem(reinterpret_cast<const void*>(ln_quant_k<true>), LnCfg<true>::SMEM);
   return cudaGetLastError() == cudaSuccess;
@@ -1453,10 +1785,13 @@ __global__ void conv_pre_k(const float* __restrict__ c, int nout, int k, int tap
 
 size_t conv_pre_floats(int which) { return which == 2 ? static_cast<size_t>(C2) * K2 : static_cast<size_t>(C3) * K3; }
 
+// either layout may be skipped (null pointers)
 int conv_prepare(const float* c2, const float* c3, float* c2pre, float* c3pre, cudaStream_t st) {
   const int n2 = (C1 / CV2_CC) * CV2_MP * C2, n3 = (C2 / CV3_CC) * CV3_MP * C3;
-  conv_pre_k<<<(n2 + 255) / 256, 256, 0, st>>>(c2, C2, K2, CV2_CC * 49, C1 / CV2_CC, reinterpret_cast<float2*>(c2pre));
-  conv_pre_k<<<(n3 + 255) / 256, 256, 0, st>>>(c3, C3, K3, CV3_CC * 9, C2 / CV3_CC, reinterpret_cast<float2*>(c3pre));
+  if (c2 && c2pre)
+    conv_pre_k<<<(n2 + 255) / 256, 256, 0, st>>>(c2, C2, K2, CV2_CC * 49, C1 / CV2_CC, reinterpret_cast<float2*>(c2pre));
+  if (c3 && c3pre)
+    conv_pre_k<<<(n3 + 255) / 256, 256, 0, st>>>(c3, C3, K3, CV3_CC * 9, C2 / CV3_CC, reinterpret_cast<float2*>(c3pre));
   return launched();
 }
 
@@ -1467,6 +1802,19 @@ int launch_conv2(const float* y1, const float* c2, const float* c2pre, Segs s, i
   for (int r0 = 0; r0 < total_rows; r0 += 65535)  // grid.y limit
     conv2_k<<<dim3(C2 / CV2_CH, std::min(65535, total_rows - r0)), TP_THREADS, CV2_SMEM, st>>>(
         y1, c2, reinterpret_cast<const float2*>(c2pre), s, r0, y2);
+  return launched();
+}
+size_t conv3_cert_prep_floats() { return static_cast<size_t>(K3) * C3 + C3; }
+int conv3_cert_prepare(const float* c3, float* prep, cudaStream_t st) {
+  conv3_cert_prep_k<<<(K3 * C3 + 255) / 256, 256, 0, st>>>(c3, prep, prep + K3 * C3);
+  return launched();
+}
+int launch_conv3_cert(const float* y2, const float* c3, const float* prep, Segs s, int total_rows, int8_t* xq,
+                      float* xs, cudaStream_t st) {
+  if (total_rows <= 0) return 0;
+  set_smem(reinterpret_cast<const void*>(conv3_cert_k), C3C_SMEM);
+  conv3_cert_k<<<(total_rows + C3C_R - 1) / C3C_R, C3C_THREADS, C3C_SMEM, st>>>(y2, c3, prep, prep + K3 * C3, s,
+                                                                             total_rows, xq, xs);
   return launched();
 }
 int launch_conv3(const float* y2, const float* c3, const float* c3pre, Segs s, int total_rows, float* y3,
@@ -1693,6 +2041,22 @@ int wk_attention_cublas_part(int part, void* stream, const float* q, const float
   (void)scratch;
   if (part == 0 || part == 1) return 0;
   return attention_abi(stream, q, k, v, t, d, heads, out);
+}
+
+// Parity hook for the certified conv3 + quant: prep = conv3_cert_prep_floats() floats (filled
+// here from c3), roff = device row offsets of nseg segments or nullptr for one segment of `rows`.
+int wasr_conv3_quant(const float* y2, const float* c3, float* prep, const int* roff, int nseg, int rows, int8_t* xq,
+                     float* xs, void* stream) {
+  if (!y2 || !c3 || !prep || !xq || !xs || rows < 0 || (roff && nseg <= 0)) return -1;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (conv3_cert_prepare(c3, prep, st) != 0) return -4;
+  Segs s{};
+  s.foff = nullptr;
+  s.roff = roff;
+  s.n = roff ? nseg : 1;
+  s.t0 = 0;
+  s.t10 = rows;
+  return launch_conv3_cert(y2, c3, prep, s, rows, xq, xs, st);
 }
 
 // Parity hooks for the certified GELU + quant: the engine's kernel choice (exact = 0) or the

@@ -53,6 +53,13 @@ int launch_conv3(const float* y2, const float* c3, const float* c3pre, Segs s, i
 // floats of the stage layout of conv2 (which = 2) or conv3 (which = 3) weights
 size_t conv_pre_floats(int which);
 int conv_prepare(const float* c2, const float* c3, float* c2pre, float* c3pre, cudaStream_t st);
+// conv3 fused with the certified row quantisation of its output (the engine's path): the int8
+// rows and scales equal quant(conv3(y2)) of the reference order; prep holds the transposed
+// weights and weight norms (conv3_cert_prepare, conv3_cert_prep_floats() floats)
+size_t conv3_cert_prep_floats();
+int conv3_cert_prepare(const float* c3, float* prep, cudaStream_t st);
+int launch_conv3_cert(const float* y2, const float* c3, const float* prep, Segs s, int total_rows, int8_t* xq,
+                      float* xs, cudaStream_t st);
 int launch_quant_rows(const float* x, int m, int k, int ldx, int8_t* xq, float* xs, cudaStream_t st);
 int launch_quant_rows_max(const float* x, int m, int k, const unsigned* rowmax, int8_t* xq, float* xs,
                           cudaStream_t st);
