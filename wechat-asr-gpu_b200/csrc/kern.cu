@@ -798,7 +798,14 @@ __device__ __forceinline__ float c3c_fold(float v) {
   return fmaxf(s, 0.0f);
 }
 
-__global__ void __launch_bounds__(C3C_THREADS, 1) conv3_cert_k(const float* __restrict__ y2,
+// Thread (cg, pg)'s 64 outputs: element j = 8a + b is channel o(a), position n(b); the running
+// totals of a stage's partial sums live in tensor memory (this thread's TMEM lane, columns
+// 64 (warp / 4) + j), which leaves the registers to the stage accumulators so that two blocks
+// fit an SM.
+__device__ __forceinline__ int c3c_o(int cg, int a) { return (a < 4 ? 0 : 96) + 4 * cg + (a & 3); }
+__device__ __forceinline__ int c3c_n(int pg, int b) { return (b < 4 ? 0 : 40) + 4 * pg + (b & 3); }
+
+__global__ void __launch_bounds__(C3C_THREADS, 2) conv3_cert_k(const float* __restrict__ y2,
                                                               const float* __restrict__ c3,
                                                               const float* __restrict__ c3t,
                                                               const float* __restrict__ nw_g, Segs s, int total,
@@ -814,13 +821,18 @@ __global__ void __launch_bounds__(C3C_THREADS, 1) conv3_cert_k(const float* __re
   float* na = sm + C3C_OFF_NA;
   float* nw = sm + C3C_OFF_NW;
   int* misc = reinterpret_cast<int*>(sm + C3C_OFF_MISC);
-  int* valid = misc;            // [12]
-  float* rowL = sm + C3C_OFF_MISC + 12;  // [4]
-  float* rowM = sm + C3C_OFF_MISC + 16;  // [4]
+  int* valid = misc;                       // [12]
+  float* rowL = sm + C3C_OFF_MISC + 12;    // [4]
+  float* rowM = sm + C3C_OFF_MISC + 16;    // [4]
   int* cnt = misc + 20;
   int* ovf = misc + 21;
   float* rowInv = sm + C3C_OFF_MISC + 24;  // [4]
-  const int t = threadIdx.x, r0 = blockIdx.x * C3C_R;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(misc + 28);
+  const int t = threadIdx.x, warp = t >> 5, r0 = blockIdx.x * C3C_R;
+  if (warp == 0) {
+    tmem_alloc(tslot, 128);
+    tmem_relinquish();
+  }
   if (t < 12) {
     const int rho = t / 3, i = t % 3, r = r0 + rho;
     bool ok = false;
@@ -852,31 +864,42 @@ __global__ void __launch_bounds__(C3C_THREADS, 1) conv3_cert_k(const float* __re
   load_stage(0, 0);
   const bool act = t < 240;
   const int cg = t % 24, pg = t / 24;
-  float tot[8][8];
+  tc_fence_before();
+  __syncthreads();  // valid[], the TMEM address
+  tc_fence_after();
+  const uint32_t tcol = *tslot + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + static_cast<uint32_t>(64 * (warp >> 2));
+  // the im2col tile's source offsets in a stage's raw rows are the same in every stage: this
+  // thread's elements e = t + 256 m of P, -1 where the input row lies outside the segment
+  constexpr int PB = (C3C_KS * C3C_N + C3C_THREADS - 1) / C3C_THREADS;
+  int poff[PB];
 #pragma unroll
-  for (int a = 0; a < 8; a++)
-#pragma unroll
-    for (int b = 0; b < 8; b++) tot[a][b] = 0.0f;
+  for (int m = 0; m < PB; m++) {
+    const int e = t + C3C_THREADS * m;
+    const int kk = e / C3C_N, n = e - kk * C3C_N, rho = n / 20, f = n - 20 * rho;
+    const int cl = kk / 9, tap = kk - 9 * cl, i = tap / 3, j = tap - 3 * i;
+    poff[m] = (e < C3C_KS * C3C_N && valid[rho * 3 + i]) ? (rho + i) * C3C_RAWR + cl * W2 + 2 * f + j : -1;
+  }
 #pragma unroll 1
   for (int st = 0; st < C3C_NST; st++) {
     cp_async_wait<0>();
     __syncthreads();  // stage st visible; the previous stage's P and buffers consumed
     if (st + 1 < C3C_NST) load_stage(st + 1, (st + 1) & 1);
     const float* rw = raw + (st & 1) * C3C_IN * C3C_RAWR;
-    for (int e = t; e < C3C_KS * C3C_N; e += C3C_THREADS) {
-      const int kk = e / C3C_N, n = e - kk * C3C_N, rho = n / 20, f = n - 20 * rho;
-      const int cl = kk / 9, tap = kk - 9 * cl, i = tap / 3, j = tap - 3 * i;
-      P[e] = valid[rho * 3 + i] ? rw[(rho + i) * C3C_RAWR + cl * W2 + 2 * f + j] : 0.0f;
+#pragma unroll
+    for (int m = 0; m < PB; m++) {
+      const int e = t + C3C_THREADS * m;
+      if (e < C3C_KS * C3C_N) P[e] = poff[m] >= 0 ? rw[poff[m]] : 0.0f;
     }
     __syncthreads();
+    // accumulators in packed pairs: acc[a][q] = (channel a, positions 2q, 2q+1 of the thread's 8)
+    float2 acc[8][4];
+#pragma unroll
+    for (int a = 0; a < 8; a++)
+#pragma unroll
+      for (int q = 0; q < 4; q++) acc[a][q] = make_float2(0.0f, 0.0f);
     if (act) {
       const float* wb = Wst + (st & 1) * C3C_KS * C3 + 4 * cg;
       const float* pb = P + 4 * pg;
-      float acc[8][8];
-#pragma unroll
-      for (int a = 0; a < 8; a++)
-#pragma unroll
-        for (int b = 0; b < 8; b++) acc[a][b] = 0.0f;
 #pragma unroll 4
       for (int kk = 0; kk < C3C_KS; kk++) {
         const float4 w0 = *reinterpret_cast<const float4*>(wb + kk * C3);
@@ -884,18 +907,42 @@ __global__ void __launch_bounds__(C3C_THREADS, 1) conv3_cert_k(const float* __re
         const float4 p0 = *reinterpret_cast<const float4*>(pb + kk * C3C_N);
         const float4 p1 = *reinterpret_cast<const float4*>(pb + kk * C3C_N + 40);
         const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-        const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+        const float2 pv[4] = {make_float2(p0.x, p0.y), make_float2(p0.z, p0.w), make_float2(p1.x, p1.y),
+                              make_float2(p1.z, p1.w)};
 #pragma unroll
-        for (int a = 0; a < 8; a++)
+        for (int a = 0; a < 8; a++) {
+          const float2 wd = make_float2(wv[a], wv[a]);
 #pragma unroll
-          for (int b = 0; b < 8; b++) acc[a][b] = __fmaf_rn(wv[a], pv[b], acc[a][b]);
+          for (int q = 0; q < 4; q++) acc[a][q] = fma2_rn(wd, pv[q], acc[a][q]);
+        }
       }
+    }
+    // running totals (whole warps: tcgen05 ld / st are warp-collective)
 #pragma unroll
-      for (int a = 0; a < 8; a++)
+    for (int h = 0; h < 2; h++) {
+      uint32_t r[32];
+      if (st > 0) {
+        tmem_st_wait();
+        tmem_ld32(tcol + 32 * h, r);
 #pragma unroll
-        for (int b = 0; b < 8; b++) tot[a][b] = __fadd_rn(tot[a][b], acc[a][b]);
+        for (int a = 0; a < 4; a++)
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            const float2 tv = add2_rn(make_float2(__uint_as_float(r[8 * a + 2 * q]), __uint_as_float(r[8 * a + 2 * q + 1])),
+                                      acc[4 * h + a][q]);
+            r[8 * a + 2 * q] = __float_as_uint(tv.x), r[8 * a + 2 * q + 1] = __float_as_uint(tv.y);
+          }
+      } else {
+#pragma unroll
+        for (int a = 0; a < 4; a++)
+#pragma unroll
+          for (int q = 0; q < 4; q++)
+            r[8 * a + 2 * q] = __float_as_uint(acc[4 * h + a][q].x), r[8 * a + 2 * q + 1] = __float_as_uint(acc[4 * h + a][q].y);
+      }
+      tmem_st32(tcol + 32 * h, r);
     }
   }
+  tmem_st_wait();
   __syncthreads();  // every stage consumed: the weight / raw region takes the whole y2 rows
   float* y2s = sm;
   for (int e = t; e < C3C_IN * (C3C_YROW / 4); e += C3C_THREADS) {
@@ -909,7 +956,7 @@ __global__ void __launch_bounds__(C3C_THREADS, 1) conv3_cert_k(const float* __re
   cp_async_wait<0>();
   __syncthreads();
   {  // patch norms: warp w takes positions w, w+8, ...; lanes split the 576 taps
-    const int warp = t >> 5, lane = t & 31;
+    const int lane = t & 31;
     for (int n = warp; n < C3C_N; n += C3C_THREADS / 32) {
       const int rho = n / 20, f = n - 20 * rho;
       float ss = 0.0f;
@@ -925,27 +972,34 @@ __global__ void __launch_bounds__(C3C_THREADS, 1) conv3_cert_k(const float* __re
     }
   }
   __syncthreads();
-  // per-element bound and each row's lower bound of its maximum
-  float E[8][8];
+  // y~ (relu of the totals) for half h of the thread's elements: a in [4h, 4h+4), all b
+  auto load_y = [&](int h, float (&y)[4][8]) {
+    uint32_t r[32];
+    tmem_ld32(tcol + 32 * h, r);
 #pragma unroll
-  for (int a = 0; a < 8; a++)
+    for (int a = 0; a < 4; a++)
 #pragma unroll
-    for (int b = 0; b < 8; b++) {
-      const int o = (a < 4 ? 0 : 96) + 4 * cg + (a & 3), n = (b < 4 ? 0 : 40) + 4 * pg + (b & 3);
-      tot[a][b] = fmaxf(tot[a][b], 0.0f);
-      E[a][b] = act ? __fmul_ru(__fmul_ru(C3C_BOUND, na[n]), nw[o]) : 0.0f;
-    }
-  if (act) {  // positions 4pg..4pg+3 lie in row pA, 40+4pg.. in row pB
+      for (int b = 0; b < 8; b++) y[a][b] = fmaxf(__uint_as_float(r[8 * a + b]), 0.0f);
+  };
+  auto bound = [&](int a, int b) { return __fmul_ru(__fmul_ru(C3C_BOUND, na[c3c_n(pg, b)]), nw[c3c_o(cg, a)]); };
+  {  // each row's lower bound of its maximum; positions 4pg.. lie in row pA, 40+4pg.. in row pB
     float loA = 0.0f, loB = 0.0f;
 #pragma unroll
-    for (int a = 0; a < 8; a++)
+    for (int h = 0; h < 2; h++) {
+      float y[4][8];
+      load_y(h, y);
+      if (act) {
 #pragma unroll
-      for (int b = 0; b < 4; b++) {
-        loA = fmaxf(loA, __fsub_rd(tot[a][b], E[a][b]));
-        loB = fmaxf(loB, __fsub_rd(tot[a][b + 4], E[a][b + 4]));
+        for (int a = 0; a < 4; a++)
+#pragma unroll
+          for (int b = 0; b < 4; b++) {
+            loA = fmaxf(loA, __fsub_rd(y[a][b], bound(4 * h + a, b)));
+            loB = fmaxf(loB, __fsub_rd(y[a][b + 4], bound(4 * h + a, b + 4)));
+          }
       }
-    if (loA > 0.0f) atomicMax(reinterpret_cast<int*>(rowL + (4 * pg) / 20), __float_as_int(loA));
-    if (loB > 0.0f) atomicMax(reinterpret_cast<int*>(rowL + (40 + 4 * pg) / 20), __float_as_int(loB));
+    }
+    if (act && loA > 0.0f) atomicMax(reinterpret_cast<int*>(rowL + (4 * pg) / 20), __float_as_int(loA));
+    if (act && loB > 0.0f) atomicMax(reinterpret_cast<int*>(rowL + (40 + 4 * pg) / 20), __float_as_int(loB));
   }
   __syncthreads();
   // candidates for each row's maximum -> the list (overflow: the whole block runs exactly)
@@ -953,15 +1007,20 @@ __global__ void __launch_bounds__(C3C_THREADS, 1) conv3_cert_k(const float* __re
     const int e = atomicAdd(cnt, 1);
     if (e < C3C_CAP) lst[e] = (rho << 16) | (o << 5) | f; else *ovf = 1;
   };
-  if (act) {
 #pragma unroll
-    for (int a = 0; a < 8; a++)
+  for (int h = 0; h < 2; h++) {
+    float y[4][8];
+    load_y(h, y);
+    if (act) {
 #pragma unroll
-      for (int b = 0; b < 8; b++) {
-        const int o = (a < 4 ? 0 : 96) + 4 * cg + (a & 3), n = (b < 4 ? 0 : 40) + 4 * pg + (b & 3);
-        const int rho = n / 20;
-        if (r0 + rho < total && __fadd_ru(tot[a][b], E[a][b]) >= rowL[rho]) push(rho, o, n - 20 * rho);
-      }
+      for (int a = 0; a < 4; a++)
+#pragma unroll
+        for (int b = 0; b < 8; b++) {
+          const int n = c3c_n(pg, b), rho = n / 20;
+          if (r0 + rho < total && __fadd_ru(y[a][b], bound(4 * h + a, b)) >= rowL[rho])
+            push(rho, c3c_o(cg, 4 * h + a), n - 20 * rho);
+        }
+    }
   }
   __syncthreads();
   const int ncand = min(*cnt, C3C_CAP);
@@ -995,23 +1054,28 @@ __global__ void __launch_bounds__(C3C_THREADS, 1) conv3_cert_k(const float* __re
   } else {
     // every element that is neither a candidate nor near a rounding boundary is quantised from
     // y~; the rest join the list after the candidates
-    if (act) {
 #pragma unroll
-      for (int a = 0; a < 8; a++)
+    for (int h = 0; h < 2; h++) {
+      float y[4][8];
+      load_y(h, y);
+      if (act) {
 #pragma unroll
-        for (int b = 0; b < 8; b++) {
-          const int o = (a < 4 ? 0 : 96) + 4 * cg + (a & 3), n = (b < 4 ? 0 : 40) + 4 * pg + (b & 3);
-          const int rho = n / 20, f = n - 20 * rho;
-          if (r0 + rho >= total || __fadd_ru(tot[a][b], E[a][b]) >= rowL[rho]) continue;
-          const float inv = rowInv[rho];
-          const float lim = __fsub_rd(0.5f, __fadd_ru(__fmul_ru(E[a][b], inv), 0x1p-16f));
-          const float sv = __fmaf_rn(tot[a][b], inv, RINT_MAGIC);
-          const float d = __fmaf_rn(tot[a][b], inv, __fsub_rn(RINT_MAGIC, sv));
-          if (fabsf(d) < lim)
-            qo[rho * FLAT + o * 20 + f] = static_cast<int8_t>(__float_as_uint(sv) & 0xffu);
-          else
-            push(rho, o, f);
-        }
+        for (int a = 0; a < 4; a++)
+#pragma unroll
+          for (int b = 0; b < 8; b++) {
+            const int n = c3c_n(pg, b), rho = n / 20, f = n - 20 * rho, o = c3c_o(cg, 4 * h + a);
+            const float E = bound(4 * h + a, b);
+            if (r0 + rho >= total || __fadd_ru(y[a][b], E) >= rowL[rho]) continue;
+            const float inv = rowInv[rho];
+            const float lim = __fsub_rd(0.5f, __fadd_ru(__fmul_ru(E, inv), 0x1p-16f));
+            const float sv = __fmaf_rn(y[a][b], inv, RINT_MAGIC);
+            const float d = __fmaf_rn(y[a][b], inv, __fsub_rn(RINT_MAGIC, sv));
+            if (fabsf(d) < lim)
+              qo[rho * FLAT + o * 20 + f] = static_cast<int8_t>(__float_as_uint(sv) & 0xffu);
+            else
+              push(rho, o, f);
+          }
+      }
     }
     __syncthreads();
     const int ntot = min(*cnt, C3C_CAP);
@@ -1029,12 +1093,16 @@ __global__ void __launch_bounds__(C3C_THREADS, 1) conv3_cert_k(const float* __re
       for (int b0 = ncand; b0 < ntot; b0 += C3C_THREADS / 8) {
         const int e = b0 + grp, en = lst[min(e, ntot - 1)], rho = en >> 16;
         const float v = c3c_fold(c3c_lane(y2s, c3, ko, valid, rho, (en >> 5) & 255, en & 31, l));
-        if (e < ntot && l == 0)
-          qo[rho * FLAT + ((en >> 5) & 255) * 20 + (en & 31)] = quant_one(v, rowInv[rho]);
+        if (e < ntot && l == 0) qo[rho * FLAT + ((en >> 5) & 255) * 20 + (en & 31)] = quant_one(v, rowInv[rho]);
       }
     }
   }
+  tc_fence_before();
   __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(*tslot, 128);
+  }
   for (int rho = 0; rho < C3C_R; rho++) {
     const int r = r0 + rho;
     if (r >= total) break;
