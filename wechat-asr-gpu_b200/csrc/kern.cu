@@ -1469,6 +1469,8 @@ __global__ void keys_to_ids_k(const unsigned long long* __restrict__ keys, int m
 constexpr int ATT_KC = 32;   // keys per chunk
 constexpr int ATT_RS = 68;   // Q / K row stride in floats: the 8 keys (or 4 row pairs) of a 16-byte load on distinct banks
 constexpr int ATT_A = (ATT_QT + 2 * ATT_KC) * ATT_RS;  // floats of the Q/K (and V) region
+static_assert(2 * ATT_QT * HD + 8 * ATT_QT <= ATT_A, "score phase: Q, the warps' key chunks and maxima");
+static_assert(2 * ATT_KC * HD <= ATT_A, "PV phase: two V chunks");
 
 __host__ __device__ inline int att_pair_stride(int max_t1) { return ((max_t1 + 15) / 16) * 16 + 1; }
 
@@ -1551,6 +1553,59 @@ __device__ __forceinline__ void att_score_chunk(const float* Qr, const float* Kr
   }
 }
 
+// Scores of one 4-key chunk (NK valid keys, rows kept 64 floats apart at Kc) for the row pair
+// (2p, 2p+1) of the swizzled Q tile (16-byte chunk d4 of row r at d4 ^ ((r >> 1) & 7)): all 8
+// dotf lanes of each score in this thread, folded in lane order; score pairs to outp[u]; mx
+// keeps the running maxima of the rows that exist (live0 / live1).
+template <int NK>
+__device__ __forceinline__ void att_score4(const float* Qs, int p, const float* Kc, float2* outp, float (&mx)[2],
+                                           bool live0, bool live1) {
+  const float* Q0 = Qs + 2 * p * HD;
+  const int sw = p & 7;
+  float2 acc[2][NK][4];
+#pragma unroll
+  for (int c = 0; c < 8; c++) {
+    float4 qv[2][2];
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+      qv[r][0] = *reinterpret_cast<const float4*>(Q0 + r * HD + 4 * ((2 * c) ^ sw));
+      qv[r][1] = *reinterpret_cast<const float4*>(Q0 + r * HD + 4 * ((2 * c + 1) ^ sw));
+    }
+#pragma unroll
+    for (int u = 0; u < NK; u++) {
+      const float4 k0 = *reinterpret_cast<const float4*>(Kc + u * HD + 8 * c);
+      const float4 k1 = *reinterpret_cast<const float4*>(Kc + u * HD + 8 * c + 4);
+#pragma unroll
+      for (int r = 0; r < 2; r++) {
+        const float2 p0 = mulp(lo2(qv[r][0]), lo2(k0)), p1 = mulp(hi2(qv[r][0]), hi2(k0));
+        const float2 p2 = mulp(lo2(qv[r][1]), lo2(k1)), p3 = mulp(hi2(qv[r][1]), hi2(k1));
+        if (c == 0) {
+          acc[r][u][0] = p0, acc[r][u][1] = p1, acc[r][u][2] = p2, acc[r][u][3] = p3;
+        } else {
+          acc[r][u][0] = add2_rn(acc[r][u][0], p0);
+          acc[r][u][1] = add2_rn(acc[r][u][1], p1);
+          acc[r][u][2] = add2_rn(acc[r][u][2], p2);
+          acc[r][u][3] = add2_rn(acc[r][u][3], p3);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < NK; u++) {
+    float sc[2];
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+      float x = __fadd_rn(acc[r][u][0].x, acc[r][u][0].y);
+#pragma unroll
+      for (int l = 1; l < 4; l++) x = __fadd_rn(__fadd_rn(x, acc[r][u][l].x), acc[r][u][l].y);
+      sc[r] = __fmul_rn(x, 0.125f);
+    }
+    outp[u] = make_float2(sc[0], sc[1]);
+    if (live0) mx[0] = fmaxf(mx[0], sc[0]);
+    if (live1) mx[1] = fmaxf(mx[1], sc[1]);
+  }
+}
+
 // Softmax passes over the flat element list e = p * t + j of a tile's row pairs p (float2
 // per key j): element e of batch slot k is e0 + 256k.  Loads are clamped to the last element
 // and every exp / quotient is computed unconditionally, so the NB pairs of a batch overlap;
@@ -1630,8 +1685,7 @@ __global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, co
   extern __shared__ __align__(16) float sm[];
   const int sp = att_pair_stride(max_t1);
   unsigned long long* tab = reinterpret_cast<unsigned long long*>(sm);
-  float* Q = sm + 64;                     // [64][68]
-  float* Kb = Q + ATT_QT * ATT_RS;        // [2][32][68]
+  float* Q = sm + 64;                     // score phase: Q [64][64] | K chunks [8 warps][2][4][64] | maxima [8][64]
   float* Vb = Q;                          // [2][32][64] (PV phase)
   float2* S2 = reinterpret_cast<float2*>(Q + ATT_A);  // [32][sp]
   float* ZY = reinterpret_cast<float*>(S2 + (ATT_QT / 2) * sp);  // [32][4]: z and 1/z of each row pair
@@ -1657,43 +1711,78 @@ __global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, co
                    (ld & 3) == 0;
   if (tid < 32) tab[tid] = kExp2Tab[tid];
   const int warp = tid >> 5, lane = tid & 31;
-  const int nchunks = (t + ATT_KC - 1) / ATT_KC;
-  // ---- scores
-  att_copy_rows(Q, ATT_RS, q, ld, rb + i0, ni, h, tid, a16);
-  att_copy_rows(Kb, ATT_RS, k, ld, rb, min(ATT_KC, t), h, tid, a16);
+  const int nchunks = (t + ATT_KC - 1) / ATT_KC;  // 32-key chunks of the PV loop
+  // ---- scores.  The tile's rows go to the lanes (lane p: rows 2p, 2p+1), its keys to the warps
+  // (warp w: 4-key chunks [w nc / 8, (w+1) nc / 8) of the nc = ceil(t / 4)), each warp streaming
+  // its own chunks by cp.async into a private double buffer, so the loop needs no block barrier.
+  // Q rows lie 64 floats apart with the 16-byte chunk d4 of row r at d4 ^ ((r >> 1) & 7): the 8
+  // row pairs of a quarter warp hit 8 distinct bank groups, and the key loads are broadcasts.
   {
-    // warp w: rows 8w .. 8w+7; lane = kg + 8 rg: rows 8w + 2rg and 8w + 2rg + 1, keys kg + 8u
-    const int kg = lane & 7, rg = lane >> 3, row0 = 8 * warp + 2 * rg;
-    const bool live = 8 * warp < ni;  // warp-uniform
-    const float* Qr = Q + row0 * ATT_RS;
-    float2* outp = S2 + (row0 >> 1) * sp;
-    float mx[2] = {-3.40282347e+38f, -3.40282347e+38f};
-    for (int ch = 0; ch < nchunks; ch++) {
-      const int j0 = ch * ATT_KC, nj = min(ATT_KC, t - j0);
-      cp_async_wait<0>();
-      __syncthreads();  // chunk ch (and Q) visible; chunk ch-1 consumed by every warp
-      if (ch + 1 < nchunks)
-        att_copy_rows(Kb + ((ch + 1) & 1) * ATT_KC * ATT_RS, ATT_RS, k, ld, rb + j0 + ATT_KC,
-                      min(ATT_KC, t - j0 - ATT_KC), h, tid, a16);
-      const float* Kr = Kb + (ch & 1) * ATT_KC * ATT_RS + kg * ATT_RS;
-      if (live) {
-        // 8-key groups holding keys of the segment: all four but in a segment's last chunk
-        switch (min(4, (nj + 7) >> 3)) {
-          case 4: att_score_chunk<4>(Qr, Kr, kg, nj, outp + j0, mx); break;
-          case 3: att_score_chunk<3>(Qr, Kr, kg, nj, outp + j0, mx); break;
-          case 2: att_score_chunk<2>(Qr, Kr, kg, nj, outp + j0, mx); break;
-          default: att_score_chunk<1>(Qr, Kr, kg, nj, outp + j0, mx); break;
-        }
+    float* Qs = Q;                                          // [64][64], swizzled
+    float* Kw = Qs + ATT_QT * HD + warp * (2 * 4 * HD);     // [2][4][64] this warp's chunks
+    float* Mw = Qs + 2 * ATT_QT * HD;                       // [8 warps][64 rows] maxima
+    for (int e = tid; e < ni * 16; e += 256) {
+      const int r = e >> 4, d4 = e & 15;
+      const float* g = q + static_cast<int64_t>(rb + i0 + r) * ld + h * HD + 4 * d4;
+      float* d = Qs + r * HD + 4 * (d4 ^ ((r >> 1) & 7));
+      if (a16) {
+        cp_async16(d, g);
+      } else {
+#pragma unroll
+        for (int u = 0; u < 4; u++) cp_async4(d + u, g + u);
       }
     }
-    // the 8 lanes of a row pair (lane bits 0-2) hold the same rows
+    cp_async_commit();
+    const int nc = (t + 3) >> 2, cb = (warp * nc) >> 3, ce = ((warp + 1) * nc) >> 3;
+    auto copy_chunk = [&](int c, int buf) {  // keys 4c .. 4c+3 (those below t)
+      const int j0 = 4 * c, nk = min(4, t - j0);
+      for (int e = lane; e < nk * 16; e += 32) {
+        const int u = e >> 4, d4 = e & 15;
+        const float* g = k + static_cast<int64_t>(rb + j0 + u) * ld + h * HD + 4 * d4;
+        float* d = Kw + buf * 4 * HD + u * HD + 4 * d4;
+        if (a16) {
+          cp_async16(d, g);
+        } else {
 #pragma unroll
-    for (int m = 0; m < 2; m++) {
-      mx[m] = fmaxf(mx[m], __shfl_xor_sync(0xffffffffu, mx[m], 1));
-      mx[m] = fmaxf(mx[m], __shfl_xor_sync(0xffffffffu, mx[m], 2));
-      mx[m] = fmaxf(mx[m], __shfl_xor_sync(0xffffffffu, mx[m], 4));
+          for (int w4 = 0; w4 < 4; w4++) cp_async4(d + w4, g + w4);
+        }
+      }
+      cp_async_commit();
+    };
+    if (cb < ce) copy_chunk(cb, 0);
+    cp_async_wait<0>();
+    __syncthreads();  // Q visible to every warp
+    const bool live0 = 2 * lane < ni, live1 = 2 * lane + 1 < ni;
+    float2* outp = S2 + lane * sp;
+    float mx[2] = {-3.40282347e+38f, -3.40282347e+38f};
+    for (int c = cb; c < ce; c++) {
+      const int buf = (c - cb) & 1;
+      if (c + 1 < ce) {
+        copy_chunk(c + 1, buf ^ 1);
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
+      __syncwarp();  // chunk c landed for every lane of the warp
+      const int j0 = 4 * c;
+      const float* Kc = Kw + buf * 4 * HD;
+      switch (min(4, t - j0)) {
+        case 4: att_score4<4>(Qs, lane, Kc, outp + j0, mx, live0, live1); break;
+        case 3: att_score4<3>(Qs, lane, Kc, outp + j0, mx, live0, live1); break;
+        case 2: att_score4<2>(Qs, lane, Kc, outp + j0, mx, live0, live1); break;
+        default: att_score4<1>(Qs, lane, Kc, outp + j0, mx, live0, live1); break;
+      }
+      __syncwarp();  // every lane is done with buffer buf before chunk c+2 goes into it
     }
-    if (live && kg == 0) Mx[row0] = mx[0], Mx[row0 + 1] = mx[1];
+    Mw[warp * ATT_QT + 2 * lane] = mx[0];
+    Mw[warp * ATT_QT + 2 * lane + 1] = mx[1];
+    __syncthreads();
+    if (tid < ATT_QT) {
+      float m = Mw[tid];
+#pragma unroll
+      for (int w = 1; w < 8; w++) m = fmaxf(m, Mw[w * ATT_QT + tid]);
+      Mx[tid] = m;
+    }
   }
   __syncthreads();  // scores and row maxima complete; the Q/K region is free
   // the first V chunk streams in while the softmax runs
