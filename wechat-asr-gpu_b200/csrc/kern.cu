@@ -1454,20 +1454,23 @@ __global__ void keys_to_ids_k(const unsigned long long* __restrict__ keys, int m
 // p_j * v_j[d] from 0 (src/model.rs:714-738).  Every element keeps the reference's exact
 // sequence of rounded multiplies and adds.
 //
-// Register tiles.  Scores: a thread owns one row pair x 4 keys (kg + 8u, u < 4) of a 32-key
-// chunk with all 8 dotf lanes of each score as 4 float2 (lane l holds dims 8c + l), so the lane
-// fold is 7 adds in one thread, in the reference order.  A lane's first step starts from the
-// product itself rather than 0 + product: the two differ at most in the sign of a zero, which
-// no later step can see (a zero score enters the softmax only through s - max and exp).  PV: a thread owns row
-// pairs (2p, 2p+1) for p = pa, pa+1 x head dims d0..d0+3; the accumulators pair (row 2p, dim d)
-// with (row 2p+1, dim d^1).  K and V chunks stream through two shared buffers by cp.async,
-// one barrier per chunk.  Shared layout: exp table | Q [64][72] + K [2][32][72] (scores) /
-// V [2][32][64] (PV) | S2 [32 row pairs][sp] float2 | ZY [32][4] | Mx [64].
-// Softmax: the row maxima come out of the score loop (each thread's running maximum, reduced
-// over the 8 thread pairs of a warp that share a row); the exp and divide passes run flat over
-// (row pair, key) with every thread on independent elements; z is one thread per row.
+// Register tiles.  Scores: lane p of every warp owns the tile's row pair (2p, 2p+1), and warp w
+// a contiguous run of 4-key chunks; a thread holds its row pair x 4 keys with all 8 dotf lanes of
+// each score as 4 float2 (lane l holds dims 8c + l), so the lane fold is 7 adds in one thread,
+// in the reference order.  A lane's first step starts from the product itself rather than
+// 0 + product: the two differ at most in the sign of a zero, which no later step can see (a
+// zero score enters the softmax only through s - max and exp).  Each warp streams its chunks
+// through a private double buffer (cp.async, warp-level sync only); Q is staged once with its
+// 16-byte chunks XOR-swizzled by row pair.  PV: a thread owns row pairs (2p, 2p+1) for
+// p = pa, pa+1 x head dims d0..d0+3; the accumulators pair (row 2p, dim d) with (row 2p+1,
+// dim d^1); V chunks of 32 keys stream through two shared buffers, one barrier per chunk.
+// Shared layout: exp table | Q [64][64] + key chunks [8 warps][2][4][64] + per-warp maxima
+// [8][64] (scores) / V [2][32][64] (PV) | S2 [32 row pairs][sp] float2 | ZY [32][4] | Mx [64].
+// Softmax: the row maxima are the maxima of the warps' running maxima; the exp and divide
+// passes run flat over (row pair, key) with every thread on independent elements; z is one
+// thread per row.
 constexpr int ATT_KC = 32;   // keys per chunk
-constexpr int ATT_RS = 68;   // Q / K row stride in floats: the 8 keys (or 4 row pairs) of a 16-byte load on distinct banks
+constexpr int ATT_RS = 68;   // row stride in floats that sizes the Q/K/V region
 constexpr int ATT_A = (ATT_QT + 2 * ATT_KC) * ATT_RS;  // floats of the Q/K (and V) region
 static_assert(2 * ATT_QT * HD + 8 * ATT_QT <= ATT_A, "score phase: Q, the warps' key chunks and maxima");
 static_assert(2 * ATT_KC * HD <= ATT_A, "PV phase: two V chunks");
@@ -1498,59 +1501,6 @@ __device__ __forceinline__ void att_copy_rows(float* dst, int ds, const float* _
     }
   }
   cp_async_commit();
-}
-
-// Scores of one 32-key chunk for the query rows Qr and Qr + ATT_RS (row stride ATT_RS) and keys
-// kg + 8u, u < NU (groups past the end of a segment are skipped whole) at Kr + 8u ATT_RS.  The
-// score pairs of the two rows go to out[j]; mx keeps the running row maxima (order-free).
-template <int NU>
-__device__ __forceinline__ void att_score_chunk(const float* Qr, const float* Kr, int kg, int nj, float2* out,
-                                                float (&mx)[2]) {
-  float2 acc[2][NU][4];
-#pragma unroll
-  for (int c = 0; c < 8; c++) {
-    float4 qv[2][2];
-#pragma unroll
-    for (int r = 0; r < 2; r++) {
-      qv[r][0] = *reinterpret_cast<const float4*>(Qr + r * ATT_RS + 8 * c);
-      qv[r][1] = *reinterpret_cast<const float4*>(Qr + r * ATT_RS + 8 * c + 4);
-    }
-#pragma unroll
-    for (int u = 0; u < NU; u++) {
-      const float4 k0 = *reinterpret_cast<const float4*>(Kr + 8 * u * ATT_RS + 8 * c);
-      const float4 k1 = *reinterpret_cast<const float4*>(Kr + 8 * u * ATT_RS + 8 * c + 4);
-#pragma unroll
-      for (int r = 0; r < 2; r++) {
-        const float2 p0 = mulp(lo2(qv[r][0]), lo2(k0)), p1 = mulp(hi2(qv[r][0]), hi2(k0));
-        const float2 p2 = mulp(lo2(qv[r][1]), lo2(k1)), p3 = mulp(hi2(qv[r][1]), hi2(k1));
-        if (c == 0) {
-          acc[r][u][0] = p0, acc[r][u][1] = p1, acc[r][u][2] = p2, acc[r][u][3] = p3;
-        } else {
-          acc[r][u][0] = add2_rn(acc[r][u][0], p0);
-          acc[r][u][1] = add2_rn(acc[r][u][1], p1);
-          acc[r][u][2] = add2_rn(acc[r][u][2], p2);
-          acc[r][u][3] = add2_rn(acc[r][u][3], p3);
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int u = 0; u < NU; u++) {
-    float sc[2];
-#pragma unroll
-    for (int r = 0; r < 2; r++) {
-      float x = __fadd_rn(acc[r][u][0].x, acc[r][u][0].y);
-#pragma unroll
-      for (int l = 1; l < 4; l++) x = __fadd_rn(__fadd_rn(x, acc[r][u][l].x), acc[r][u][l].y);
-      sc[r] = __fmul_rn(x, 0.125f);
-    }
-    const int j = kg + 8 * u;
-    if (j < nj) {
-      out[j] = make_float2(sc[0], sc[1]);
-      mx[0] = fmaxf(mx[0], sc[0]);
-      mx[1] = fmaxf(mx[1], sc[1]);
-    }
-  }
 }
 
 // Scores of one 4-key chunk (NK valid keys, rows kept 64 floats apart at Kc) for the row pair
