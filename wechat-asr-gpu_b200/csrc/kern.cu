@@ -735,12 +735,15 @@ __global__ void __launch_bounds__(256) ln_quant_any_k(float* __restrict__ h, con
 // the row maximum and every element near a rounding boundary from the reference-order value
 // (the same reasoning as the certified GELU).
 //
-// Bound.  For output (o, f) with patch a and weight row w: the dotf result (one rounded product
-// and at most 72 + 7 + 1 rounded adds per term) is within g80 * sum |a_k w_k| of the exact sum;
-// the fused multiply-add value (per 36-tap stage a chain of at most 36 roundings from zero, then
-// 16 adds of the stage partials) within g52 * sum |a_k w_k|; relu is 1-Lipschitz; and
-// sum |a_k w_k| <= |a|_2 |w|_2.  So |y~ - y| <= E = C3C_BOUND * na(f) * nw(o), g_n = n u / (1 - n u),
-// u = 2^-24, with na and nw upper bounds of the norms.
+// Bound.  For output (o, f) with patch a and weight row w, both sums are the exact sum with term
+// k multiplied by at most n(k) factors (1 + d), |d| <= u = 2^-24: in the dotf order its product,
+// the adds of its lane chain from chunk c = k / 8 on (72 - c) and the lane fold (7 for lanes 0
+// and 1, 8 - l for lane l >= 2); in the fused multiply-add order the stage chain from tap
+// i = k % 36 on (36 - i) and the adds of the stage partials into the total (15 for stage 0,
+// 16 - s for stage s >= 1).  Both n <= 131, so each sum is within u (1 + 2^-10) sum_k
+// |a_k w_k| n(k) of the exact sum, relu is 1-Lipschitz, and by Cauchy-Schwarz
+// |y~ - y| <= E = C3C_BOUND * na(f) * nw(o), with na >= |a|_2 and nw >= |w o n|_2 (the weight
+// row scaled by the two depths, computed once per model).
 //
 // Work split: a block owns 4 output rows (80 positions) and all 192 channels, 16 stages of 4
 // input channels (36 taps).  Per stage the weights [36 taps][192] (pre-transposed once per model)
@@ -772,8 +775,8 @@ constexpr int C3C_OFF_NW = C3C_OFF_NA + C3C_N;                    // [192]
 constexpr int C3C_OFF_MISC = C3C_OFF_NW + C3;                     // ints: valid[12], L[4], M[4], cnt, ovf
 constexpr int C3C_SMEM = (C3C_OFF_MISC + 32) * 4;
 static_assert(C3C_IN * C3C_YROW <= C3C_OFF_P, "the staged y2 rows reuse the weight / raw buffers");
-// (80 + 52 + 1) * 2^-24 * (1 + 2^-10): the two g_n above, with margin for their 1/(1 - n u)
-constexpr float C3C_BOUND = 133.2f * 0x1p-24f;
+// u (1 + 2^-10): the first-order bound above with margin for its (1 + u)^n - 1 <= n u (1 + n u)
+constexpr float C3C_BOUND = 0x1p-24f * (1.0f + 0x1p-10f);
 
 // lane l's dotf chain (taps l, l+8, ..., l+568) of output (row rho, channel o, position f) from
 // the staged y2 rows; valid[rho*3 + i] says whether input row rho+i-1 is inside the segment
@@ -1113,8 +1116,13 @@ __global__ void __launch_bounds__(C3C_THREADS, 2) conv3_cert_k(const float* __re
   }
 }
 
-// c3t[k][o] = c3[o][k] (the stage tiles of conv3_cert_k) and nw[o] >= |c3[o]|_2 (the square
-// root of the double sum of squares, rounded up), once per model
+// c3t[k][o] = c3[o][k] (the stage tiles of conv3_cert_k) and nw[o] >= |c3[o] o n|_2, n(k) the
+// rounding depth of tap k in the two summation orders (see the bound above), from the double
+// sum of squares rounded up; once per model
+__device__ __forceinline__ int c3c_depth(int k) {
+  const int c = k / 8, l = k % 8, s = k / C3C_KS, i = k % C3C_KS;
+  return 1 + (72 - c) + (l < 2 ? 7 : 8 - l) + (C3C_KS - i) + (s == 0 ? C3C_NST - 1 : C3C_NST - s);
+}
 __global__ void conv3_cert_prep_k(const float* __restrict__ c3, float* __restrict__ c3t, float* __restrict__ nw) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < K3 * C3) {
@@ -1123,7 +1131,10 @@ __global__ void conv3_cert_prep_k(const float* __restrict__ c3, float* __restric
   }
   if (i < C3) {
     double ss = 0.0;
-    for (int k = 0; k < K3; k++) ss += static_cast<double>(c3[static_cast<int64_t>(i) * K3 + k]) * c3[static_cast<int64_t>(i) * K3 + k];
+    for (int k = 0; k < K3; k++) {
+      const double w = static_cast<double>(c3[static_cast<int64_t>(i) * K3 + k]) * c3c_depth(k);
+      ss += w * w;
+    }
     nw[i] = __double2float_ru(__dsqrt_ru(ss) * (1.0 + 0x1p-40));
   }
 }
