@@ -132,15 +132,17 @@ def algorithmic_work(t1_list, n_layers=40, vocab=10502):
         "gemm_out_argmax": 2 * rows * D * vocab,
     }
     # bytes: attention reads q,k,v (fp32) once and writes the output; LN reads h, writes int8 + scale;
-    # conv2 reads y1 rows once and writes y2; conv3 reads y2 and writes y3; quant reads fp32 rows
-    # and writes int8
+    # conv2 reads y1 rows once and writes y2; conv3 (with its quantisation fused) reads y2 and
+    # writes int8 rows + scales; GELU + quant reads the FF1 output and writes int8 + scale; quant
+    # (attention output, final h) reads fp32 rows and writes int8
     byts = {
         "attention": n_layers * rows * (3 * D * 4 + D * 4),
         "layernorm": 2 * n_layers * rows * (D * 4 + D + 4),
         "conv2": rows * (5 * 32 * 40 * 4 + 64 * 41 * 4),
-        "conv3": rows * (64 * 41 * 4 + FLAT * 4),
+        "conv3": rows * (64 * 41 * 4 + FLAT + 4),
         "conv1": rows * 5 * (40 * 4 + 32 * 40 * 4),
-        "quant": rows * ((FLAT + n_layers * (D + FF) + D) * 5),
+        "gelu_quant": n_layers * rows * (FF * 4 + FF + 4),
+        "quant": rows * ((n_layers * D + D) * 5),
     }
     flops = {"attention": n_layers * 4.0 * sq * D}
     # exactly rounded fp32 multiply-adds (one FMUL + one FADD each on the CUDA-core pipe): the
@@ -148,9 +150,11 @@ def algorithmic_work(t1_list, n_layers=40, vocab=10502):
     macs = {
         "attention": n_layers * sq * 8 * 64 * 2,      # QK^T and PV, 8 heads of 64
         "conv2": rows * 64 * 40 * 32 * 49,
-        "conv3": rows * 192 * 20 * 64 * 9,
     }
-    return ops, byts, flops, rows, macs
+    # fused multiply-adds (one fp32 lane-op each): conv3 sums its products in any order and
+    # certifies the quantised result against the reference order
+    fmas = {"conv3": rows * 192 * 20 * 64 * 9}
+    return ops, byts, flops, rows, macs, fmas
 
 
 # ---------------------------------------------------------------- int8 GEMM probe
@@ -561,7 +565,7 @@ def main():
     i8 = int8_peak(pkg, local, stream)
     i8_peak = i8["tops"] if i8["rc"] == 0 and i8["wait_error"] == 0 else 2 * bf16
     names = pkg.abi.KERNEL_CLASSES
-    ops, byts, flops, rows, macs = algorithmic_work(t1, plan.n_layers)
+    ops, byts, flops, rows, macs, fmas = algorithmic_work(t1, plan.n_layers)
     dom = max(range(len(names)), key=lambda i: prof_ms[i])
     dname = names[dom]
     dms = prof_ms[dom]
@@ -616,6 +620,15 @@ def main():
                               "frac": round(macs[k] / (prof_ms[names.index(k)] / 1e3) / 1e12 / peak_mac, 4),
                               "ms": round(prof_ms[names.index(k)], 3)}
                           for k in macs if prof_ms[names.index(k)] > 0}
+    peak_fma = 2 * peak_mac  # one lane-op per fused multiply-add
+    roof["fma_fp32"] = {k: {"tfma_s": round(fmas[k] / (prof_ms[names.index(k)] / 1e3) / 1e12, 3),
+                            "frac": round(fmas[k] / (prof_ms[names.index(k)] / 1e3) / 1e12 / peak_fma, 4),
+                            "peak": round(peak_fma, 2), "ms": round(prof_ms[names.index(k)], 3)}
+                        for k in fmas if prof_ms[names.index(k)] > 0}
+    roof["hbm_classes"] = {k: {"gbs": round(byts[k] / (prof_ms[names.index(k)] / 1e3) / 1e9, 1),
+                               "frac": round(byts[k] / (prof_ms[names.index(k)] / 1e3) / 1e9 / hbm, 4),
+                               "ms": round(prof_ms[names.index(k)], 3)}
+                           for k in ("gelu_quant", "layernorm", "quant") if k in byts and prof_ms[names.index(k)] > 0}
     roof["kernel_ms_last_step"] = {names[i]: round(prof_ms[i], 3) for i in range(len(names)) if prof_n[i]}
 
     gprobe = gemm_probe(pkg, local, stream, i8_peak) if (rank == 0 and not args.no_gemm_probe) else None
