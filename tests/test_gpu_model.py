@@ -125,6 +125,29 @@ def test_batched_ragged_equals_one_by_one(pkg, gpu_lib):
         eng.close()
 
 
+def test_large_chunk_two_branches_equal_small_chunks(pkg, gpu_lib):
+    """A chunk of at least 40,000 rows runs as two halves of its windows on two streams (one
+    graph with two branches); its ids equal those of the same windows run as chunks below that
+    size (one stream), graph captured and replayed."""
+    blob, plan = pkg.synth.make_model(seed=6, n_layers=2)
+    lengths = pkg.synth.config_lengths(4)[:300]
+    wins = [pkg.fbank(pkg.synth.make_audio(500 + i, s))[0] for i, s in enumerate(lengths)]
+    rows = sum((w.shape[0] - 5) // 5 + 1 for w in wins)
+    assert rows >= 40000, rows
+    big = pkg.Engine(blob, plan, max_rows=rows)
+    small = pkg.Engine(blob, plan, max_rows=16384)
+    try:
+        ids_small = small.forward(wins)
+        ids_big = big.forward(wins)
+        ids_big2 = big.forward(wins)
+        for a, b, c in zip(ids_small, ids_big, ids_big2):
+            np.testing.assert_array_equal(a, b)
+            np.testing.assert_array_equal(a, c)
+    finally:
+        big.close()
+        small.close()
+
+
 def test_transcribe_schedule_vs_oracle(pkg, orc, gpu_lib):
     """src/stream.rs schedule (commit windows, blank-pair cut, tail decode, whole utterance
     <= 2000 frames) over a batch of utterances, 4-layer model."""

@@ -84,6 +84,9 @@ struct WasrModel {
   int seg_cap = 0;
   int* err_host = nullptr;
   int* err_dev = nullptr;
+  // second branch of a chunk's forward (small chunks run as two halves that overlap)
+  cudaStream_t side = nullptr;
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
   bool graphs = true;
   bool prof = false;
   int64_t launches = 0;
@@ -204,7 +207,8 @@ struct Launcher {
   int operator()(int cat, F&& f) {
     Rec r{cat, nullptr, nullptr};
     // during stream capture a plain record only becomes a dependency edge; the External flag
-    // makes it a real event-record node that is timed at every replay
+    // makes it a real event-record node that is timed at every replay (profiling runs every
+    // chunk on the model's stream alone)
     if (recs) {
       if (cudaEventCreate(&r.a) != cudaSuccess || cudaEventCreate(&r.b) != cudaSuccess) return -4;
       cudaEventRecordWithFlags(r.a, m->stream, cudaEventRecordExternal);
@@ -219,11 +223,24 @@ struct Launcher {
   }
 };
 
-// Enqueue the whole forward of one chunk on m->stream.  The chunk's frames are at m->feats;
-// seg points at its device segment tables [foff n+1 | roff n+1 | toff n+1 | tord tiles].
-int enqueue_chunk(WasrModel* m, const Chunk& c, const int* seg, float* logits, Launcher& K) {
-  cudaStream_t st = m->stream;
+// Enqueue the whole forward of windows c on stream st.  Their frames are at m->feats + fo
+// frames; every per-row buffer is used from row ro on (so two halves of a chunk can run at once
+// on their own rows); seg points at their device segment tables [foff n+1 | roff n+1 | toff
+// n+1 | tord tiles].
+int enqueue_chunk(WasrModel* m, const Chunk& c, const int* seg, float* logits, Launcher& K, cudaStream_t st,
+                  int64_t fo, int64_t ro) {
   const int n = c.w1 - c.w0;
+  float* const feats = m->feats + fo * DIM;
+  float* const y1 = m->y1 + fo * C1 * DIM;
+  float* const y2 = m->y2 + ro * C2 * W2;
+  int8_t* const xq = m->xq + ro * FLAT;
+  float* const xs = m->xs + ro;
+  float* const hh = m->h + ro * D;
+  float* const qkv = m->qkv + ro * 3 * D;
+  float* const att = m->att + ro * D;
+  float* const ff = m->f + ro * FF;
+  unsigned long long* const keys = m->keys + ro;
+  uint32_t* const ids = m->ids + ro;
   Segs s{};
   s.foff = seg;
   s.roff = seg + (n + 1);
@@ -233,17 +250,17 @@ int enqueue_chunk(WasrModel* m, const Chunk& c, const int* seg, float* logits, L
   const int M = c.rows;
   const WasrPlan& P = m->plan;
   // conv frontend -> int8 rows of y3 -> linear (src/model.rs:389-478,489)
-  TRY(K(WASR_K_CONV1, [&] { return launch_conv1(m->feats, fptr(m, P.c1), s, c.frames, m->y1, st); }));
-  TRY(K(WASR_K_CONV2, [&] { return launch_conv2(m->y1, fptr(m, P.c2), m->c2pre, s, M, m->y2, st); }));
+  TRY(K(WASR_K_CONV1, [&] { return launch_conv1(feats, fptr(m, P.c1), s, c.frames, y1, st); }));
+  TRY(K(WASR_K_CONV2, [&] { return launch_conv2(y1, fptr(m, P.c2), m->c2pre, s, M, y2, st); }));
   // conv3 with its row quantisation fused and certified (int8 rows identical to quant(conv3))
-  TRY(K(WASR_K_CONV3, [&] { return launch_conv3_cert(m->y2, fptr(m, P.c3), m->c3cert, s, M, m->xq, m->xs, st); }));
-  TRY(K(WASR_K_GEMM_LIN, [&] { return gemm_run(gemm_args(m, m->xq, m->xs, M, FLAT, P.lin, D, P.lin_b, EPI_F32, m->h, D), st); }));
+  TRY(K(WASR_K_CONV3, [&] { return launch_conv3_cert(y2, fptr(m, P.c3), m->c3cert, s, M, xq, xs, st); }));
+  TRY(K(WASR_K_GEMM_LIN, [&] { return gemm_run(gemm_args(m, xq, xs, M, FLAT, P.lin, D, P.lin_b, EPI_F32, hh, D), st); }));
   for (int l = 0; l < P.n_layers; l++) {
     const WasrLayer& L = P.layers[l];
     // prior norm -> q, k, v
-    TRY(K(WASR_K_LN, [&] { return launch_ln_quant(m->h, nullptr, fptr(m, L.pn_g), fptr(m, L.pn_b), M, m->xq, m->xs, st); }));
+    TRY(K(WASR_K_LN, [&] { return launch_ln_quant(hh, nullptr, fptr(m, L.pn_g), fptr(m, L.pn_b), M, xq, xs, st); }));
     if (m->qkv_fused[l]) {
-      GemmArgs g = gemm_args(m, m->xq, m->xs, M, D, L.q, 3 * D, WASR_NONE, EPI_F32, m->qkv, 3 * D);
+      GemmArgs g = gemm_args(m, xq, xs, M, D, L.q, 3 * D, WASR_NONE, EPI_F32, qkv, 3 * D);
       g.ws_vec = m->qkv_scale[l];
       g.bias = m->qkv_bias[l];
       TRY(K(WASR_K_GEMM_QKV, [&] { return gemm_run(g, st); }));
@@ -252,33 +269,33 @@ int enqueue_chunk(WasrModel* m, const Chunk& c, const int* seg, float* logits, L
       const uint64_t pb[3] = {L.qb, L.kb, L.vb};
       for (int p = 0; p < 3; p++)
         TRY(K(WASR_K_GEMM_QKV, [&] {
-          return gemm_run(gemm_args(m, m->xq, m->xs, M, D, *pm[p], D, pb[p], EPI_F32, m->qkv + p * D, 3 * D), st);
+          return gemm_run(gemm_args(m, xq, xs, M, D, *pm[p], D, pb[p], EPI_F32, qkv + p * D, 3 * D), st);
         }));
     }
     // attention -> quant -> o projection, residual fused (src/model.rs:493)
-    TRY(K(WASR_K_ATTN, [&] { return launch_attention(m->qkv, m->qkv + D, m->qkv + 2 * D, 3 * D, s, toff, tord, c.tiles, c.max_t1, m->att, D, st); }));
-    TRY(K(WASR_K_QUANT, [&] { return launch_quant_rows(m->att, M, D, D, m->xq, m->xs, st); }));
-    TRY(K(WASR_K_GEMM_O, [&] { return gemm_run(gemm_args(m, m->xq, m->xs, M, D, L.o, D, L.ob, EPI_F32_ADD, m->h, D), st); }));
+    TRY(K(WASR_K_ATTN, [&] { return launch_attention(qkv, qkv + D, qkv + 2 * D, 3 * D, s, toff, tord, c.tiles, c.max_t1, att, D, st); }));
+    TRY(K(WASR_K_QUANT, [&] { return launch_quant_rows(att, M, D, D, xq, xs, st); }));
+    TRY(K(WASR_K_GEMM_O, [&] { return gemm_run(gemm_args(m, xq, xs, M, D, L.o, D, L.ob, EPI_F32_ADD, hh, D), st); }));
     // middle norm -> f1 + bias + GELU (+ row max) -> quant -> f2 + bias, residual fused
-    TRY(K(WASR_K_LN, [&] { return launch_ln_quant(m->h, nullptr, fptr(m, L.mn_g), fptr(m, L.mn_b), M, m->xq, m->xs, st); }));
+    TRY(K(WASR_K_LN, [&] { return launch_ln_quant(hh, nullptr, fptr(m, L.mn_g), fptr(m, L.mn_b), M, xq, xs, st); }));
     TRY(K(WASR_K_GEMM_F1, [&] {
-      return gemm_run(gemm_args(m, m->xq, m->xs, M, D, L.f1, FF, L.f1b, EPI_F32, m->f, FF), st);
+      return gemm_run(gemm_args(m, xq, xs, M, D, L.f1, FF, L.f1b, EPI_F32, ff, FF), st);
     }));
-    TRY(K(WASR_K_GELU, [&] { return launch_gelu_quant_ro(m->f, M, FF, m->xq, m->xs, st); }));
-    TRY(K(WASR_K_GEMM_F2, [&] { return gemm_run(gemm_args(m, m->xq, m->xs, M, FF, L.f2, D, L.f2b, EPI_F32_ADD, m->h, D), st); }));
+    TRY(K(WASR_K_GELU, [&] { return launch_gelu_quant_ro(ff, M, FF, xq, xs, st); }));
+    TRY(K(WASR_K_GEMM_F2, [&] { return gemm_run(gemm_args(m, xq, xs, M, FF, L.f2, D, L.f2b, EPI_F32_ADD, hh, D), st); }));
   }
   // output layer + argmax (src/model.rs:498-501)
-  TRY(K(WASR_K_QUANT, [&] { return launch_quant_rows(m->h, M, D, D, m->xq, m->xs, st); }));
+  TRY(K(WASR_K_QUANT, [&] { return launch_quant_rows(hh, M, D, D, xq, xs, st); }));
   if (logits) {
-    TRY(K(WASR_K_GEMM_OUT, [&] { return gemm_run(gemm_args(m, m->xq, m->xs, M, D, P.out, P.out_n, P.out_b, EPI_F32, logits, P.out_n), st); }));
-    TRY(K(WASR_K_IDS, [&] { return launch_argmax_rows(logits, M, P.out_n, m->ids, st); }));
+    TRY(K(WASR_K_GEMM_OUT, [&] { return gemm_run(gemm_args(m, xq, xs, M, D, P.out, P.out_n, P.out_b, EPI_F32, logits, P.out_n), st); }));
+    TRY(K(WASR_K_IDS, [&] { return launch_argmax_rows(logits, M, P.out_n, ids, st); }));
   } else {
-    if (cudaMemsetAsync(m->keys, 0, static_cast<size_t>(M) * sizeof(unsigned long long), st) != cudaSuccess)
+    if (cudaMemsetAsync(keys, 0, static_cast<size_t>(M) * sizeof(unsigned long long), st) != cudaSuccess)
       return -4;
-    GemmArgs g = gemm_args(m, m->xq, m->xs, M, D, P.out, P.out_n, P.out_b, EPI_ARGMAX, nullptr, P.out_n);
-    g.keys = m->keys;
+    GemmArgs g = gemm_args(m, xq, xs, M, D, P.out, P.out_n, P.out_b, EPI_ARGMAX, nullptr, P.out_n);
+    g.keys = keys;
     TRY(K(WASR_K_GEMM_OUT, [&] { return gemm_run(g, st); }));
-    TRY(K(WASR_K_IDS, [&] { return launch_keys_to_ids(m->keys, M, m->ids, st); }));
+    TRY(K(WASR_K_IDS, [&] { return launch_keys_to_ids(keys, M, ids, st); }));
   }
   return 0;
 }
@@ -348,11 +365,70 @@ void free_graphs(WasrModel* m) {
   m->graph_cache.clear();
 }
 
+// A chunk of at least this many rows runs as two halves of its windows on two streams (one graph
+// with two branches), so that each kernel's last partial wave overlaps the other half's work
+// (measured: 71,599 rows 115.2 -> 114.7 ms per forward; below this size the halves' smaller
+// kernels lose more than the overlap gains: 8,802 rows 16.2 -> 17.3 ms).
+constexpr int kSplitRows = 40000;
+
+// windows [w0, w1) as one chunk's totals
+Chunk chunk_of(const int32_t* t, int w0, int w1) {
+  Chunk c{w0, w1, 0, 0, 0, 0};
+  for (int i = w0; i < w1; i++) {
+    const int tt = std::max(0, t[i]), t1 = t1_of(tt);
+    c.frames += tt;
+    c.rows += t1;
+    c.max_t1 = std::max(c.max_t1, t1);
+    c.tiles += (t1 + ATT_QT - 1) / ATT_QT;
+  }
+  return c;
+}
+size_t seg_ints_of(const Chunk& c) { return 3 * static_cast<size_t>(c.w1 - c.w0 + 1) + static_cast<size_t>(c.tiles); }
+
+// the halves of a chunk split by rows (false: no split)
+bool split_halves(const WasrModel* m, const int32_t* t, const Chunk& c, bool logits, Chunk* a, Chunk* b) {
+  if (logits || m->prof || c.rows < kSplitRows || c.w1 - c.w0 < 2) return false;
+  int rows = 0, w = c.w0;
+  while (w < c.w1 - 1 && 2 * (rows + t1_of(std::max(0, t[w]))) <= c.rows) rows += t1_of(std::max(0, t[w++]));
+  if (w == c.w0) w = c.w0 + 1;
+  *a = chunk_of(t, c.w0, w);
+  *b = chunk_of(t, w, c.w1);
+  return a->rows > 0 && b->rows > 0;
+}
+
+// Enqueue chunk c (seg: its device tables; for a split chunk the two halves' tables back to
+// back) on m->stream, the second half on m->side between a fork and a join event.
+int enqueue_forward(WasrModel* m, const int32_t* t, const Chunk& c, const int* seg, float* logits, Launcher& K) {
+  Chunk a, b;
+  cudaStream_t st = m->stream;
+  if (!split_halves(m, t, c, logits != nullptr, &a, &b)) return enqueue_chunk(m, c, seg, logits, K, st, 0, 0);
+  if (cudaEventRecord(m->ev_fork, st) != cudaSuccess || cudaStreamWaitEvent(m->side, m->ev_fork, 0) != cudaSuccess)
+    return -4;
+  const int ra = enqueue_chunk(m, a, seg, nullptr, K, st, 0, 0);
+  const int rb = ra ? 0 : enqueue_chunk(m, b, seg + seg_ints_of(a), nullptr, K, m->side, a.frames, a.rows);
+  // always join, so that a capture in progress ends with both branches merged
+  const bool joined = cudaEventRecord(m->ev_join, m->side) == cudaSuccess &&
+                      cudaStreamWaitEvent(st, m->ev_join, 0) == cudaSuccess;
+  return ra ? ra : rb ? rb : joined ? 0 : -4;
+}
+// host segment tables of chunk c, split like enqueue_forward
+size_t build_tables(const WasrModel* m, const int32_t* t, const Chunk& c, bool logits, int* out) {
+  Chunk a, b;
+  if (!split_halves(m, t, c, logits, &a, &b)) {
+    build_seg(t, c.w0, c.w1, out);
+    return seg_ints_of(c);
+  }
+  build_seg(t, a.w0, a.w1, out);
+  build_seg(t, b.w0, b.w1, out + seg_ints_of(a));
+  return seg_ints_of(a) + seg_ints_of(b);
+}
+
 // Run one chunk (frames already in m->feats): replay its graph if this layout was seen,
 // else capture it (graphs on) or run it eagerly.
 int run_chunk(WasrModel* m, const int32_t* t, const Chunk& c, float* logits) {
   const int n = c.w1 - c.w0;
-  const size_t seg_ints = 3 * static_cast<size_t>(n + 1) + static_cast<size_t>(c.tiles);
+  // (a split chunk's two tables hold one more entry per table than the whole chunk's)
+  const size_t seg_ints = 3 * static_cast<size_t>(n + 1) + static_cast<size_t>(c.tiles) + 3;
   if (!hgrow(&m->h_seg, &m->h_seg_cap, seg_ints)) return -5;
   cudaStream_t st = m->stream;
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
@@ -374,7 +450,7 @@ int run_chunk(WasrModel* m, const int32_t* t, const Chunk& c, float* logits) {
       }
       GraphEntry e;
       if (!dmalloc(&e.seg, seg_ints)) return -5;
-      build_seg(t, c.w0, c.w1, m->h_seg);
+      build_tables(m, t, c, false, m->h_seg);
       if (cudaMemcpy(e.seg, m->h_seg, seg_ints * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) {
         cudaFree(e.seg);
         return -4;
@@ -385,7 +461,7 @@ int run_chunk(WasrModel* m, const int32_t* t, const Chunk& c, float* logits) {
         return -10;
       }
       Launcher K{m, m->prof ? &e.recs : nullptr};
-      const int rc = enqueue_chunk(m, c, e.seg, nullptr, K);
+      const int rc = enqueue_forward(m, t, c, e.seg, nullptr, K);
       e.kernels = K.kernels;
       cudaGraph_t g = nullptr;
       const cudaError_t ee = cudaStreamEndCapture(st, &g);
@@ -419,13 +495,13 @@ int run_chunk(WasrModel* m, const int32_t* t, const Chunk& c, float* logits) {
     if (!dmalloc(&m->seg, seg_ints * 2)) return -5;
     m->seg_cap = static_cast<int>(seg_ints * 2);
   }
-  build_seg(t, c.w0, c.w1, m->h_seg);
+  build_tables(m, t, c, logits != nullptr, m->h_seg);
   if (cudaMemcpyAsync(m->seg, m->h_seg, seg_ints * sizeof(int), cudaMemcpyHostToDevice, st) != cudaSuccess)
     return -4;
   cudaStreamSynchronize(st);  // the previous eager chunk's events may still be pending
   free_recs(&m->eager_recs);
   Launcher K{m, m->prof ? &m->eager_recs : nullptr};
-  const int rc = enqueue_chunk(m, c, m->seg, logits, K);
+  const int rc = enqueue_forward(m, t, c, m->seg, logits, K);
   m->launches += K.kernels;
   // the pinned table is reused by the next chunk: make sure this copy has consumed it
   cudaStreamSynchronize(st);
@@ -515,7 +591,10 @@ WasrModel* wasr_model_create(const void* blob, size_t bytes, const WasrPlan* pla
   m->plan = *plan;
   m->max_rows = max_rows;
   m->max_frames = 5 * max_rows + 4 * std::max(1, max_rows / 20);  // t = 5*t1 + 0..4 per window
-  bool ok = cudaStreamCreateWithFlags(&m->own, cudaStreamNonBlocking) == cudaSuccess;
+  bool ok = cudaStreamCreateWithFlags(&m->own, cudaStreamNonBlocking) == cudaSuccess &&
+            cudaStreamCreateWithFlags(&m->side, cudaStreamNonBlocking) == cudaSuccess &&
+            cudaEventCreateWithFlags(&m->ev_fork, cudaEventDisableTiming) == cudaSuccess &&
+            cudaEventCreateWithFlags(&m->ev_join, cudaEventDisableTiming) == cudaSuccess;
   m->stream = m->own;
   ok = ok && cudaHostAlloc(reinterpret_cast<void**>(&m->err_host), sizeof(int), cudaHostAllocMapped) == cudaSuccess;
   ok = ok && cudaHostGetDevicePointer(reinterpret_cast<void**>(&m->err_dev), m->err_host, 0) == cudaSuccess;
@@ -584,6 +663,9 @@ void wasr_model_destroy(WasrModel* m) {
   if (m->h_seg) cudaFreeHost(m->h_seg);
   if (m->err_host) cudaFreeHost(m->err_host);
   if (m->own) cudaStreamDestroy(m->own);
+  if (m->side) cudaStreamDestroy(m->side);
+  if (m->ev_fork) cudaEventDestroy(m->ev_fork);
+  if (m->ev_join) cudaEventDestroy(m->ev_join);
   delete m;
 }
 
