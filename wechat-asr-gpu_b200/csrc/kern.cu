@@ -903,7 +903,7 @@ __global__ void __launch_bounds__(C3C_THREADS, 2) conv3_cert_k(const float* __re
     if (act) {
       const float* wb = Wst + (st & 1) * C3C_KS * C3 + 4 * cg;
       const float* pb = P + 4 * pg;
-#pragma unroll 4
+#pragma unroll 12
       for (int kk = 0; kk < C3C_KS; kk++) {
         const float4 w0 = *reinterpret_cast<const float4*>(wb + kk * C3);
         const float4 w1 = *reinterpret_cast<const float4*>(wb + kk * C3 + 96);
