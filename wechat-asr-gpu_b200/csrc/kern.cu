@@ -223,7 +223,7 @@ __global__ void __launch_bounds__(TP_THREADS, 3) conv2_k(const float* __restrict
       }
     }
     __syncthreads();
-    tp_accumulate<DIM, CV2_WS, 4>(X2, Wt, CV2_MP, (q - (c0 >> 1)) & 3, f0, o0, acc);
+    tp_accumulate<DIM, CV2_WS, 12>(X2, Wt, CV2_MP, (q - (c0 >> 1)) & 3, f0, o0, acc);
   }
   __syncthreads();
   float2* part = reinterpret_cast<float2*>(sm);  // [4][32][42]
