@@ -1803,7 +1803,7 @@ __global__ void __launch_bounds__(256, 2) attn_k(const float* __restrict__ q, co
     const float2* p1 = p0 + sp;
     const float* vr = Vb + (ch & 1) * ATT_KC * HD + 4 * dg;
     if (live) {
-#pragma unroll 4
+#pragma unroll 8
       for (int jj = 0; jj < nj; jj++) {
         const float2 pa2 = p0[jj], pb2 = p1[jj];
         const float4 x = *reinterpret_cast<const float4*>(vr + jj * HD);
