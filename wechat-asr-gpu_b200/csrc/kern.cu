@@ -1624,14 +1624,12 @@ __device__ __forceinline__ void att_div_batch(float2* S2, const float4* ZY, int 
   for (int k = 0; k < NB; k++)
     if (e0 + 256 * k < E) S2[off[k]] = q[k];
 }
-// runs batches of 6 slots, then the remainder (Kw slots in all for this warp)
+// runs batches of 4 slots, then the remainder (Kw slots in all for this warp)
 #define ATT_BATCHES(FN, ...)                                   \
   {                                                            \
     int k0 = 0;                                                \
-    for (; k0 + 6 <= Kw; k0 += 6) FN<6>(__VA_ARGS__, tid + 256 * k0); \
+    for (; k0 + 4 <= Kw; k0 += 4) FN<4>(__VA_ARGS__, tid + 256 * k0); \
     switch (Kw - k0) {                                         \
-      case 5: FN<5>(__VA_ARGS__, tid + 256 * k0); break;       \
-      case 4: FN<4>(__VA_ARGS__, tid + 256 * k0); break;       \
       case 3: FN<3>(__VA_ARGS__, tid + 256 * k0); break;       \
       case 2: FN<2>(__VA_ARGS__, tid + 256 * k0); break;       \
       case 1: FN<1>(__VA_ARGS__, tid + 256 * k0); break;       \
