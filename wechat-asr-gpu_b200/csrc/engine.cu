@@ -72,7 +72,7 @@ struct WasrModel {
   bool qkv_fused[WASR_MAX_LAYERS] = {};
   // activations
   float *feats = nullptr, *y1 = nullptr, *y2 = nullptr;
-  float* c2pre = nullptr;   // conv2 weights laid out per conv stage
+  float* c2pre = nullptr;   // conv2 weights transposed to [tap][out] (the position-pair kernel)
   float* c3cert = nullptr;  // conv3 weights transposed for conv3_cert_k, and their row norms
   int8_t* xq = nullptr;
   float* xs = nullptr;
@@ -633,8 +633,8 @@ WasrModel* wasr_model_create(const void* blob, size_t bytes, const WasrPlan* pla
     m->qkv_fused[l] = ok;
   }
   // conv2 / conv3 weights in the per-stage layout their kernels stage from (once per model)
-  ok = ok && dmalloc(&m->c2pre, conv_pre_floats(2)) && dmalloc(&m->c3cert, conv3_cert_prep_floats()) &&
-       conv_prepare(fptr(m, plan->c2), nullptr, m->c2pre, nullptr, m->stream) == 0 &&
+  ok = ok && dmalloc(&m->c2pre, conv2_prepare_floats()) && dmalloc(&m->c3cert, conv3_cert_prep_floats()) &&
+       conv2_prepare(fptr(m, plan->c2), m->c2pre, m->stream) == 0 &&
        conv3_cert_prepare(fptr(m, plan->c3), m->c3cert, m->stream) == 0 &&
        cudaStreamSynchronize(m->stream) == cudaSuccess;
   if (!ok) {

@@ -143,8 +143,7 @@ __device__ __forceinline__ float tp_fold(const float2* part, int nch, int npos, 
 // outside the segment / the 40 columns), column 40 = 0 -- src/model.rs:420-444.
 // Block = (row r, 32 output channels); stages of 4 input channels.
 __global__ void __launch_bounds__(TP_THREADS, 3) conv2_k(const float* __restrict__ y1, const float* __restrict__ c2,
-                                                      const float2* __restrict__ c2pre, Segs s, int row0,
-                                                      float* __restrict__ y2) {
+                                                      Segs s, int row0, float* __restrict__ y2) {
   extern __shared__ __align__(16) float sm[];
   float2* X2 = reinterpret_cast<float2*>(sm);    // [98][40]
   float2* Wt = X2 + CV2_MP * DIM;                 // [98][34]
@@ -177,23 +176,15 @@ __global__ void __launch_bounds__(TP_THREADS, 3) conv2_k(const float* __restrict
 #pragma unroll 1
   for (int c0 = 0; c0 < C1; c0 += CV2_CC) {
     __syncthreads();  // the previous stage is consumed (and the zeros / offsets are visible)
-    if (c2pre) {  // the stage's [pair][64 channels] rows, laid out once per model: 16-byte copies
-      const float2* src = c2pre + static_cast<int64_t>(c0 / CV2_CC) * CV2_MP * C2 + og * CV2_CH;
-      for (int e = tid; e < CV2_MP * (CV2_CH / 2); e += TP_THREADS) {
-        const int m = e >> 4, c2x = (e & 15) * 2;
-        cp_async16(Wt + m * CV2_WS + c2x, src + m * C2 + c2x);
-      }
-    } else {
-      for (int e = tid; e < CV2_MP * CV2_CH; e += TP_THREADS) {
-        const int o = e / CV2_MP, m = e - o * CV2_MP;
-        const float* w = c2 + static_cast<int64_t>(og * CV2_CH + o) * K2 + c0 * 49 + 2 * m;
-        float2* d = Wt + m * CV2_WS + o;
-        if (w8) {
-          cp_async8(d, w);
-        } else {
-          cp_async4(d, w);
-          cp_async4(reinterpret_cast<float*>(d) + 1, w + 1);
-        }
+    for (int e = tid; e < CV2_MP * CV2_CH; e += TP_THREADS) {  // weight pairs from the [out][tap] layout
+      const int o = e / CV2_MP, m = e - o * CV2_MP;
+      const float* w = c2 + static_cast<int64_t>(og * CV2_CH + o) * K2 + c0 * 49 + 2 * m;
+      float2* d = Wt + m * CV2_WS + o;
+      if (w8) {
+        cp_async8(d, w);
+      } else {
+        cp_async4(d, w);
+        cp_async4(reinterpret_cast<float*>(d) + 1, w + 1);
       }
     }
     for (int e = tid; e < 7 * CV2_CC * (DIM / 4); e += TP_THREADS) {
@@ -240,12 +231,135 @@ __global__ void __launch_bounds__(TP_THREADS, 3) conv2_k(const float* __restrict
   if (tid < CV2_CH) out[tid * W2 + DIM] = 0.0f;
 }
 
+// Position-pair conv2 (the engine's; weights transposed once per model to c2t[k][o]).  Warp w
+// accumulates dotf lane w of every output of the block: the lane's taps k = w, w+8, ... in
+// order, which in stage s are the stage taps t = (w - 4s) mod 8, +8, ... (196 = 4 mod 8).  A
+// thread owns 4 output channels x 10 positions as 5 packed pairs (f, f+1) of that lane.  The two
+// inputs of a position pair at one tap are adjacent in the staged input row, so they are one
+// 8-byte load: each stage's input rows are staged twice, the second copy shifted by one float,
+// and a tap reads whichever copy puts its pairs on an 8-byte boundary.  A product pair is one
+// packed fma.rn(x, w, -0) -- exactly the rounded product, the sign of a zero product included --
+// with the -0 a kernel argument, so that the code generator cannot turn it into a multiply and
+// contract that with the following packed rounded add; the accumulate is that add.  Every
+// element thus rounds exactly like the scalar dotf sequence, at two packed instructions per two
+// multiply-adds.  Stages (4 input channels: the weights [196 taps][32 channels]
+// and both copies of 7 input rows) are double-buffered by cp.async, one barrier per stage.
+constexpr int CP_CH = 32;                          // output channels per block
+constexpr int CP_CC = 4;                           // input channels per stage
+constexpr int CP_T = CP_CC * 49;                   // taps per stage
+constexpr int CP_NST = C1 / CP_CC;                 // stages
+constexpr int CP_RW = 48;                          // staged row: 4 zeros | 40 values | 4 zeros
+constexpr int CP_RAW = 7 * CP_CC * CP_RW;          // floats of one copy of a stage's input rows
+constexpr int CP_BUF = CP_T * CP_CH + 2 * CP_RAW;  // floats of one stage buffer: weights, copy 0, copy 1
+constexpr int CP_PS = DIM + 2;                     // row stride of the lane-fold buffer
+constexpr int CP_SMEM = cmax(2 * CP_BUF * 4 + CP_T * 4, 8 * CP_CH * CP_PS * 4);
+static_assert(CP_NST * CP_CC == C1 && (CP_BUF * 4) % 16 == 0 && (CP_T * CP_CH * 4) % 16 == 0 &&
+                  (CP_RAW * 4) % 16 == 0 && CP_T % 8 == 4,
+              "position-pair conv2 layout");
+
+__global__ void __launch_bounds__(TP_THREADS, 3) conv2p_k(const float* __restrict__ y1, const float* __restrict__ c2t,
+                                                       Segs s, int row0, float* __restrict__ y2, float nz) {
+  extern __shared__ __align__(16) float sm[];
+  const float2 z2 = make_float2(nz, nz);
+  int* tapoff = reinterpret_cast<int*>(sm + 2 * CP_BUF);  // [196] tap -> float offset from copy 0
+  const int r = row0 + blockIdx.y, og = blockIdx.x, tid = threadIdx.x;
+  const int sw = s.seg_of_row(r);
+  const int fb = s.frame_begin(sw), t = s.frames(sw), ti = r - s.row_begin(sw);
+  const int lane = tid >> 5, cg = tid & 7, pg = (tid >> 3) & 3;
+  const int f0 = 10 * pg, o0 = 4 * cg;
+  // tap c*49 + i*7 + j reads row (i, c) at column f + j + 1 of copy 0 (x column f+j-3, +4); for
+  // even j the same pair starts at column f + j of copy 1 (copy1[k] = copy0[k + 1]), so that
+  // every pair (f even) starts on an 8-byte boundary
+  for (int e = tid; e < CP_T; e += TP_THREADS) {
+    const int cl = e / 49, rem = e - cl * 49, i = rem / 7, j = rem - i * 7, row = i * CP_CC + cl;
+    tapoff[e] = (j & 1) ? row * CP_RW + j + 1 : CP_RAW + row * CP_RW + j;
+  }
+  // zeros that no copy overwrites, in both buffers: copy 0's columns 0-3 and 44-47, copy 1's
+  // 0-2 and 43-47, and whole rows outside the segment
+  for (int e = tid; e < 2 * 2 * CP_RAW; e += TP_THREADS) {
+    const int b = e / (2 * CP_RAW), cpy = (e / CP_RAW) & 1, w = e % CP_RAW;
+    const int col = w % CP_RW, i = w / (CP_RW * CP_CC), tt = ti * 5 + i - 1;
+    const int lo = cpy ? 3 : 4;
+    if (col < lo || col >= lo + DIM || tt < 0 || tt >= t) sm[b * CP_BUF + CP_T * CP_CH + e % (2 * CP_RAW)] = 0.0f;
+  }
+  auto load_stage = [&](int st, int b) {
+    float* buf = sm + b * CP_BUF;
+    const float* src = c2t + static_cast<int64_t>(st) * CP_T * C2 + og * CP_CH;
+    for (int e = tid; e < CP_T * (CP_CH / 4); e += TP_THREADS) {
+      const int tp = e >> 3, q = e & 7;
+      cp_async16(buf + tp * CP_CH + 4 * q, src + tp * C2 + 4 * q);
+    }
+    float* c0p = buf + CP_T * CP_CH;
+    for (int e = tid; e < 7 * CP_CC * (DIM / 4); e += TP_THREADS) {
+      const int row = e / (DIM / 4), p4 = e - row * (DIM / 4), i = row / CP_CC, cl = row - i * CP_CC;
+      const int tt = ti * 5 + i - 1;
+      if (tt >= 0 && tt < t)
+        cp_async16(c0p + row * CP_RW + 4 + 4 * p4,
+                   y1 + static_cast<int64_t>(fb + tt) * (C1 * DIM) + (st * CP_CC + cl) * DIM + 4 * p4);
+    }
+    for (int e = tid; e < 7 * CP_CC * DIM; e += TP_THREADS) {
+      const int row = e / DIM, c = e - row * DIM, i = row / CP_CC, cl = row - i * CP_CC;
+      const int tt = ti * 5 + i - 1;
+      if (tt >= 0 && tt < t)
+        cp_async4(c0p + CP_RAW + row * CP_RW + 3 + c,
+                  y1 + static_cast<int64_t>(fb + tt) * (C1 * DIM) + (st * CP_CC + cl) * DIM + c);
+    }
+    cp_async_commit();
+  };
+  load_stage(0, 0);
+  float2 acc[5][4];
+#pragma unroll
+  for (int k = 0; k < 5; k++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) acc[k][c] = make_float2(0.0f, 0.0f);
+#pragma unroll 1
+  for (int st = 0; st < CP_NST; st++) {
+    cp_async_wait<0>();
+    __syncthreads();  // stage st landed everywhere; stage st-1's buffer is consumed
+    if (st + 1 < CP_NST) load_stage(st + 1, (st + 1) & 1);
+    const float* buf = sm + (st & 1) * CP_BUF;
+    const float* xb = buf + CP_T * CP_CH + f0;
+    const float* wb = buf + o0;
+#pragma unroll 12
+    for (int tp = (lane - 4 * st) & 7; tp < CP_T; tp += 8) {
+      const float* xr = xb + tapoff[tp];
+      float2 xv[5];
+#pragma unroll
+      for (int k = 0; k < 5; k++) xv[k] = *reinterpret_cast<const float2*>(xr + 2 * k);
+      const float4 w4 = *reinterpret_cast<const float4*>(wb + tp * CP_CH);
+      const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+      for (int k = 0; k < 5; k++)
+#pragma unroll
+        for (int c = 0; c < 4; c++)
+          acc[k][c] = add2_rn(acc[k][c], fma2_rn(xv[k], make_float2(wv[c], wv[c]), z2));
+    }
+  }
+  __syncthreads();
+  float* part = sm;  // [8 lanes][32 channels][42]
+#pragma unroll
+  for (int k = 0; k < 5; k++)
+#pragma unroll
+    for (int c = 0; c < 4; c++)
+      *reinterpret_cast<float2*>(part + (lane * CP_CH + o0 + c) * CP_PS + f0 + 2 * k) = acc[k][c];
+  __syncthreads();
+  float* out = y2 + static_cast<int64_t>(r) * (C2 * W2) + og * CP_CH * W2;
+  for (int e = tid; e < CP_CH * DIM; e += TP_THREADS) {
+    const int o = e / DIM, f = e - o * DIM;
+    const float* pp = part + o * CP_PS + f;
+    float v = __fadd_rn(pp[0], pp[CP_CH * CP_PS]);
+#pragma unroll
+    for (int l = 2; l < 8; l++) v = __fadd_rn(v, pp[l * CP_CH * CP_PS]);
+    out[o * W2 + f] = fmaxf(v, 0.0f);
+  }
+  if (tid < CP_CH) out[tid * W2 + DIM] = 0.0f;
+}
+
 // y3[r][o*20+f] = relu(dotf(c3[o], patch)), patch[c*9+i*3+j] = y2[r+i-1][c][2f+j] (zero
 // outside the segment) -- src/model.rs:446-468.  Block = (row r, 64 output channels);
 // stages of 8 input channels.
 __global__ void __launch_bounds__(TP_THREADS, 3) conv3_k(const float* __restrict__ y2, const float* __restrict__ c3,
-                                                      const float2* __restrict__ c3pre, Segs s, int row0,
-                                                      float* __restrict__ y3) {
+                                                      Segs s, int row0, float* __restrict__ y3) {
   extern __shared__ __align__(16) float sm[];
   float2* X2 = reinterpret_cast<float2*>(sm);    // [36][20]
   float2* Wt = X2 + CV3_MP * 20;                  // [36][66]
@@ -276,23 +390,15 @@ __global__ void __launch_bounds__(TP_THREADS, 3) conv3_k(const float* __restrict
 #pragma unroll 1
   for (int c0 = 0; c0 < C2; c0 += CV3_CC) {
     __syncthreads();
-    if (c3pre) {  // the stage's [pair][192 channels] rows, laid out once per model
-      const float2* src = c3pre + static_cast<int64_t>(c0 / CV3_CC) * CV3_MP * C3 + og * CV3_CH;
-      for (int e = tid; e < CV3_MP * (CV3_CH / 2); e += TP_THREADS) {
-        const int m = e >> 5, c2x = (e & 31) * 2;
-        cp_async16(Wt + m * CV3_WS + c2x, src + m * C3 + c2x);
-      }
-    } else {
-      for (int e = tid; e < CV3_MP * CV3_CH; e += TP_THREADS) {
-        const int o = e / CV3_MP, m = e - o * CV3_MP;
-        const float* w = c3 + static_cast<int64_t>(og * CV3_CH + o) * K3 + c0 * 9 + 2 * m;
-        float2* d = Wt + m * CV3_WS + o;
-        if (w8) {
-          cp_async8(d, w);
-        } else {
-          cp_async4(d, w);
-          cp_async4(reinterpret_cast<float*>(d) + 1, w + 1);
-        }
+    for (int e = tid; e < CV3_MP * CV3_CH; e += TP_THREADS) {  // weight pairs from the [out][tap] layout
+      const int o = e / CV3_MP, m = e - o * CV3_MP;
+      const float* w = c3 + static_cast<int64_t>(og * CV3_CH + o) * K3 + c0 * 9 + 2 * m;
+      float2* d = Wt + m * CV3_WS + o;
+      if (w8) {
+        cp_async8(d, w);
+      } else {
+        cp_async4(d, w);
+        cp_async4(reinterpret_cast<float*>(d) + 1, w + 1);
       }
     }
     for (int i = 0; i < 3; i++) {  // input row i: channels c0 .. c0+15 are 656 contiguous floats
@@ -1871,6 +1977,7 @@ static void set_smem(const void* kern, int bytes) {
 
 bool kern_prepare() {
   set_smem(reinterpret_cast<const void*>(conv2_k), CV2_SMEM);
+  set_smem(reinterpret_cast<const void*>(conv2p_k), CP_SMEM);
   set_smem(reinterpret_cast<const void*>(conv3_k), CV3_SMEM);
   set_smem(reinterpret_cast<const void*>(attn_k), 227 * 1024);
   set_smem(reinterpret_cast<const void*>(gelu_quant_ro_k), 227 * 1024);
@@ -1887,37 +1994,33 @@ int launch_conv1(const float* x, const float* c1, Segs s, int total_frames, floa
   conv1_k<<<(n + 127) / 128, 128, 0, st>>>(x, c1, s, total_frames, y1);
   return launched();
 }
-// out[s][m][o] = (c[o][s*taps + 2m], c[o][s*taps + 2m + 1]) for stage s, tap pair m < taps/2,
-// output channel o: the weight pairs of one conv stage, rows of all output channels.
-__global__ void conv_pre_k(const float* __restrict__ c, int nout, int k, int taps, int nstage,
-                           float2* __restrict__ out) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int mp = taps / 2;
-  if (i >= static_cast<int64_t>(nstage) * mp * nout) return;
-  const int o = static_cast<int>(i % nout), m = static_cast<int>((i / nout) % mp), st = static_cast<int>(i / (nout * mp));
-  const float* w = c + static_cast<int64_t>(o) * k + st * taps + 2 * m;
-  out[i] = make_float2(w[0], w[1]);
+// c2t[k][o] = c2[o][k]: the position-pair conv2's weight layout
+__global__ void conv2t_pre_k(const float* __restrict__ c2, float* __restrict__ c2t) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= K2 * C2) return;
+  const int k = i / C2, o = i - k * C2;
+  c2t[i] = c2[static_cast<int64_t>(o) * K2 + k];
 }
 
-size_t conv_pre_floats(int which) { return which == 2 ? static_cast<size_t>(C2) * K2 : static_cast<size_t>(C3) * K3; }
-
-// either layout may be skipped (null pointers)
-int conv_prepare(const float* c2, const float* c3, float* c2pre, float* c3pre, cudaStream_t st) {
-  const int n2 = (C1 / CV2_CC) * CV2_MP * C2, n3 = (C2 / CV3_CC) * CV3_MP * C3;
-  if (c2 && c2pre)
-    conv_pre_k<<<(n2 + 255) / 256, 256, 0, st>>>(c2, C2, K2, CV2_CC * 49, C1 / CV2_CC, reinterpret_cast<float2*>(c2pre));
-  if (c3 && c3pre)
-    conv_pre_k<<<(n3 + 255) / 256, 256, 0, st>>>(c3, C3, K3, CV3_CC * 9, C2 / CV3_CC, reinterpret_cast<float2*>(c3pre));
+size_t conv2_prepare_floats() { return static_cast<size_t>(C2) * K2; }
+int conv2_prepare(const float* c2, float* c2t, cudaStream_t st) {
+  conv2t_pre_k<<<(K2 * C2 + 255) / 256, 256, 0, st>>>(c2, c2t);
   return launched();
 }
 
-int launch_conv2(const float* y1, const float* c2, const float* c2pre, Segs s, int total_rows, float* y2,
+int launch_conv2(const float* y1, const float* c2, const float* c2t, Segs s, int total_rows, float* y2,
                  cudaStream_t st) {
   if (total_rows <= 0) return 0;
+  if (c2t && (reinterpret_cast<uintptr_t>(y1) & 15) == 0 && (reinterpret_cast<uintptr_t>(c2t) & 15) == 0) {
+    set_smem(reinterpret_cast<const void*>(conv2p_k), CP_SMEM);
+    for (int r0 = 0; r0 < total_rows; r0 += 65535)  // grid.y limit
+      conv2p_k<<<dim3(C2 / CP_CH, std::min(65535, total_rows - r0)), TP_THREADS, CP_SMEM, st>>>(y1, c2t, s, r0, y2, -0.0f);
+    return launched();
+  }
   set_smem(reinterpret_cast<const void*>(conv2_k), CV2_SMEM);
   for (int r0 = 0; r0 < total_rows; r0 += 65535)  // grid.y limit
     conv2_k<<<dim3(C2 / CV2_CH, std::min(65535, total_rows - r0)), TP_THREADS, CV2_SMEM, st>>>(
-        y1, c2, reinterpret_cast<const float2*>(c2pre), s, r0, y2);
+        y1, c2, s, r0, y2);
   return launched();
 }
 size_t conv3_cert_prep_floats() { return static_cast<size_t>(K3) * C3 + C3; }
@@ -1933,13 +2036,12 @@ int launch_conv3_cert(const float* y2, const float* c3, const float* prep, Segs 
                                                                              total_rows, xq, xs);
   return launched();
 }
-int launch_conv3(const float* y2, const float* c3, const float* c3pre, Segs s, int total_rows, float* y3,
-                 cudaStream_t st) {
+int launch_conv3(const float* y2, const float* c3, Segs s, int total_rows, float* y3, cudaStream_t st) {
   if (total_rows <= 0) return 0;
   set_smem(reinterpret_cast<const void*>(conv3_k), CV3_SMEM);
   for (int r0 = 0; r0 < total_rows; r0 += 65535)  // grid.y limit
     conv3_k<<<dim3(C3 / CV3_CH, std::min(65535, total_rows - r0)), TP_THREADS, CV3_SMEM, st>>>(
-        y2, c3, reinterpret_cast<const float2*>(c3pre), s, r0, y3);
+        y2, c3, s, r0, y3);
   return launched();
 }
 int launch_quant_rows(const float* x, int m, int k, int ldx, int8_t* xq, float* xs, cudaStream_t st) {
@@ -2051,7 +2153,7 @@ void wk_front(void* stream, const float* x, const float* c1, const float* c2, co
   const Segs s = one_seg(t, t1);
   launch_conv1(x, c1, s, t, y1, st);
   launch_conv2(y1, c2, nullptr, s, t1, y2, st);
-  launch_conv3(y2, c3, nullptr, s, t1, y3, st);
+  launch_conv3(y2, c3, s, t1, y3, st);
 }
 
 // the 512-wide kernel moves rows as float4 / char4

@@ -44,15 +44,14 @@ struct Segs {
 
 // host launchers (stream-ordered, no allocation); return 0 or -4 on launch failure
 int launch_conv1(const float* x, const float* c1, Segs s, int total_frames, float* y1, cudaStream_t st);
-// c2pre / c3pre: optional copies of the weights laid out per conv stage by conv_prepare (one
-// contiguous block of weight pairs per stage); nullptr stages them from the [out][tap] layout.
-int launch_conv2(const float* y1, const float* c2, const float* c2pre, Segs s, int total_rows, float* y2,
+// c2t: the conv2 weights transposed to [tap][out] by conv2_prepare (conv2_prepare_floats()
+// floats), which selects the position-pair kernel; nullptr stages the weights from c2's
+// [out][tap] layout (the reference ABI's wk_front).
+int launch_conv2(const float* y1, const float* c2, const float* c2t, Segs s, int total_rows, float* y2,
                  cudaStream_t st);
-int launch_conv3(const float* y2, const float* c3, const float* c3pre, Segs s, int total_rows, float* y3,
-                 cudaStream_t st);
-// floats of the stage layout of conv2 (which = 2) or conv3 (which = 3) weights
-size_t conv_pre_floats(int which);
-int conv_prepare(const float* c2, const float* c3, float* c2pre, float* c3pre, cudaStream_t st);
+int launch_conv3(const float* y2, const float* c3, Segs s, int total_rows, float* y3, cudaStream_t st);
+size_t conv2_prepare_floats();
+int conv2_prepare(const float* c2, float* c2t, cudaStream_t st);
 // conv3 fused with the certified row quantisation of its output (the engine's path): the int8
 // rows and scales equal quant(conv3(y2)) of the reference order; prep holds the transposed
 // weights and weight norms (conv3_cert_prepare, conv3_cert_prep_floats() floats)
