@@ -211,6 +211,16 @@ int wasr_gelu_quant(const float* y, int m, int k, int8_t* xq, float* xs, int exa
 int wasr_conv3_quant(const float* y2, const float* c3, float* prep, const int* roff, int nseg, int rows,
                      int8_t* xq, float* xs, void* stream);
 
+/* conv2 of the conv frontend (src/model.rs:420-444) on device buffers: y1 [frames][32][40],
+ * c2 [64][1568], y2 [rows][64][41] (column 40 written 0).  c2t: scratch of 64 * 1568 floats,
+ * filled here with the transposed weights, selects the engine's position-pair kernel; NULL runs
+ * the kernel of the reference ABI's wk_front (csrc/wtl_kern.cu:409-462).  foff / roff: device
+ * frame / row prefix offsets of nseg windows stacked in y1 / y2, or both NULL for one window.
+ * Both kernels keep the reference's dotf order, so y2 equals the CPU's bit for bit.  No
+ * counterpart in the reference ABI (a parity hook).  Returns 0, -1 (arguments) or -4 (launch). */
+int wasr_conv2(const float* y1, const float* c2, float* c2t, const int* foff, const int* roff, int nseg, int frames,
+               int rows, float* y2, void* stream);
+
 /* Parity hook for the certified GELU: scans the float bit patterns [start, start + count)
  * (both even, start + count <= 2^32) and accumulates into the device array stats[8] (zeroed by
  * the caller), with g~ the approximation and g the exact GELU: [0] the largest |g~ - g| - B |g~|

@@ -44,6 +44,7 @@ def lib():
             "wo_gelu_array": (None, [P, P, I64]),
             "wo_attention": (None, [P, P, P, I, P]),
             "wo_frontend": (I, [P, I, P, P, P, P]),
+            "wo_conv2": (None, [P, I, P, P]),
             "wo_conv3": (None, [P, I, P, P]),
             "wo_forward": (I, [P, P, P, I, P, P]),
             "wo_run_post": (I, [P, P, I, P, P, P]),
@@ -163,6 +164,16 @@ def frontend(x, c1, c2, c3):
                       _p(np.ascontiguousarray(c2, np.float32)),
                       _p(np.ascontiguousarray(c3, np.float32)), _p(y3))
     return y3[:t1]
+
+
+def conv2(y1, c2):
+    """The conv2 stage alone (src/model.rs:420-444): y1 [t][32][40] -> y2 [t1][64][41]."""
+    y1 = np.ascontiguousarray(y1, np.float32)
+    t = y1.shape[0]
+    t1 = (t - 5) // 5 + 1 if t >= 5 else 0
+    y2 = np.zeros((max(t1, 1), 64, 41), np.float32)
+    lib().wo_conv2(_p(y1), t, _p(np.ascontiguousarray(c2, np.float32)), _p(y2))
+    return y2[:t1]
 
 
 def conv3(y2, c3):

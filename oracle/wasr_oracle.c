@@ -242,6 +242,38 @@ void wo_attention(const float* q, const float* k, const float* v, int t, float* 
   }
 }
 
+/* src/model.rs:420-444: conv 7x7, 32->64, time stride 5 (pad 1), frequency pad 3 of one
+ * window's y1 [t][32][40] -> y2 [t1][64][41], t1 = (t - 5) / 5 + 1; column 40 is 0 */
+void wo_conv2(const float* y1, int t, const float* c2, float* y2) {
+  if (t < 5) return;
+  int t1 = (t - 5) / 5 + 1;
+#pragma omp parallel
+  {
+    float* p = (float*)malloc(sizeof(float) * DIM * K2);
+#pragma omp for schedule(static)
+    for (int ti = 0; ti < t1; ti++) {
+      memset(p, 0, sizeof(float) * DIM * K2);
+      for (int i = 0; i < 7; i++) {
+        int tt = ti * 5 + i - 1;
+        if (tt < 0 || tt >= t) continue;
+        const float* row = y1 + (int64_t)tt * F1 * DIM;
+        for (int c = 0; c < F1; c++)
+          for (int f = 0; f < DIM; f++)
+            for (int j = 0; j < 7; j++) {
+              int ff = f + j - 3;
+              if (ff >= 0 && ff < DIM) p[f * K2 + c * 49 + i * 7 + j] = row[c * DIM + ff];
+            }
+      }
+      float* y = y2 + (int64_t)ti * F2 * W2;
+      for (int o = 0; o < F2; o++) {
+        for (int f = 0; f < DIM; f++) y[o * W2 + f] = fmaxf(wo_dotf(c2 + (int64_t)o * K2, p + f * K2, K2), 0.0f);
+        y[o * W2 + DIM] = 0.0f;
+      }
+    }
+    free(p);
+  }
+}
+
 /* src/model.rs:446-468: conv 3x3, 64->192, frequency stride 2, time pad 1 of one window's
  * y2 [t1][64][41] -> y3 [t1][192*20] (im2col + dotf + ReLU) */
 void wo_conv3(const float* y2, int t1, const float* c3, float* y3) {
@@ -293,31 +325,7 @@ int wo_frontend(const float* x, int t, const float* c1, const float* c2, const f
     for (int o = 0; o < F1; o++)
       for (int f = 0; f < DIM; f++) y[o * DIM + f] = fmaxf(wo_dotf(c1 + o * 25, p[f], 25), 0.0f);
   }
-  /* conv 7x7, 32->64, time stride 5 (pad 1), frequency pad 3; column 40 stays 0 */
-#pragma omp parallel
-  {
-    float* p = (float*)malloc(sizeof(float) * DIM * K2);
-#pragma omp for schedule(static)
-    for (int ti = 0; ti < t1; ti++) {
-      memset(p, 0, sizeof(float) * DIM * K2);
-      for (int i = 0; i < 7; i++) {
-        int tt = ti * 5 + i - 1;
-        if (tt < 0 || tt >= t) continue;
-        const float* row = y1 + (int64_t)tt * F1 * DIM;
-        for (int c = 0; c < F1; c++)
-          for (int f = 0; f < DIM; f++)
-            for (int j = 0; j < 7; j++) {
-              int ff = f + j - 3;
-              if (ff >= 0 && ff < DIM) p[f * K2 + c * 49 + i * 7 + j] = row[c * DIM + ff];
-            }
-      }
-      float* y = y2 + (int64_t)ti * F2 * W2;
-      for (int o = 0; o < F2; o++)
-        for (int f = 0; f < DIM; f++)
-          y[o * W2 + f] = fmaxf(wo_dotf(c2 + (int64_t)o * K2, p + f * K2, K2), 0.0f);
-    }
-    free(p);
-  }
+  wo_conv2(y1, t, c2, y2);
   wo_conv3(y2, t1, c3, y3);
   free(y1);
   free(y2);

@@ -181,6 +181,25 @@ def test_frontend_matches_torch_conv(orc):
     np.testing.assert_allclose(y3, y3r, rtol=1e-4, atol=1e-4)
 
 
+def test_conv2_stage_matches_torch_conv(orc):
+    """The conv2 stage alone (the checker of the GPU conv2 kernels), incl. a window of fewer
+    than 5 frames (no output rows) and the zero column 40."""
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(10)
+    c2 = rng.standard_normal((64, 32, 7, 7)).astype(np.float32) * 0.03
+    assert orc.conv2(np.ones((4, 32, 40), np.float32), c2).shape == (0, 64, 41)
+    for t in (5, 9, 10, 37):
+        y1 = np.maximum(rng.standard_normal((t, 32, 40)), 0.0).astype(np.float32)
+        y2 = orc.conv2(y1, c2)
+        Y1 = torch.from_numpy(y1).double().permute(1, 0, 2)[None]      # [1][32][t][40]
+        y2r = torch.relu(torch.nn.functional.conv2d(Y1, torch.from_numpy(c2).double(), stride=(5, 1),
+                                                    padding=(1, 3)))
+        y2r = y2r[0].permute(1, 0, 2).numpy()                           # [t1][64][40]
+        assert y2.shape == ((t - 5) // 5 + 1, 64, 41)
+        assert not y2[:, :, 40].any()
+        np.testing.assert_allclose(y2[:, :, :40], y2r, rtol=1e-4, atol=1e-4)
+
+
 def test_fbank_frame_matches_numpy_fft(orc):
     rng = np.random.default_rng(11)
     x = rng.integers(-20000, 20000, size=400).astype(np.int16)

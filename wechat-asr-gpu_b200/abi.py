@@ -115,6 +115,7 @@ SIGNATURES = {
     "wasr_eval_math": (I, [I, P, P, I, P]),
     "wasr_gelu_quant": (I, [P, I, I, P, P, I, P]),
     "wasr_conv3_quant": (I, [P, P, P, P, I, I, P, P, P]),
+    "wasr_conv2": (I, [P, P, P, P, P, I, I, I, P, P]),
     "wasr_gelu_cert_scan": (I, [U64, U64, P, P]),
     "wasr_i8_mma_peak": (I, [I, I, P, P]),
     "wasr_version": (C.c_char_p, []),

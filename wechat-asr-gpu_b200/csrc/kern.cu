@@ -2277,6 +2277,23 @@ int wasr_conv3_quant(const float* y2, const float* c3, float* prep, const int* r
   return launch_conv3_cert(y2, c3, prep, s, rows, xq, xs, st);
 }
 
+// Parity hook for conv2: c2t = conv2_prepare_floats() floats (filled here from c2) selects the
+// engine's position-pair kernel, nullptr the reference ABI's; foff / roff = device frame / row
+// offsets of nseg windows, or both nullptr for one window of `frames` frames and `rows` rows.
+int wasr_conv2(const float* y1, const float* c2, float* c2t, const int* foff, const int* roff, int nseg, int frames,
+               int rows, float* y2, void* stream) {
+  if (!y1 || !c2 || !y2 || rows < 0 || frames < 0 || (!foff != !roff) || (roff && nseg <= 0)) return -1;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (c2t && conv2_prepare(c2, c2t, st) != 0) return -4;
+  Segs s{};
+  s.foff = foff;
+  s.roff = roff;
+  s.n = roff ? nseg : 1;
+  s.t0 = frames;
+  s.t10 = rows;
+  return launch_conv2(y1, c2, c2t, s, rows, y2, st);
+}
+
 // Parity hooks for the certified GELU + quant: the engine's kernel choice (exact = 0) or the
 // all-exact kernel (exact = 1) on a read-only [m][k] input; and the exhaustive bound scan.
 int wasr_gelu_quant(const float* y, int m, int k, int8_t* xq, float* xs, int exact, void* stream) {
