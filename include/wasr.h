@@ -221,6 +221,17 @@ int wasr_conv3_quant(const float* y2, const float* c3, float* prep, const int* r
 int wasr_conv2(const float* y1, const float* c2, float* c2t, const int* foff, const int* roff, int nseg, int frames,
                int rows, float* y2, void* stream);
 
+/* The engine's fused feed-forward up-projection (src/model.rs:495-496 with quant,
+ * src/kernels.rs:11-25) on device buffers: q [M][N] int8 and qs [M] equal quant(gelu(x)) for
+ * x = (acc * xs[row]) * ws[col] + bias[col] (ws_vec / bias may be NULL: ws, 0), acc the int32
+ * products of a [M][K] and w [N][K]; the fp32 x is never stored.  work: M + 2 ints, work[0] the
+ * error word (0 on entry; a bounded wait that gave up writes its code), the rest the list of rows
+ * left to the exact kernel.  Shapes: K a multiple of 128 up to 2048, N a multiple of 256 up to
+ * 2048, a / w / q 16-byte aligned.  No counterpart in the reference ABI (a parity hook).
+ * Returns 0, -1 (arguments or shape) or -4 (launch). */
+int wasr_gemm_gelu_quant(const int8_t* a, const float* xs, const int8_t* w, float ws, const float* ws_vec,
+                         const float* bias, int M, int K, int N, int8_t* q, float* qs, int* work, void* stream);
+
 /* Parity hook for the certified GELU: scans the float bit patterns [start, start + count)
  * (both even, start + count <= 2^32) and accumulates into the device array stats[8] (zeroed by
  * the caller), with g~ the approximation and g the exact GELU: [0] the largest |g~ - g| - B |g~|

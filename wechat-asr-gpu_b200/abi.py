@@ -116,6 +116,7 @@ SIGNATURES = {
     "wasr_gelu_quant": (I, [P, I, I, P, P, I, P]),
     "wasr_conv3_quant": (I, [P, P, P, P, I, I, P, P, P]),
     "wasr_conv2": (I, [P, P, P, P, P, I, I, I, P, P]),
+    "wasr_gemm_gelu_quant": (I, [P, P, P, F, P, P, I, I, I, P, P, P, P]),
     "wasr_gelu_cert_scan": (I, [U64, U64, P, P]),
     "wasr_i8_mma_peak": (I, [I, I, P, P]),
     "wasr_version": (C.c_char_p, []),

@@ -278,11 +278,24 @@ int enqueue_chunk(WasrModel* m, const Chunk& c, const int* seg, float* logits, L
     TRY(K(WASR_K_GEMM_O, [&] { return gemm_run(gemm_args(m, xq, xs, M, D, L.o, D, L.ob, EPI_F32_ADD, hh, D), st); }));
     // middle norm -> f1 + bias + GELU (+ row max) -> quant -> f2 + bias, residual fused
     TRY(K(WASR_K_LN, [&] { return launch_ln_quant(hh, nullptr, fptr(m, L.mn_g), fptr(m, L.mn_b), M, xq, xs, st); }));
-    TRY(K(WASR_K_GEMM_F1, [&] {
-      return gemm_run(gemm_args(m, xq, xs, M, D, L.f1, FF, L.f1b, EPI_F32, ff, FF), st);
-    }));
-    TRY(K(WASR_K_GELU, [&] { return launch_gelu_quant_ro(ff, M, FF, xq, xs, st); }));
-    TRY(K(WASR_K_GEMM_F2, [&] { return gemm_run(gemm_args(m, xq, xs, M, FF, L.f2, D, L.f2b, EPI_F32_ADD, hh, D), st); }));
+    // f1, GELU and the row quantisation in one kernel (gemm_gq.cuh): its int8 rows, scales and
+    // exact-row list take the place of the fp32 f1 output in the ff region
+    int8_t* const q2 = reinterpret_cast<int8_t*>(ff);
+    float* const s2 = reinterpret_cast<float*>(q2 + static_cast<size_t>(M) * FF);
+    GemmArgs g1 = gemm_args(m, xq, xs, M, D, L.f1, FF, L.f1b, EPI_GELU_Q, nullptr, FF);
+    g1.q_out = q2;
+    g1.q_scale = s2;
+    g1.fix = reinterpret_cast<int*>(s2 + M);
+    if (gemm_gq_supported(g1)) {
+      TRY(K(WASR_K_GEMM_F1, [&] { return gemm_run(g1, st); }));
+      TRY(K(WASR_K_GEMM_F2, [&] { return gemm_run(gemm_args(m, q2, s2, M, FF, L.f2, D, L.f2b, EPI_F32_ADD, hh, D), st); }));
+    } else {  // f1's fp32 output, then the certified GELU + quant kernel
+      TRY(K(WASR_K_GEMM_F1, [&] {
+        return gemm_run(gemm_args(m, xq, xs, M, D, L.f1, FF, L.f1b, EPI_F32, ff, FF), st);
+      }));
+      TRY(K(WASR_K_GELU, [&] { return launch_gelu_quant_ro(ff, M, FF, xq, xs, st); }));
+      TRY(K(WASR_K_GEMM_F2, [&] { return gemm_run(gemm_args(m, xq, xs, M, FF, L.f2, D, L.f2b, EPI_F32_ADD, hh, D), st); }));
+    }
   }
   // output layer + argmax (src/model.rs:498-501)
   TRY(K(WASR_K_QUANT, [&] { return launch_quant_rows(hh, M, D, D, xq, xs, st); }));
@@ -577,6 +590,31 @@ int forward_impl(WasrModel* m, const float* feats, const int32_t* t, int n, uint
 extern "C" {
 
 const char* wasr_version(void) { return "wasr-b200 engine 1.0 (batched ragged windows; sm_100a)"; }
+
+// Parity hook for the engine's fused f1 + GELU + row quantisation (see include/wasr.h).
+int wasr_gemm_gelu_quant(const int8_t* a, const float* xs, const int8_t* w, float ws, const float* ws_vec,
+                         const float* bias, int M, int K, int N, int8_t* q, float* qs, int* work, void* stream) {
+  if (!a || !xs || !w || !q || !qs || !work || M < 0 || K <= 0 || N <= 0) return -1;
+  if (M == 0) return 0;
+  if (!gemm_init()) return -4;
+  GemmArgs g{};
+  g.a = a;
+  g.b = w;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.n_store = N;
+  g.xs = xs;
+  g.ws = ws;
+  g.ws_vec = ws_vec;
+  g.bias = bias;
+  g.err = work;
+  g.epi = EPI_GELU_Q;
+  g.q_out = q;
+  g.q_scale = qs;
+  g.fix = work + 1;
+  return gemm_run(g, static_cast<cudaStream_t>(stream));
+}
 
 WasrModel* wasr_model_create(const void* blob, size_t bytes, const WasrPlan* plan, int device, int max_rows) {
   if (!blob || !bytes || !plan || max_rows <= 0) return nullptr;

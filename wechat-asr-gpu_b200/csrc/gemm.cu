@@ -11,6 +11,7 @@
 #include <unordered_map>
 
 #include "gemm.cuh"
+#include "gemm_gq.cuh"
 
 namespace wasr {
 
@@ -156,12 +157,49 @@ int launch_epi(const GemmArgs& g, cudaStream_t s) {
   return launch_tc<64, EPI>(g, s);
 }
 
+bool ensure_gq_attr() {
+  static unsigned done = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (done & (1u << (dev & 31))) return true;
+  if (cudaFuncSetAttribute(gemm_i8_gelu_q, cudaFuncAttributeMaxDynamicSharedMemorySize, GqCfg::SMEM) != cudaSuccess)
+    return false;
+  done |= 1u << (dev & 31);
+  return true;
+}
+
+}  // namespace
+
+bool gemm_gq_supported(const GemmArgs& g) {
+  const uintptr_t al = reinterpret_cast<uintptr_t>(g.a) | reinterpret_cast<uintptr_t>(g.b) |
+                       reinterpret_cast<uintptr_t>(g.q_out);
+  return gemm_init() && g.K % GqCfg::BK == 0 && g.K <= 2048 && g.n_store == g.N && g.N % GqCfg::BN == 0 &&
+         g.N <= GqCfg::NMAX && g.q_out && g.q_scale && g.fix && (al & 15) == 0;
+}
+
+namespace {
+
+// f1 + GELU + row quantisation (gemm_gq.cuh): the fused kernel, then the exact kernel for the
+// rows it listed.  Shapes it does not take return -1 (gemm_gq_supported says which).
+int launch_gq(const GemmArgs& g, cudaStream_t s) {
+  if (!gemm_gq_supported(g)) return -1;
+  CUtensorMap ta, tb;
+  if (!tensor_map(g.a, g.M, g.K, g.K, 128, 0, &ta) || !tensor_map(g.b, g.N, g.K, g.K, GqCfg::BN, 0, &tb)) return -4;
+  if (!ensure_gq_attr()) return -4;
+  if (cudaMemsetAsync(g.fix, 0, sizeof(int), s) != cudaSuccess) return -4;
+  const int blocks = (g.M + GqCfg::BM - 1) / GqCfg::BM;
+  gemm_i8_gelu_q<<<std::min(blocks, num_sms()), GqCfg::THREADS, GqCfg::SMEM, s>>>(ta, tb, g);
+  gelu_q_rows_exact_k<<<std::min(g.M, 2 * num_sms()), 256, 0, s>>>(g);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}
+
 }  // namespace
 
 bool gemm_prepare() {
   gemm_init();
   return prepare_epi<EPI_F32>() && prepare_epi<EPI_F32_ADD>() && prepare_epi<EPI_I32>() &&
-         prepare_epi<EPI_F32_ROWMAX>() && prepare_epi<EPI_GELU_ROWMAX>() && prepare_epi<EPI_ARGMAX>();
+         prepare_epi<EPI_F32_ROWMAX>() && prepare_epi<EPI_GELU_ROWMAX>() && prepare_epi<EPI_ARGMAX>() &&
+         ensure_gq_attr();
 }
 
 int gemm_run(const GemmArgs& g, cudaStream_t s) {
@@ -174,6 +212,7 @@ int gemm_run(const GemmArgs& g, cudaStream_t s) {
     case EPI_F32_ROWMAX: return launch_epi<EPI_F32_ROWMAX>(g, s);
     case EPI_GELU_ROWMAX: return launch_epi<EPI_GELU_ROWMAX>(g, s);
     case EPI_ARGMAX: return launch_epi<EPI_ARGMAX>(g, s);
+    case EPI_GELU_Q: return launch_gq(g, s);
   }
   return -1;
 }

@@ -26,6 +26,7 @@ enum Epi : int {
   EPI_F32_ROWMAX = 3,  // EPI_F32 + atomic row max of |out|  (first half of wp_gemm_q)
   EPI_GELU_ROWMAX = 4, // out = gelu(...) + row max of |out| (first half of wp_gemm_qg / FF1)
   EPI_ARGMAX = 5,      // per-row (max logit, first index) into packed 64-bit keys
+  EPI_GELU_Q = 6,      // int8 rows + scales of quant(gelu(out)), out never stored (gemm_gq.cuh)
 };
 
 struct GemmArgs {
@@ -48,6 +49,9 @@ struct GemmArgs {
   unsigned long long wait_ns;  // limit of every mbarrier wait (0: WAIT_LIMIT_NS)
   int idle_producer;   // failure-handling test only: the producer issues no loads, so the
                        // consumers' waits run out with nothing in flight
+  int8_t* q_out;       // EPI_GELU_Q: int8 rows [M][n_store]
+  float* q_scale;      // EPI_GELU_Q: row scales [M]
+  int* fix;            // EPI_GELU_Q: [1 + M] ints, the count and the rows left to the exact kernel
 };
 
 template <int EPI>
@@ -649,6 +653,9 @@ __global__ void __launch_bounds__(256) gemm_i8_simt(GemmArgs g) {
 int gemm_run(const GemmArgs& g, cudaStream_t stream);
 // Initialise the tensor-map encoder (driver entry point); false if unavailable.
 bool gemm_init();
+// Whether gemm_run takes this EPI_GELU_Q call (K a multiple of 128 up to 2048, N a multiple of
+// 256 up to 2048, 16-byte aligned operands and output, the output buffers given).
+bool gemm_gq_supported(const GemmArgs& g);
 // Set every kernel's shared-memory attribute on the current device (call outside capture).
 bool gemm_prepare();
 
