@@ -62,8 +62,9 @@ def _check(L, dev, orc, args):
     return nfix
 
 
+# 9729 rows: 77 row blocks of 128, more than half of the 148 SMs
 @pytest.mark.parametrize("m,k,n", [(1, 512, 2048), (127, 512, 2048), (300, 512, 2048), (4097, 512, 2048),
-                                   (200, 128, 256), (333, 1024, 1024)])
+                                   (9729, 512, 2048), (200, 128, 256), (333, 1024, 1024)])
 def test_gemm_gelu_q_random(gpu_lib, dev, orc, m, k, n):
     rng = np.random.default_rng(m * 7 + k + n)
     assert _check(gpu_lib, dev, orc, _case(rng, m, k, n)) == 0

@@ -125,6 +125,31 @@ def test_batched_ragged_equals_one_by_one(pkg, gpu_lib):
         eng.close()
 
 
+@pytest.mark.parametrize("per_channel", [False, True])
+def test_fused_ff1_chunk_equals_two_kernel_chunks(pkg, gpu_lib, per_channel):
+    """A chunk of at least 12,800 rows runs f1 + GELU + quant as one fused kernel; smaller chunks
+    run the f1 GEMM and the GELU kernel.  Both keep the reference's results, so the logits and
+    ids of the same windows agree bit for bit (a small vocabulary keeps the logits small)."""
+    blob, plan = pkg.synth.make_model(seed=7, n_layers=2, vocab=512, per_channel=per_channel)
+    lengths = pkg.synth.config_lengths(4)[:110]
+    wins = [pkg.fbank(pkg.synth.make_audio(700 + i, s))[0] for i, s in enumerate(lengths)]
+    rows = sum((w.shape[0] - 5) // 5 + 1 for w in wins)
+    assert 12800 <= rows < 40000, rows
+    fused = pkg.Engine(blob, plan, max_rows=rows)
+    split = pkg.Engine(blob, plan, max_rows=6000)
+    try:
+        ids_f, lo_f = fused.forward(wins, want_logits=True)
+        ids_s, lo_s = split.forward(wins, want_logits=True)
+        assert fused.error() == 0 and split.error() == 0
+        for a, b in zip(lo_f, lo_s):
+            np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32))
+        for a, b in zip(ids_f, ids_s):
+            np.testing.assert_array_equal(a, b)
+    finally:
+        fused.close()
+        split.close()
+
+
 def test_large_chunk_two_branches_equal_small_chunks(pkg, gpu_lib):
     """A chunk of at least 40,000 rows runs as two halves of its windows on two streams (one
     graph with two branches); its ids equal those of the same windows run as chunks below that

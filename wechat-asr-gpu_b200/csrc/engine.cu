@@ -164,6 +164,10 @@ const float* fptr(const WasrModel* m, uint64_t off) {
   return off == WASR_NONE ? nullptr : reinterpret_cast<const float*>(m->w + off);
 }
 
+// Chunks of at least this many rows run f1 + GELU + quant as one fused kernel (100 row blocks
+// of 128: two thirds of a wave of 148 SMs and more).
+constexpr int kFusedGeluRows = 12800;
+
 GemmArgs gemm_args(WasrModel* m, const int8_t* a, const float* xs, int M, int K, const WasrMat& q, int N,
                    uint64_t bias, int epi, float* out, int ldo) {
   GemmArgs g{};
@@ -278,15 +282,18 @@ int enqueue_chunk(WasrModel* m, const Chunk& c, const int* seg, float* logits, L
     TRY(K(WASR_K_GEMM_O, [&] { return gemm_run(gemm_args(m, xq, xs, M, D, L.o, D, L.ob, EPI_F32_ADD, hh, D), st); }));
     // middle norm -> f1 + bias + GELU (+ row max) -> quant -> f2 + bias, residual fused
     TRY(K(WASR_K_LN, [&] { return launch_ln_quant(hh, nullptr, fptr(m, L.mn_g), fptr(m, L.mn_b), M, xq, xs, st); }));
-    // f1, GELU and the row quantisation in one kernel (gemm_gq.cuh): its int8 rows, scales and
-    // exact-row list take the place of the fp32 f1 output in the ff region
+    // f1, GELU and the row quantisation in one kernel (gemm_gq.cuh) for chunks of at least
+    // kFusedGeluRows rows: its int8 rows, scales and exact-row list take the place of the fp32 f1
+    // output in the ff region.  It runs one CTA per 128-row block, so a small chunk leaves SMs
+    // idle and the two-kernel path is faster (measured: 8,802 rows 15.69 against 16.72 ms per
+    // step, 17,329 rows 29.13 against 28.84)
     int8_t* const q2 = reinterpret_cast<int8_t*>(ff);
     float* const s2 = reinterpret_cast<float*>(q2 + static_cast<size_t>(M) * FF);
     GemmArgs g1 = gemm_args(m, xq, xs, M, D, L.f1, FF, L.f1b, EPI_GELU_Q, nullptr, FF);
     g1.q_out = q2;
     g1.q_scale = s2;
     g1.fix = reinterpret_cast<int*>(s2 + M);
-    if (gemm_gq_supported(g1)) {
+    if (M >= kFusedGeluRows && gemm_gq_supported(g1)) {
       TRY(K(WASR_K_GEMM_F1, [&] { return gemm_run(g1, st); }));
       TRY(K(WASR_K_GEMM_F2, [&] { return gemm_run(gemm_args(m, q2, s2, M, FF, L.f2, D, L.f2b, EPI_F32_ADD, hh, D), st); }));
     } else {  // f1's fp32 output, then the certified GELU + quant kernel
