@@ -71,6 +71,31 @@ def test_wk_norm_quant_and_add(gpu_lib, dev, orc, t):
     assert L.wk_last_error() == 0
 
 
+def test_wk_norm_quant_ties_and_non_finite(gpu_lib, dev, orc):
+    """With g = 0 every normalised value is its bias, so biases of 127 and +-(k + 0.5) put exact
+    .5 ties in every row (scale 1, round half away from zero); one row holds a NaN and one an
+    infinity (the rows the kernel quantises element by element)."""
+    L = gpu_lib
+    t = 40
+    rng = np.random.default_rng(3)
+    h = rng.standard_normal((t, 512)).astype(np.float32)
+    h[5, 17] = np.nan
+    h[9, 100] = np.inf
+    g = np.zeros(512, np.float32)
+    b = np.round(rng.uniform(-126, 126, 512)).astype(np.float32) + np.float32(0.5)
+    b[0] = 127.0
+    b[1:9] = [0.5, -0.5, 1.5, -1.5, 2.5, -2.5, 126.5, -126.5]
+    ph, pg, pb = dev.put(h), dev.put(g), dev.put(b)
+    pq, ps = dev.empty(t * 512), dev.empty(t * 4)
+    L.wk_norm_quant(None, ph, pg, pb, t, 512, pq, ps)
+    assert L.wk_last_error() == 0
+    q, s = orc.quant(orc.norm(h, g, b))
+    got = dev.get(pq, (t, 512), np.int8)
+    np.testing.assert_array_equal(dev.get(ps, (t,), np.float32).view(np.uint32), s.view(np.uint32))
+    np.testing.assert_array_equal(got, q)
+    assert list(got[0, 1:9]) == [1, -1, 2, -2, 3, -3, 127, -127]
+
+
 def test_wk_norm_quant_other_width(gpu_lib, dev, orc):
     L = gpu_lib
     t, d = 9, 200
