@@ -232,6 +232,15 @@ int wasr_conv2(const float* y1, const float* c2, float* c2t, const int* foff, co
 int wasr_gemm_gelu_quant(const int8_t* a, const float* xs, const int8_t* w, float ws, const float* ws_vec,
                          const float* bias, int M, int K, int N, int8_t* q, float* qs, int* work, void* stream);
 
+/* Failure-handling probe of the same kernel (no counterpart in the reference ABI): its producer
+ * issues no loads, so the bounded wait for the first operands runs out after wait_ns
+ * (0 < wait_ns <= 1e9) with nothing in flight; the kernel writes a nonzero code to work[0] (0 on
+ * entry), frees its tensor memory and returns, and the stream stays usable.  q and qs receive no
+ * meaningful values.  Returns 0, -1 / -2 (arguments) or -4 (launch). */
+int wasr_gemm_gelu_quant_wait_probe(const int8_t* a, const float* xs, const int8_t* w, float ws, const float* ws_vec,
+                                    const float* bias, int M, int K, int N, int8_t* q, float* qs, int* work,
+                                    unsigned long long wait_ns, void* stream);
+
 /* Parity hook for the certified GELU: scans the float bit patterns [start, start + count)
  * (both even, start + count <= 2^32) and accumulates into the device array stats[8] (zeroed by
  * the caller), with g~ the approximation and g the exact GELU: [0] the largest |g~ - g| - B |g~|

@@ -118,6 +118,25 @@ def test_gemm_gelu_q_near_tied_and_boundary_rows(gpu_lib, dev, orc):
     assert _check(gpu_lib, dev, orc, (a, xs * np.float32(8.0), w, ws, ws_vec, bias)) == 0
 
 
+def test_gemm_gelu_q_bounded_wait_runs_out_and_recovers(gpu_lib, dev, orc):
+    """The producer issues no loads, so the MMA warp's bounded wait (1 ms) runs out with nothing
+    in flight: the kernel records an error code and returns (no fault, no hang), and the next
+    call on the same stream is bit-exact again."""
+    L = gpu_lib
+    rng = np.random.default_rng(12)
+    a, xs, w, ws, ws_vec, bias = _case(rng, 300, 512, 2048)
+    m, n = a.shape[0], w.shape[0]
+    pa, px, pw, pv, pb = dev.put(a), dev.put(xs), dev.put(w), dev.put(ws_vec), dev.put(bias)
+    pq, ps = dev.empty(m * n), dev.empty(m * 4)
+    work = dev.put(np.zeros(m + 2, np.int32))
+    assert L.wasr_gemm_gelu_quant_wait_probe(pa, px, pw, float(ws), pv, pb, m, 512, n, pq, ps, work,
+                                             1_000_000, None) == 0
+    wk = dev.get(work, (m + 2,), np.int32)
+    assert wk[0] in (1, 2, 3), f"error word {wk[0]}"
+    assert wk[1] == 0
+    _check(L, dev, orc, (a, xs, w, ws, ws_vec, bias))
+
+
 def test_gemm_gelu_q_twice_same_result(gpu_lib, dev, orc):
     """Two calls in a row on the same buffers: the row list is reset per call."""
     rng = np.random.default_rng(8)

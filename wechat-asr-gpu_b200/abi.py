@@ -117,6 +117,7 @@ SIGNATURES = {
     "wasr_conv3_quant": (I, [P, P, P, P, I, I, P, P, P]),
     "wasr_conv2": (I, [P, P, P, P, P, I, I, I, P, P]),
     "wasr_gemm_gelu_quant": (I, [P, P, P, F, P, P, I, I, I, P, P, P, P]),
+    "wasr_gemm_gelu_quant_wait_probe": (I, [P, P, P, F, P, P, I, I, I, P, P, P, U64, P]),
     "wasr_gelu_cert_scan": (I, [U64, U64, P, P]),
     "wasr_i8_mma_peak": (I, [I, I, P, P]),
     "wasr_version": (C.c_char_p, []),

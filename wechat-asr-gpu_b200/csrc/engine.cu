@@ -623,6 +623,36 @@ int wasr_gemm_gelu_quant(const int8_t* a, const float* xs, const int8_t* w, floa
   return gemm_run(g, static_cast<cudaStream_t>(stream));
 }
 
+// Failure-handling probe of the fused kernel: its producer issues no loads, so the MMA warp's wait
+// for the first k-block runs out after wait_ns with nothing in flight; the kernel records the
+// error code in work[0], releases its tensor memory and returns.
+int wasr_gemm_gelu_quant_wait_probe(const int8_t* a, const float* xs, const int8_t* w, float ws, const float* ws_vec,
+                                    const float* bias, int M, int K, int N, int8_t* q, float* qs, int* work,
+                                    unsigned long long wait_ns, void* stream) {
+  if (!a || !xs || !w || !q || !qs || !work || M <= 0 || K <= 0 || N <= 0) return -1;
+  if (wait_ns == 0 || wait_ns > 1000000000ull) return -2;
+  if (!gemm_init()) return -4;
+  GemmArgs g{};
+  g.a = a;
+  g.b = w;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.n_store = N;
+  g.xs = xs;
+  g.ws = ws;
+  g.ws_vec = ws_vec;
+  g.bias = bias;
+  g.err = work;
+  g.epi = EPI_GELU_Q;
+  g.q_out = q;
+  g.q_scale = qs;
+  g.fix = work + 1;
+  g.wait_ns = wait_ns;
+  g.idle_producer = 1;
+  return gemm_run(g, static_cast<cudaStream_t>(stream));
+}
+
 WasrModel* wasr_model_create(const void* blob, size_t bytes, const WasrPlan* plan, int device, int max_rows) {
   if (!blob || !bytes || !plan || max_rows <= 0) return nullptr;
   if (plan->n_layers < 0 || plan->n_layers > WASR_MAX_LAYERS || plan->out_n <= 0) return nullptr;
