@@ -211,6 +211,16 @@ int wasr_gelu_quant(const float* y, int m, int k, int8_t* xq, float* xs, int exa
 int wasr_conv3_quant(const float* y2, const float* c3, float* prep, const int* roff, int nseg, int rows,
                      int8_t* xq, float* xs, void* stream);
 
+/* conv1 of the conv frontend (src/model.rs:398-418) on device buffers: x [frames][40],
+ * c1 [32][25], y1 [frames][32][40].  by_value = 1 runs the engine's kernel, which takes the
+ * weights as a kernel argument (this call copies them to the host first and waits for the copy);
+ * 0 the kernel of the reference ABI's wk_front.  foff: device frame prefix offsets of nseg
+ * windows stacked in x, or NULL for one window.  Both keep the reference's dotf order, so y1
+ * equals the CPU's bit for bit.  No counterpart in the reference ABI (a parity hook).  Returns 0,
+ * -1 (arguments) or -4 (copy or launch). */
+int wasr_conv1(const float* x, const float* c1, const int* foff, int nseg, int frames, int by_value, float* y1,
+               void* stream);
+
 /* conv2 of the conv frontend (src/model.rs:420-444) on device buffers: y1 [frames][32][40],
  * c2 [64][1568], y2 [rows][64][41] (column 40 written 0).  c2t: scratch of 64 * 1568 floats,
  * filled here with the transposed weights, selects the engine's position-pair kernel; NULL runs

@@ -44,6 +44,7 @@ def lib():
             "wo_gelu_array": (None, [P, P, I64]),
             "wo_attention": (None, [P, P, P, I, P]),
             "wo_frontend": (I, [P, I, P, P, P, P]),
+            "wo_conv1": (None, [P, I, P, P]),
             "wo_conv2": (None, [P, I, P, P]),
             "wo_conv3": (None, [P, I, P, P]),
             "wo_forward": (I, [P, P, P, I, P, P]),
@@ -164,6 +165,15 @@ def frontend(x, c1, c2, c3):
                       _p(np.ascontiguousarray(c2, np.float32)),
                       _p(np.ascontiguousarray(c3, np.float32)), _p(y3))
     return y3[:t1]
+
+
+def conv1(x, c1):
+    """The conv1 stage alone (src/model.rs:398-418): x [t][40] -> y1 [t][32][40]."""
+    x = np.ascontiguousarray(x, np.float32)
+    t = x.shape[0]
+    y1 = np.zeros((max(t, 1), 32, 40), np.float32)
+    lib().wo_conv1(_p(x), t, _p(np.ascontiguousarray(c1, np.float32)), _p(y1))
+    return y1[:t]
 
 
 def conv2(y1, c2):

@@ -242,6 +242,28 @@ void wo_attention(const float* q, const float* k, const float* v, int t, float* 
   }
 }
 
+/* src/model.rs:398-418: conv 5x5, 1->32, pad 2 in time and frequency, of one window's
+ * x [t][40] -> y1 [t][32][40] (im2col + dotf + ReLU) */
+void wo_conv1(const float* x, int t, const float* c1, float* y1) {
+#pragma omp parallel for schedule(static)
+  for (int ti = 0; ti < t; ti++) {
+    float p[DIM][25];
+    memset(p, 0, sizeof(p));
+    for (int f = 0; f < DIM; f++)
+      for (int i = 0; i < 5; i++) {
+        int tt = ti + i - 2;
+        if (tt < 0 || tt >= t) continue;
+        for (int j = 0; j < 5; j++) {
+          int ff = f + j - 2;
+          if (ff >= 0 && ff < DIM) p[f][i * 5 + j] = x[(int64_t)tt * DIM + ff];
+        }
+      }
+    float* y = y1 + (int64_t)ti * F1 * DIM;
+    for (int o = 0; o < F1; o++)
+      for (int f = 0; f < DIM; f++) y[o * DIM + f] = fmaxf(wo_dotf(c1 + o * 25, p[f], 25), 0.0f);
+  }
+}
+
 /* src/model.rs:420-444: conv 7x7, 32->64, time stride 5 (pad 1), frequency pad 3 of one
  * window's y1 [t][32][40] -> y2 [t1][64][41], t1 = (t - 5) / 5 + 1; column 40 is 0 */
 void wo_conv2(const float* y1, int t, const float* c2, float* y2) {
@@ -307,24 +329,7 @@ int wo_frontend(const float* x, int t, const float* c1, const float* c2, const f
   int t1 = (t - 5) / 5 + 1;
   float* y1 = (float*)calloc((size_t)t * F1 * DIM, sizeof(float));
   float* y2 = (float*)calloc((size_t)t1 * F2 * W2, sizeof(float));
-  /* conv 5x5, 1->32, pad 2 in time and frequency */
-#pragma omp parallel for schedule(static)
-  for (int ti = 0; ti < t; ti++) {
-    float p[DIM][25];
-    memset(p, 0, sizeof(p));
-    for (int f = 0; f < DIM; f++)
-      for (int i = 0; i < 5; i++) {
-        int tt = ti + i - 2;
-        if (tt < 0 || tt >= t) continue;
-        for (int j = 0; j < 5; j++) {
-          int ff = f + j - 2;
-          if (ff >= 0 && ff < DIM) p[f][i * 5 + j] = x[(int64_t)tt * DIM + ff];
-        }
-      }
-    float* y = y1 + (int64_t)ti * F1 * DIM;
-    for (int o = 0; o < F1; o++)
-      for (int f = 0; f < DIM; f++) y[o * DIM + f] = fmaxf(wo_dotf(c1 + o * 25, p[f], 25), 0.0f);
-  }
+  wo_conv1(x, t, c1, y1);
   wo_conv2(y1, t, c2, y2);
   wo_conv3(y2, t1, c3, y3);
   free(y1);

@@ -52,6 +52,8 @@ void wo_gelu_array(const float* x, float* y, int64_t n);
 void wo_attention(const float* q, const float* k, const float* v, int t, float* out);
 /* src/model.rs:389-478: x [t][40] -> y3 [t1][3840]; returns t1 (0 if t < 5) */
 int wo_frontend(const float* x, int t, const float* c1, const float* c2, const float* c3, float* y3);
+/* the conv1 stage alone (src/model.rs:398-418): x [t][40] -> y1 [t][32][40] */
+void wo_conv1(const float* x, int t, const float* c1, float* y1);
 /* the conv2 stage alone (src/model.rs:420-444): y1 [t][32][40] -> y2 [t1][64][41] */
 void wo_conv2(const float* y1, int t, const float* c2, float* y2);
 /* the conv3 stage alone (src/model.rs:446-468): y2 [t1][64][41] -> y3 [t1][3840] */

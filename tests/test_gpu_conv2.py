@@ -1,4 +1,8 @@
-"""conv2 of the conv frontend (src/model.rs:420-444) through the wasr_conv2 parity hook.
+"""conv1 and conv2 of the conv frontend (src/model.rs:398-444) through the wasr_conv1 /
+wasr_conv2 parity hooks.
+
+conv1: the engine's kernel takes its 32 x 25 weights by value (a kernel argument), the reference
+ABI's reads them from device memory; both must give the oracle's y1 bit for bit.
 
 Two kernels compute it: the engine's position-pair kernel (c2t given: packed products
 fma.rn(x, w, -0) and packed rounded adds per dotf lane) and the reference ABI's lane-pair kernel
@@ -88,3 +92,32 @@ def test_conv2_special_inputs(gpu_lib, dev, orc):
     _check(gpu_lib, dev, orc, tiny, _c2(rng, 1e-20), [17])
     huge = _y1(rng, 12, 1e30)
     _check(gpu_lib, dev, orc, huge, _c2(rng, 1e10), [12])
+
+
+def _run_conv1(L, dev, x, c1, lens, by_value):
+    frames = x.shape[0]
+    py1 = dev.put(np.full((frames, 32, 40), np.nan, np.float32))
+    if len(lens) == 1:
+        rc = L.wasr_conv1(dev.put(x), dev.put(c1), None, 0, frames, by_value, py1, None)
+    else:
+        foff = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+        rc = L.wasr_conv1(dev.put(x), dev.put(c1), dev.put(foff), len(lens), frames, by_value, py1, None)
+    assert rc == 0
+    return dev.get(py1, (frames, 32, 40), np.float32)
+
+
+@pytest.mark.parametrize("lens", [[1], [2], [5], [57], [400], [5, 1, 13, 2, 7, 64, 3]])
+def test_conv1(gpu_lib, dev, orc, lens):
+    rng = np.random.default_rng(sum(lens) + len(lens))
+    x = rng.standard_normal((sum(lens), 40)).astype(np.float32)
+    x[rng.random(x.shape) < 0.05] = -0.0
+    c1 = (rng.standard_normal((32, 1, 5, 5)) * 0.2).astype(np.float32)
+    want, f = [], 0
+    for t in lens:
+        want.append(orc.conv1(x[f:f + t], c1))
+        f += t
+    want = np.concatenate(want)
+    for by_value in (1, 0):
+        got = _run_conv1(gpu_lib, dev, x, c1, lens, by_value)
+        np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32),
+                                      err_msg="weights by value" if by_value else "weights from memory")

@@ -115,6 +115,7 @@ SIGNATURES = {
     "wasr_eval_math": (I, [I, P, P, I, P]),
     "wasr_gelu_quant": (I, [P, I, I, P, P, I, P]),
     "wasr_conv3_quant": (I, [P, P, P, P, I, I, P, P, P]),
+    "wasr_conv1": (I, [P, P, P, I, I, I, P, P]),
     "wasr_conv2": (I, [P, P, P, P, P, I, I, I, P, P]),
     "wasr_gemm_gelu_quant": (I, [P, P, P, F, P, P, I, I, I, P, P, P, P]),
     "wasr_gemm_gelu_quant_wait_probe": (I, [P, P, P, F, P, P, I, I, I, P, P, P, U64, P]),

@@ -72,6 +72,7 @@ struct WasrModel {
   bool qkv_fused[WASR_MAX_LAYERS] = {};
   // activations
   float *feats = nullptr, *y1 = nullptr, *y2 = nullptr;
+  Conv1W c1w{};             // conv1 weights on the host: conv1w_k takes them by value
   float* c2pre = nullptr;   // conv2 weights transposed to [tap][out] (the position-pair kernel)
   float* c3cert = nullptr;  // conv3 weights transposed for conv3_cert_k, and their row norms
   int8_t* xq = nullptr;
@@ -254,7 +255,7 @@ int enqueue_chunk(WasrModel* m, const Chunk& c, const int* seg, float* logits, L
   const int M = c.rows;
   const WasrPlan& P = m->plan;
   // conv frontend -> int8 rows of y3 -> linear (src/model.rs:389-478,489)
-  TRY(K(WASR_K_CONV1, [&] { return launch_conv1(feats, fptr(m, P.c1), s, c.frames, y1, st); }));
+  TRY(K(WASR_K_CONV1, [&] { return launch_conv1_w(feats, m->c1w, s, c.frames, y1, st); }));
   TRY(K(WASR_K_CONV2, [&] { return launch_conv2(y1, fptr(m, P.c2), m->c2pre, s, M, y2, st); }));
   // conv3 with its row quantisation fused and certified (int8 rows identical to quant(conv3))
   TRY(K(WASR_K_CONV3, [&] { return launch_conv3_cert(y2, fptr(m, P.c3), m->c3cert, s, M, xq, xs, st); }));
@@ -676,6 +677,8 @@ WasrModel* wasr_model_create(const void* blob, size_t bytes, const WasrPlan* pla
   if (ok) *m->err_host = 0;
   m->w_bytes = bytes;
   ok = ok && dmalloc(&m->w, bytes) && cudaMemcpy(m->w, blob, bytes, cudaMemcpyHostToDevice) == cudaSuccess;
+  ok = ok && plan->c1 <= bytes && bytes - plan->c1 >= sizeof(m->c1w.w);
+  if (ok) std::memcpy(m->c1w.w, static_cast<const uint8_t*>(blob) + plan->c1, sizeof(m->c1w.w));
   const size_t R = static_cast<size_t>(max_rows), Fr = static_cast<size_t>(m->max_frames);
   ok = ok && dmalloc(&m->feats, Fr * DIM) && dmalloc(&m->y1, Fr * C1 * DIM) && dmalloc(&m->y2, R * C2 * W2) &&
        dmalloc(&m->xq, R * FLAT) && dmalloc(&m->xs, R) && dmalloc(&m->h, R * D) &&

@@ -60,6 +60,45 @@ __global__ void __launch_bounds__(128) conv1_k(const float* __restrict__ x, cons
   }
 }
 
+// conv1 of the engine: the weights arrive as a kernel argument (a __grid_constant__ struct in the
+// constant bank) and the channel loop is fully unrolled, so every multiply names its weight
+// directly instead of loading it from shared memory (one load per multiply in conv1_k).
+__global__ void __launch_bounds__(128) conv1w_k(const float* __restrict__ x, const __grid_constant__ Conv1W cw,
+                                                Segs s, int total, float* __restrict__ y1) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= total * DIM) return;
+  const int g = idx / DIM, f = idx - g * DIM;
+  const int sw = s.seg_of_frame(g);
+  const int fb = s.frame_begin(sw), t = s.frames(sw), ti = g - fb;
+  float p[25];
+#pragma unroll
+  for (int i = 0; i < 5; i++) {
+    const int tt = ti + i - 2;
+#pragma unroll
+    for (int j = 0; j < 5; j++) {
+      const int ff = f + j - 2;
+      p[i * 5 + j] = (tt >= 0 && tt < t && ff >= 0 && ff < DIM) ? x[static_cast<int64_t>(fb + tt) * DIM + ff] : 0.0f;
+    }
+  }
+  float* out = y1 + static_cast<int64_t>(g) * (C1 * DIM) + f;
+#pragma unroll
+  for (int o = 0; o < C1; o++) {
+    const float* wo = cw.w + o * 25;
+    float a[8];
+#pragma unroll
+    for (int l = 0; l < 8; l++) a[l] = __fadd_rn(0.0f, __fmul_rn(wo[l], p[l]));
+#pragma unroll
+    for (int c = 1; c < 3; c++)
+#pragma unroll
+      for (int l = 0; l < 8; l++) a[l] = __fadd_rn(a[l], __fmul_rn(wo[c * 8 + l], p[c * 8 + l]));
+    float sum = a[0];
+#pragma unroll
+    for (int l = 1; l < 8; l++) sum = __fadd_rn(sum, a[l]);
+    const float v = __fadd_rn(sum, __fmul_rn(wo[24], p[24]));
+    out[o * DIM] = fmaxf(v, 0.0f);
+  }
+}
+
 // ------------------------------------------------------------------------ conv2 / conv3
 // Both are dotf products of a weight row with a zero-padded patch (src/kernels.rs dotf: 8
 // lane accumulators, lane l takes taps l, l+8, l+16, ... in order, then the lanes are folded
@@ -1988,6 +2027,12 @@ bool kern_prepare() {
   return cudaGetLastError() == cudaSuccess;
 }
 
+int launch_conv1_w(const float* x, const Conv1W& w, Segs s, int total_frames, float* y1, cudaStream_t st) {
+  if (total_frames <= 0) return 0;
+  const int n = total_frames * DIM;
+  conv1w_k<<<(n + 127) / 128, 128, 0, st>>>(x, w, s, total_frames, y1);
+  return launched();
+}
 int launch_conv1(const float* x, const float* c1, Segs s, int total_frames, float* y1, cudaStream_t st) {
   if (total_frames <= 0) return 0;
   const int n = total_frames * DIM;
@@ -2275,6 +2320,27 @@ int wasr_conv3_quant(const float* y2, const float* c3, float* prep, const int* r
   s.t0 = 0;
   s.t10 = rows;
   return launch_conv3_cert(y2, c3, prep, s, rows, xq, xs, st);
+}
+
+// Parity hook for conv1: by_value = 1 runs the engine's kernel (the weights copied to the host
+// here and passed by value; this call waits for that copy), 0 the reference ABI's (weights read
+// from device memory).  foff = device frame offsets of nseg windows, or nullptr for one window.
+int wasr_conv1(const float* x, const float* c1, const int* foff, int nseg, int frames, int by_value, float* y1,
+               void* stream) {
+  if (!x || !c1 || !y1 || frames < 0 || (foff && nseg <= 0)) return -1;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Segs s{};
+  s.foff = foff;
+  s.roff = nullptr;
+  s.n = foff ? nseg : 1;
+  s.t0 = frames;
+  s.t10 = 0;
+  if (!by_value) return launch_conv1(x, c1, s, frames, y1, st);
+  Conv1W w;
+  if (cudaMemcpyAsync(w.w, c1, sizeof(w.w), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return -4;
+  return launch_conv1_w(x, w, s, frames, y1, st);
 }
 
 // Parity hook for conv2: c2t = conv2_prepare_floats() floats (filled here from c2) selects the

@@ -44,6 +44,12 @@ struct Segs {
 
 // host launchers (stream-ordered, no allocation); return 0 or -4 on launch failure
 int launch_conv1(const float* x, const float* c1, Segs s, int total_frames, float* y1, cudaStream_t st);
+// conv1 with its 32 x 25 weights passed by value (a kernel argument): every product reads its
+// weight from the constant bank, no shared-memory loads.  Same results as launch_conv1.
+struct Conv1W {
+  float w[C1 * 25];
+};
+int launch_conv1_w(const float* x, const Conv1W& w, Segs s, int total_frames, float* y1, cudaStream_t st);
 // c2t: the conv2 weights transposed to [tap][out] by conv2_prepare (conv2_prepare_floats()
 // floats), which selects the position-pair kernel; nullptr stages the weights from c2's
 // [out][tap] layout (the reference ABI's wk_front).
