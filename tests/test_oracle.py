@@ -181,6 +181,22 @@ def test_frontend_matches_torch_conv(orc):
     np.testing.assert_allclose(y3, y3r, rtol=1e-4, atol=1e-4)
 
 
+def test_conv1_stage_matches_torch_conv(orc):
+    """The conv1 stage alone (the checker of the GPU conv1 kernels), on windows of 1, 2 and 57
+    frames (padding 2 in time and frequency)."""
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(11)
+    c1 = rng.standard_normal((32, 1, 5, 5)).astype(np.float32) * 0.3
+    for t in (1, 2, 57):
+        x = rng.standard_normal((t, 40)).astype(np.float32)
+        y1 = orc.conv1(x, c1)
+        ref = torch.relu(torch.nn.functional.conv2d(torch.from_numpy(x).double()[None, None],
+                                                    torch.from_numpy(c1).double(), padding=2))
+        ref = ref[0].permute(1, 0, 2).numpy()                           # [t][32][40]
+        assert y1.shape == (t, 32, 40)
+        np.testing.assert_allclose(y1, ref, rtol=1e-5, atol=1e-5)
+
+
 def test_conv2_stage_matches_torch_conv(orc):
     """The conv2 stage alone (the checker of the GPU conv2 kernels), incl. a window of fewer
     than 5 frames (no output rows) and the zero column 40."""
